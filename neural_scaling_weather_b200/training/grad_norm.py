@@ -1,0 +1,66 @@
+"""Sharding-aware global gradient (or weight) norm without host synchronisation.
+
+The reference (``utils/trainer.py:416-448``) sums ``p.grad**2`` per parameter, all-reduces
+that scalar over every group the parameter is sharded on, adds the results and calls
+``.item()`` (a host sync), twice per step.  Here parameters are grouped by their set of
+sharding groups; one kernel computes the per-class sums of squares over the flat buffer,
+each class's scalar is all-reduced over its groups (device tensors, no sync) and the
+clip coefficient ``max_norm / (norm + 1e-6)`` (when ``norm > max_norm``) stays on device
+for the fused optimizer to read.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+from ..parallel import comm
+
+
+class ShardedNorm:
+    def __init__(self, space):
+        self.space = space
+        classes: Dict[Tuple[str, ...], int] = {}
+        seg_lo, seg_hi, seg_cls = [], [], []
+        for i, p in enumerate(space.params):
+            key = tuple(g for g in getattr(p, "comm_metadata", {}).get("sharded", []) if g is not None)
+            c = classes.setdefault(key, len(classes))
+            lo = space.offsets[i]
+            seg_lo.append(lo)
+            seg_hi.append(lo + p.numel())
+            seg_cls.append(c)
+        self.classes = sorted(classes, key=classes.get)
+        dev = space.data.device
+        self.seg_lo = torch.tensor(seg_lo, dtype=torch.int64, device=dev)
+        self.seg_hi = torch.tensor(seg_hi, dtype=torch.int64, device=dev)
+        self.seg_cls = torch.tensor(seg_cls, dtype=torch.int32, device=dev)
+        self._lo, self._hi, self._cls = seg_lo, seg_hi, seg_cls
+
+    def _class_sums(self, buf: torch.Tensor) -> torch.Tensor:
+        if buf.is_cuda:
+            return _ext.require().segment_sumsq(buf, self.seg_lo, self.seg_hi, self.seg_cls,
+                                                len(self.classes))
+        out = torch.zeros(len(self.classes), dtype=torch.float32)
+        for lo, hi, c in zip(self._lo, self._hi, self._cls):
+            out[c] += buf[lo:hi].float().square().sum()
+        return out
+
+    def norm(self, which: str = "grad") -> torch.Tensor:
+        """Global L2 norm (device scalar tensor, shape [1])."""
+        buf = self.space.grad if which == "grad" else self.space.data
+        sums = self._class_sums(buf)
+        total = torch.zeros(1, dtype=torch.float32, device=buf.device)
+        for c, groups in enumerate(self.classes):
+            s = sums[c:c + 1].clone()
+            for g in groups:
+                if comm.get_size(g) > 1:
+                    dist.all_reduce(s, group=comm.get_group(g))
+            total += s
+        return total.sqrt()
+
+    @staticmethod
+    def clip_coef(norm: torch.Tensor, max_norm: float) -> torch.Tensor:
+        return torch.where(norm > max_norm, max_norm / (norm + 1e-6), torch.ones_like(norm))
