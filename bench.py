@@ -1,0 +1,433 @@
+"""Headline benchmark: training samples/s of Swin p4-e1024-d16 on 720x1440x70 (bf16).
+
+``python bench.py --gpus N --steps K --warmup W`` (N > 1 under torchrun, one rank per GPU).
+One step is one optimizer step over the global batch (16 samples, micro-batch 1, so each
+of the N data-parallel ranks runs 16/N micro-batches).  W untimed steps, then K steps
+bracketed by a barrier and ``torch.cuda.synchronize()``, timed with CUDA events on the
+launching stream; the reported time is the maximum over ranks.  Inputs are synthetic
+fields of the named shape (300 MB per sample in fp32, larger than the 126 MB L2, so no
+extra flush is needed between steps).  Rank 0 prints one JSON line.
+
+``--impl reference`` runs the reference implementation's own model, DDP hook, loss,
+optimizer and gradient clipping (see ``baseline/reference_harness.py``) on the same data.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "train samples/s @1/2/4/8 B200 (device-timed, max over ranks); ms/rollout step"
+MODEL = dict(embed_dim=1024, depth=16, num_heads=16, patch_size=4, window_size=[9, 18], mlp_ratio=4)
+NLAT, NLON = 720, 1440
+N_CH = 70
+N_INV = 3
+GLOBAL_BATCH = 16
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
+    ap.add_argument("--depth", type=int, default=MODEL["depth"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-rollout", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- infra
+def init_dist(n):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    return rank, world, local
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = os.path.join("/tmp", f"nsw_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                pass
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() in ("active", "1", "yes"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- data
+def make_batches(n, device, pinned=False):
+    """n synthetic micro-batches (1, 2, 73, 720, 1440) fp32: inputs + target time step."""
+    from neural_scaling_weather_b200.data.synthetic import SyntheticERA5
+
+    ds = SyntheticERA5(mode="train", nlat=NLAT, nlon=NLON, sfc_vars=["u10m", "v10m", "t2m", "tcwv", "msl"],
+                       pl_vars=["u", "v", "z", "t", "q"],
+                       levels=[50, 100, 150, 200, 250, 300, 400, 500, 600, 700, 850, 925, 1000],
+                       n_times=200, dt_scale=6, model_patch_size=4, invariants=["lsm", "orog", "coslat"])
+    out = []
+    for i in range(n):
+        x = ds.generate(ds.window_hours(7 * i), device=device)  # (2, 70, 720, 1440)
+        out.append(x.unsqueeze(0))
+    inv = torch.from_numpy(ds.invar).to(device)
+    if pinned:
+        out = [b.cpu().pin_memory() for b in out]
+    return ds, out, inv
+
+
+# ----------------------------------------------------------------------------- native arm
+def native(args, rank, world, local):
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.ops import _ext
+    from neural_scaling_weather_b200.training.trainer import Trainer
+
+    overrides = [
+        f"hydra.run.dir=/tmp/nsw_bench_{os.getpid()}", "parallelism.backend=nccl", "optimizer=adamw",
+        "optimizer.lr=5e-4", "optimizer.scheduler=null", "train.clip_grad_norm=1.0", "train.amp_dtype=bf16",
+        "train.enable_amp=true", "loss=mse", "loss.area_weights=true", "logging.log_to_wandb=false",
+        "logging.log_to_screen=false", "train.save_checkpoint=false",
+        f"model.embed_dim={MODEL['embed_dim']}", f"model.depth={args.depth}",
+        f"model.num_heads={MODEL['num_heads']}", f"model.patch_size={MODEL['patch_size']}",
+        "model.window_size=[9,18]", f"data.batch_size={args.global_batch}",
+        "data.synthetic.n_samples=200", "train.seed=0",
+    ]
+    cfg = C.compose("default", overrides)
+    tr = Trainer(cfg)
+    tr.build()
+    accum = tr.gradient_accum_steps
+    _, batches, _ = make_batches(2, "cuda")
+    dev_batches = batches
+
+    def step(src, pinned):
+        last = None
+        for i in range(accum):
+            b = src[i % len(src)]
+            if pinned:
+                b = b.to("cuda", non_blocking=True)
+            last = tr.train_step(b, is_optimizer_step=(i == accum - 1))
+        return last
+
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step(dev_batches, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # launch count (one extra step under the profiler, outside the timed region)
+    launches = count_launches(lambda: step(dev_batches, False))
+
+    sampler = ClockSampler(gpus=list(range(world)) if world > 1 else [torch.cuda.current_device()])
+    if rank == 0:
+        sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(dev_batches, False)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop() if rank == 0 else None
+    ms = max_over_ranks(ms, world)
+
+    e2e = None
+    if not args.no_e2e:
+        _, host_batches, _ = make_batches(2, "cuda", pinned=True)
+        for _ in range(1):
+            step(host_batches, True)
+            tr.train_loss.item()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            step(host_batches, True)
+            float(tr.train_loss.item())  # device -> host read of the step's result
+        f1.record()
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+        bi = host_batches[0].numel() * host_batches[0].element_size() * accum * world
+        e2e = {"value": args.global_batch / (e_ms / 1000.0), "unit": "samples/s",
+               "h2d_bytes_per_step": int(bi), "d2h_bytes_per_step": 4 * world,
+               "ms_per_step": e_ms,
+               "path": "Trainer.train_step on pinned-host batches + loss.item() each step"}
+
+    rollout_ms = None
+    if not args.no_rollout and rank == 0:
+        rollout_ms = rollout_latency(tr, dev_batches[0])
+    err = _ext.require().read_error_flag(True)
+    return ms, clocks, e2e, launches, rollout_ms, err
+
+
+def rollout_latency(tr, batch, n=5):
+    """ms per autoregressive model step (forward only, bf16), one initial condition."""
+    model = tr.model
+    model.eval()
+    inp, _ = tr.preprocessor(batch, device=torch.device("cuda"))
+    ts = []
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        for _ in range(2):
+            model(inp)
+        for _ in range(n):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            model(inp)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+    model.train()
+    return statistics.median(ts)
+
+
+def count_launches(fn):
+    """Kernels of this repository's extension launched by ``fn`` (profiled once)."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        mine, total = 0, 0
+        for ev in prof.events():
+            if ev.device_type is not None and "CUDA" in str(ev.device_type):
+                total += 1
+                if "nsw::" in ev.name:
+                    mine += 1
+        return mine, total
+    except Exception as e:  # pragma: no cover
+        return None, str(e)
+
+
+# ----------------------------------------------------------------------------- reference arm
+def reference(args, rank, world, local):
+    sys.path.insert(0, os.path.join(HERE, "baseline"))
+    import reference_harness as RH
+
+    if not RH.available():
+        return None
+    ns = RH.import_reference()
+    cfgd = dict(
+        model=dict(arch="swin", embed_dim=MODEL["embed_dim"], patch_size=4, depth=args.depth, window_size=[9, 18],
+                   num_heads=MODEL["num_heads"], dropout=0.0, mlp_ratio=4, coord_pos_embed=True),
+        data=dict(invariants=["lsm", "orog", "coslat"], batch_size=args.global_batch),
+        train=dict(temporal_context_window=1, num_rollout_steps=1, clip_grad_norm=1.0),
+        parallelism=dict(use_transformer_engine=True, tp=1, sp1=1, sp2=1, pp=1, order="sp1-sp2-tp-pp-dp",
+                         backend="nccl", micro_batch_size=1),
+        optimizer=dict(optimizer="adamw", scheduler=None, lr=5e-4, weight_decay=1e-4, max_iterations=100000),
+        loss=dict(loss_func="mse", sfc_weights=False, pressure_weights=False, area_weights=True),
+    )
+    cfg = RH.make_cfg(cfgd)
+    comm = ns.comm
+    if world > 1:
+        comm.init_model_parallel_info(tp=1, sp1=1, sp2=1, dp=world, pp=1, order="sp1-sp2-tp-pp-dp")
+    else:
+        # the reference always runs inside a process group
+        import datetime
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29600 + os.getpid() % 1000))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        comm.init_model_parallel_info(tp=1, sp1=1, sp2=1, dp=1, pp=1, order="sp1-sp2-tp-pp-dp")
+    lat = np.linspace(90, -90, NLAT + 1)[:-1]
+    lon = np.arange(NLON) * 360.0 / NLON
+    md = {
+        "sp_shapes": [[NLAT], [NLON]], "sp_slices": [slice(0, NLAT), slice(0, NLON)],
+        "spatial_dims": [NLAT, NLON], "n_channels": N_CH, "channels": [f"c{i}" for i in range(N_CH)],
+        "coords": ns.misc_utils.get_spatial_coords((lat, lon)).float(),
+        "area_weights": ns.misc_utils.build_spherical_area_weights(lat)[:, None].float(),
+        "global_latitudes": lat, "global_longitudes": lon,
+    }
+    device = torch.device("cuda", local)
+    torch.manual_seed(0)
+    model = ns.model_helpers.get_model(cfg, md).to(device)
+    model = ns.mappings.init_ddp_model_and_reduction_hooks(model, device_ids=[local], output_device=[local],
+                                                           backend="nccl")
+    opt = ns.optimizer_utils.set_optimizer(cfg, model)
+    loss_fn = ns.losses.WeightedLoss(area_weighting=True, weights=md["area_weights"]).to(device)
+    accum = args.global_batch // world
+    tr_cls = ns.trainer.Trainer if ns.trainer is not None else None
+
+    class _T:  # the trainer's clip/norm methods only read self.device
+        pass
+
+    fake = _T()
+    fake.device = device
+    _, batches, inv = make_batches(2, "cuda")
+    from contextlib import nullcontext
+
+    def step():
+        for i in range(accum):
+            b = batches[i % len(batches)]
+            b = torch.cat([b, inv.expand(1, 2, -1, -1, -1)], dim=2)
+            inputs, targets = b[:, :1], b[:, 1:, :N_CH]
+            ctx = model.no_sync() if (world > 1 and i < accum - 1) else nullcontext()
+            with ctx:
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    gen = model(inputs)
+                    loss = loss_fn(gen, targets)
+                (loss / accum).backward()
+        if tr_cls is not None:
+            tr_cls.clip_grad_norm(fake, model, max_norm=1.0)
+        opt.step()
+        model.zero_grad(set_to_none=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(gpus=list(range(world)))
+    if rank == 0:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    clocks = sampler.stop() if rank == 0 else None
+    return ms, clocks
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    args = parse()
+    if args.impl == "reference":
+        rank, world, local = init_dist(args.gpus)
+        try:
+            res = reference(args, rank, world, local)
+        except Exception as e:  # noqa: BLE001
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}))
+            return
+        if res is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "reference source not present in baseline/_ref"}))
+            return
+        ms, clocks = res
+        if rank == 0:
+            print(json.dumps({
+                "impl": "reference", "metric": METRIC, "value": args.global_batch / (ms / 1000.0),
+                "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic", "clocks": clocks,
+                "config": {"model": "swin-p4-e1024-d16", "global_batch": args.global_batch, "seq_len": 64800,
+                           "parallelism": f"dp{world}", "path": "reference vanilla (no TE), torch.compile'd helpers, DDP"},
+            }))
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        return
+
+    rank, world, local = init_dist(args.gpus)
+    ms, clocks, e2e, launches, rollout_ms, err = native(args, rank, world, local)
+    if rank == 0:
+        per_step_launch = launches[0] if isinstance(launches, tuple) else None
+        line = {
+            "metric": METRIC, "value": args.global_batch / (ms / 1000.0), "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded advected sinusoids + noise, 70 ch x 720 x 1440), random-init weights",
+            "config": {"model": "swin-p4-e1024-d16", "global_batch": args.global_batch, "seq_len": 64800,
+                       "parallelism": f"dp{world}", "micro_batch": 1, "optimizer": "adamw lr 5e-4 clip 1.0",
+                       "l2": "inputs (300 MB fp32 per sample) larger than L2; no extra flush",
+                       "depth": args.depth},
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": (per_step_launch * args.steps) if per_step_launch is not None else None,
+            "gpu_launches_note": f"own kernels per step {launches}",
+            "rollout_ms_per_step": rollout_ms,
+            "device_error_flag": err,
+        }
+        print(json.dumps(line))
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

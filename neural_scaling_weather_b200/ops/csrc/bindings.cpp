@@ -1,0 +1,375 @@
+// PyTorch bindings of the sm_100a kernels: argument checks, output allocation and the
+// current CUDA stream; the kernels themselves live in the .cu files (no torch headers).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels.h"
+
+namespace {
+
+using torch::Tensor;
+
+int dt_code(const Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kBFloat16: return nsw::kBF16;
+    case at::kHalf: return nsw::kF16;
+    case at::kFloat: return nsw::kF32;
+    default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+  }
+  return -1;
+}
+
+at::ScalarType scalar_of(int code) {
+  return code == nsw::kBF16 ? at::kBFloat16 : (code == nsw::kF16 ? at::kHalf : at::kFloat);
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+void need_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+const float* opt_f32(const c10::optional<Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->is_cuda(), "expected fp32 CUDA tensor");
+  return t->data_ptr<float>();
+}
+
+// ------------------------------------------------------------------------------ misc
+int read_error_flag(bool clear) {
+  int* f = nsw::device_error_flag();
+  int v = 0;
+  check(cudaMemcpy(&v, f, sizeof(int), cudaMemcpyDeviceToHost), "read_error_flag");
+  if (clear && v) check(cudaMemset(f, 0, sizeof(int)), "clear_error_flag");
+  return v;
+}
+
+// ------------------------------------------------------------------------------ norms
+std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
+  need_cuda(x, "x");
+  need_cuda(w, "w");
+  const int n = (int)x.size(-1);
+  const int64_t rows = x.numel() / n;
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({rows}, x.options().dtype(at::kFloat));
+  check(nsw::rmsnorm_fwd(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), rows,
+                         n, (float)eps, dt_code(x), stream()),
+        "rmsnorm_fwd");
+  return {y, rstd};
+}
+
+std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
+  need_cuda(dy, "dy");
+  need_cuda(x, "x");
+  const int n = (int)x.size(-1);
+  const int64_t rows = x.numel() / n;
+  auto dx = torch::empty_like(x);
+  int parts = 2 * 148;
+  if (rows < parts * 8) parts = (int)std::max<int64_t>(1, (rows + 7) / 8);
+  auto part = torch::empty({parts, n}, x.options().dtype(at::kFloat));
+  check(nsw::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(),
+                         dx.data_ptr(), part.data_ptr<float>(), parts, rows, n, dt_code(x), stream()),
+        "rmsnorm_bwd");
+  return {dx, part.sum(0)};
+}
+
+// ------------------------------------------------------------------------------ GEMM
+Tensor gemm(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor> residual,
+            int64_t res_period, int64_t act, c10::optional<Tensor> preact, bool out_f32, double alpha,
+            c10::optional<Tensor> out, bool accumulate) {
+  need_cuda(A, "A");
+  need_cuda(B, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm: A [M,K], B [N,K]");
+  TORCH_CHECK(A.scalar_type() == B.scalar_type(), "gemm: A and B must share a dtype");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  Tensor D;
+  if (out.has_value() && out->defined()) {
+    D = *out;
+    need_cuda(D, "out");
+  } else {
+    D = torch::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : A.scalar_type()));
+  }
+  nsw::GemmArgs g{};
+  g.A = A.data_ptr();
+  g.B = B.data_ptr();
+  g.D = D.data_ptr();
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.lda = K;
+  g.ldb = K;
+  g.ldd = N;
+  g.bias = opt_f32(bias);
+  if (residual.has_value() && residual->defined()) {
+    need_cuda(*residual, "residual");
+    TORCH_CHECK(residual->scalar_type() == A.scalar_type(), "residual dtype");
+    g.residual = residual->data_ptr();
+    g.ldr = N;
+    g.res_period = res_period > 0 ? res_period : M;
+  }
+  if (preact.has_value() && preact->defined()) {
+    need_cuda(*preact, "preact");
+    g.preact = preact->data_ptr();
+  }
+  g.act = (int)act;
+  g.dtype = dt_code(A);
+  g.out_f32 = out_f32 ? 1 : 0;
+  g.alpha = (float)alpha;
+  g.accumulate = accumulate ? 1 : 0;
+  TORCH_CHECK(nsw::gemm_tcgen05_supported(g), "gemm: shape/alignment not supported by the tcgen05 kernel");
+  check(nsw::gemm_tcgen05(g, stream()), "gemm_tcgen05");
+  return D;
+}
+
+bool gemm_supported(Tensor A, Tensor B, bool out_f32) {
+  nsw::GemmArgs g{};
+  g.A = A.data_ptr();
+  g.B = B.data_ptr();
+  g.D = A.data_ptr();
+  g.M = A.size(0);
+  g.N = B.size(0);
+  g.K = A.size(1);
+  g.lda = A.stride(0);
+  g.ldb = B.stride(0);
+  g.ldd = B.size(0);
+  g.dtype = dt_code(A);
+  g.out_f32 = out_f32;
+  return A.is_contiguous() && B.is_contiguous() && nsw::gemm_tcgen05_supported(g);
+}
+
+std::vector<Tensor> bias_act_residual(Tensor acc, c10::optional<Tensor> bias, c10::optional<Tensor> residual,
+                                      int64_t res_period, int64_t act, bool want_preact, int64_t out_dtype) {
+  need_cuda(acc, "acc");
+  const int n = (int)acc.size(-1);
+  const int64_t rows = acc.numel() / n;
+  auto y = torch::empty(acc.sizes(), acc.options().dtype(scalar_of((int)out_dtype)));
+  Tensor pre;
+  if (want_preact) pre = torch::empty_like(y);
+  const void* res = nullptr;
+  if (residual.has_value() && residual->defined()) {
+    need_cuda(*residual, "residual");
+    res = residual->data_ptr();
+  }
+  check(nsw::bias_act_residual(acc.data_ptr(), dt_code(acc), opt_f32(bias), res, res_period,
+                               y.data_ptr(), want_preact ? pre.data_ptr() : nullptr, rows, n, (int)act,
+                               (int)out_dtype, stream()),
+        "bias_act_residual");
+  return {y, pre};
+}
+
+Tensor gelu_bwd(Tensor dy, Tensor u) {
+  need_cuda(dy, "dy");
+  need_cuda(u, "u");
+  auto du = torch::empty_like(u);
+  check(nsw::gelu_bwd(dy.data_ptr(), u.data_ptr(), du.data_ptr(), u.numel(), dt_code(u), stream()),
+        "gelu_bwd");
+  return du;
+}
+
+Tensor col_sum(Tensor x) {
+  need_cuda(x, "x");
+  const int n = (int)x.size(-1);
+  const int64_t rows = x.numel() / n;
+  int parts = 4 * 148;
+  if (rows < parts) parts = (int)std::max<int64_t>(1, rows);
+  auto part = torch::empty({parts, n}, x.options().dtype(at::kFloat));
+  auto out = torch::empty({n}, x.options().dtype(at::kFloat));
+  check(nsw::col_sum(x.data_ptr(), out.data_ptr<float>(), part.data_ptr<float>(), parts, rows, n,
+                     dt_code(x), stream()),
+        "col_sum");
+  return out;
+}
+
+// ------------------------------------------------------------------------------ patches
+Tensor im2col(Tensor x, int64_t p, int64_t out_dtype) {
+  need_cuda(x, "x");
+  const int N = (int)x.size(0), C = (int)x.size(1), H = (int)x.size(2), W = (int)x.size(3);
+  auto cols = torch::empty({(int64_t)N * (H / p) * (W / p), (int64_t)C * p * p},
+                           x.options().dtype(scalar_of((int)out_dtype)));
+  check(nsw::im2col_patch(x.data_ptr(), dt_code(x), cols.data_ptr(), N, C, H, W, (int)p, (int)out_dtype,
+                          stream()),
+        "im2col");
+  return cols;
+}
+
+Tensor col2im(Tensor dcols, int64_t N, int64_t C, int64_t H, int64_t W, int64_t p, int64_t x_dtype) {
+  need_cuda(dcols, "dcols");
+  auto dx = torch::empty({N, C, H, W}, dcols.options().dtype(scalar_of((int)x_dtype)));
+  check(nsw::col2im_patch(dcols.data_ptr(), dx.data_ptr(), (int)x_dtype, (int)N, (int)C, (int)H, (int)W,
+                          (int)p, dt_code(dcols), stream()),
+        "col2im");
+  return dx;
+}
+
+Tensor unpatchify(Tensor y2, int64_t B, int64_t T, int64_t h, int64_t w, int64_t p, int64_t C) {
+  need_cuda(y2, "y2");
+  auto out = torch::empty({B, T, C, h * p, w * p}, y2.options());
+  check(nsw::unpatchify(y2.data_ptr(), out.data_ptr(), (int)(B * T), (int)h, (int)w, (int)p, (int)C,
+                        dt_code(y2), stream()),
+        "unpatchify");
+  return out;
+}
+
+Tensor patchify(Tensor dout, int64_t h, int64_t w, int64_t p, int64_t C) {
+  need_cuda(dout, "dout");
+  const int64_t BT = dout.numel() / (C * h * p * w * p);
+  auto dy2 = torch::empty({BT * h * w, p * p * C}, dout.options());
+  check(nsw::patchify(dout.data_ptr(), dy2.data_ptr(), (int)BT, (int)h, (int)w, (int)p, (int)C,
+                      dt_code(dout), stream()),
+        "patchify");
+  return dy2;
+}
+
+// ------------------------------------------------------------------------------ losses
+Tensor weighted_sse(Tensor x, Tensor y, c10::optional<Tensor> aw, c10::optional<Tensor> cw) {
+  need_cuda(x, "x");
+  need_cuda(y, "y");
+  TORCH_CHECK(x.sizes() == y.sizes(), "weighted_sse: shape mismatch");
+  const int W = (int)x.size(-1), H = (int)x.size(-2), C = (int)x.size(-3);
+  const int64_t lead = x.numel() / ((int64_t)C * H * W);
+  const int parts = 4 * 148;
+  auto part = torch::empty({parts}, x.options().dtype(at::kFloat));
+  auto out = torch::empty({}, x.options().dtype(at::kFloat));
+  check(nsw::weighted_sse(x.data_ptr(), dt_code(x), y.data_ptr(), dt_code(y), opt_f32(aw), opt_f32(cw),
+                          part.data_ptr<float>(), parts, out.data_ptr<float>(), lead, C, H, W, stream()),
+        "weighted_sse");
+  return out;
+}
+
+Tensor weighted_sse_bwd(Tensor x, Tensor y, c10::optional<Tensor> aw, c10::optional<Tensor> cw, Tensor gscale) {
+  need_cuda(x, "x");
+  need_cuda(y, "y");
+  const int W = (int)x.size(-1), H = (int)x.size(-2), C = (int)x.size(-3);
+  const int64_t lead = x.numel() / ((int64_t)C * H * W);
+  auto dx = torch::empty_like(x);
+  check(nsw::weighted_sse_bwd(x.data_ptr(), dt_code(x), y.data_ptr(), dt_code(y), opt_f32(aw), opt_f32(cw),
+                              gscale.data_ptr<float>(), dx.data_ptr(), lead, C, H, W, stream()),
+        "weighted_sse_bwd");
+  return dx;
+}
+
+Tensor weighted_se_per_plane(Tensor x, Tensor y, Tensor aw) {
+  need_cuda(x, "x");
+  need_cuda(y, "y");
+  const int W = (int)x.size(-1), H = (int)x.size(-2);
+  const int64_t planes = x.numel() / ((int64_t)H * W);
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end() - 2);
+  auto out = torch::empty(shape, x.options().dtype(at::kFloat));
+  check(nsw::weighted_se_per_plane(x.data_ptr(), dt_code(x), y.data_ptr(), dt_code(y),
+                                   aw.data_ptr<float>(), out.data_ptr<float>(), planes, H, W, stream()),
+        "weighted_se_per_plane");
+  return out;
+}
+
+// ------------------------------------------------------------------------------ optimizer
+void adamw_step(Tensor p, Tensor g, Tensor m, Tensor v, Tensor shadow, Tensor gscale, Tensor skip, double lr,
+                double b1, double b2, double eps, double wd, double bc1, double bc2, bool decoupled) {
+  need_cuda(p, "p");
+  TORCH_CHECK(p.scalar_type() == at::kFloat && g.scalar_type() == at::kFloat, "adamw: fp32 buffers");
+  void* sh = shadow.numel() ? shadow.data_ptr() : nullptr;
+  const int shd = shadow.numel() ? dt_code(shadow) : nsw::kF32;
+  check(nsw::adamw_step(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), sh,
+                        shd, gscale.data_ptr<float>(), skip.data_ptr<int>(), p.numel(), (float)lr, (float)b1,
+                        (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2, decoupled, stream()),
+        "adamw_step");
+}
+
+Tensor segment_sumsq(Tensor x, Tensor block_lo, Tensor block_hi, Tensor block_cls, int64_t ncls) {
+  need_cuda(x, "x");
+  const int nb = (int)block_lo.numel();
+  auto part = torch::empty({nb}, x.options().dtype(at::kFloat));
+  auto out = torch::empty({ncls}, x.options().dtype(at::kFloat));
+  check(nsw::segment_sumsq(x.data_ptr<float>(), block_lo.data_ptr<int64_t>(), block_hi.data_ptr<int64_t>(),
+                           block_cls.data_ptr<int>(), nb, (int)ncls, part.data_ptr<float>(), out.data_ptr<float>(),
+                           stream()),
+        "segment_sumsq");
+  return out;
+}
+
+// ------------------------------------------------------------------------------ attention
+nsw::AttnGeom make_geom(const std::vector<int64_t>& gi, double scale) {
+  TORCH_CHECK(gi.size() == 14, "geometry: 14 ints expected");
+  nsw::AttnGeom g{};
+  g.B = (int)gi[0];
+  g.T = (int)gi[1];
+  g.H = (int)gi[2];
+  g.W = (int)gi[3];
+  g.nh = (int)gi[4];
+  g.hd = (int)gi[5];
+  g.wh = (int)gi[6];
+  g.ww = (int)gi[7];
+  g.sh = (int)gi[8];
+  g.sw = (int)gi[9];
+  g.mask = (int)gi[10];
+  g.mask_shift = (int)gi[11];
+  g.row_offset = (int)gi[12];
+  g.h_global = (int)gi[13];
+  g.scale = (float)scale;
+  g.qkv_stride = 3LL * g.nh * g.hd;
+  g.out_stride = (int64_t)g.nh * g.hd;
+  return g;
+}
+
+std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vector<int64_t> gi, double scale) {
+  need_cuda(qkv, "qkv");
+  auto g = make_geom(gi, scale);
+  const int64_t tokens = (int64_t)g.B * g.T * g.H * g.W;
+  TORCH_CHECK(qkv.numel() == tokens * g.qkv_stride, "qkv size");
+  auto out = torch::empty({tokens, (int64_t)g.nh * g.hd}, qkv.options());
+  const int L = g.T * g.wh * g.ww;
+  const int64_t nwin = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww);
+  auto lse = torch::empty({nwin * g.nh * L}, qkv.options().dtype(at::kFloat));
+  check(nsw::window_attn_fwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                             lse.data_ptr<float>(), g, dt_code(qkv), stream()),
+        "window_attn_fwd");
+  return {out, lse};
+}
+
+std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out, Tensor dout, Tensor lse,
+                                    std::vector<int64_t> gi, double scale) {
+  need_cuda(qkv, "qkv");
+  need_cuda(dout, "dout");
+  auto g = make_geom(gi, scale);
+  auto dqkv = torch::empty_like(qkv);
+  const int64_t nwin = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww);
+  auto qp = torch::empty({nwin * g.nh, (int64_t)g.hd}, qkv.options().dtype(at::kFloat));
+  auto kp = torch::empty_like(qp);
+  check(nsw::window_attn_bwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                             dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp.data_ptr<float>(),
+                             kp.data_ptr<float>(), g, dt_code(qkv), stream()),
+        "window_attn_bwd");
+  return {dqkv, qp.sum(0), kp.sum(0)};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of neural_scaling_weather_b200";
+  m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
+        py::arg("res_period") = 0, py::arg("act") = 0, py::arg("preact") = py::none(), py::arg("out_f32") = false,
+        py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false);
+  m.def("gemm_supported", &gemm_supported);
+  m.def("bias_act_residual", &bias_act_residual);
+  m.def("gelu_bwd", &gelu_bwd);
+  m.def("col_sum", &col_sum);
+  m.def("im2col", &im2col);
+  m.def("col2im", &col2im);
+  m.def("unpatchify", &unpatchify);
+  m.def("patchify", &patchify);
+  m.def("weighted_sse", &weighted_sse);
+  m.def("weighted_sse_bwd", &weighted_sse_bwd);
+  m.def("weighted_se_per_plane", &weighted_se_per_plane);
+  m.def("adamw_step", &adamw_step);
+  m.def("segment_sumsq", &segment_sumsq);
+  m.def("window_attn_fwd", &window_attn_fwd);
+  m.def("window_attn_bwd", &window_attn_bwd);
+}

@@ -1,0 +1,88 @@
+// Shared device helpers for the sm_100a kernels of neural_scaling_weather_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nsw {
+
+// Device-side error word: kernels that give up a bounded wait or see an out-of-range
+// index record a code here instead of trapping; the host reads and clears it.
+enum ErrorCode : int {
+  kErrNone = 0,
+  kErrWaitTimeout = 1,
+  kErrBounds = 2,
+  kErrBadArg = 3,
+};
+
+__device__ __forceinline__ void record_error(int* flag, int code) {
+  if (flag) atomicCAS(flag, 0, code);
+}
+
+template <typename T>
+struct Vec8;  // 8 x 16-bit values in one 16-byte register group
+
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f(float v) { return v; }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+
+// unpack/pack 8 16-bit floats from/to a uint4
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f(h[i]);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = from_f<T>(f[i]);
+  return u;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Exact (erf-based) GELU, as torch.nn.GELU() with approximate='none'.
+__device__ __forceinline__ float gelu_f(float u) {
+  return 0.5f * u * (1.0f + erff(u * 0.70710678118654752440f));
+}
+__device__ __forceinline__ float gelu_grad_f(float u) {
+  const float cdf = 0.5f * (1.0f + erff(u * 0.70710678118654752440f));
+  const float pdf = expf(-0.5f * u * u) * 0.39894228040143267794f;
+  return cdf + u * pdf;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+}  // namespace nsw
+
+#define NSW_CUDA_CHECK(expr)                                                          \
+  do {                                                                                \
+    cudaError_t _e = (expr);                                                          \
+    if (_e != cudaSuccess) return _e;                                                 \
+  } while (0)

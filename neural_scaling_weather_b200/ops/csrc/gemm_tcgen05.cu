@@ -1,0 +1,458 @@
+// Persistent, warp-specialised tcgen05 GEMM with fused epilogues for sm_100a.
+//
+//   D[m, n] = epilogue( alpha * sum_k A[m, k] * B[n, k] )
+//   epilogue: (+ bias[n]) -> (store pre-activation) -> (GELU) -> (+ residual[m % P, n])
+//             -> bf16/fp16 store, or fp32 store / fp32 accumulate (D += ...)
+//
+// A [M, K] and B [N, K] are K-major (row-major with K contiguous), bf16 or fp16.
+// Tiles are 128 x BN x 64.  Roles inside a CTA of 6 warps:
+//   warp 0: TMA producer (one elected lane) filling a STAGES-deep ring of A/B tiles
+//           (128-byte swizzle) tracked by full/empty mbarriers;
+//   warp 1: allocates 2*BN TMEM columns and issues tcgen05.mma (one elected lane),
+//           committing each stage back to its empty barrier and each finished tile to
+//           a tmem_full barrier; two accumulators let the epilogue of tile i overlap
+//           the MMAs of tile i+1;
+//   warps 2-5: epilogue, one TMEM lane quadrant (32 rows) each, tcgen05.ld 32 columns
+//           at a time, fused bias/GELU/residual, 16-byte global stores.
+// The CTA grid is the SM count; tiles are walked with N fastest so concurrently
+// running CTAs share the A tile through L2.  Every mbarrier wait is bounded by a
+// %globaltimer budget: on expiry the kernel records kErrWaitTimeout in the device error
+// word, stops issuing work, and still frees its TMEM before returning.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nsw {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // bf16: 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+constexpr unsigned long long kWaitBudgetNs = 4000000000ull;  // 4 s
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; returns false (and raises the abort flag) on timeout or abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitBudgetNs) {
+        *abort_flag = 1;
+        record_error(err, kErrWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+  // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO), LBO unused (1),
+  // descriptor version 1, layout type 2 (SWIZZLE_128B).
+  const uint32_t a = smem_u32(p);
+  uint64_t d = 0;
+  d |= (uint64_t)((a >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+struct EpiParams {
+  void* D;
+  int64_t M, N, ldd;
+  const float* bias;
+  const void* residual;
+  int64_t ldr, res_period;
+  void* preact;
+  int act;
+  int out_f32;
+  int accumulate;
+  float alpha;
+};
+
+template <typename T, int BN, int STAGES>
+struct Smem {
+  alignas(1024) T a[STAGES][BM * BK];
+  alignas(1024) T b[STAGES][BN * BK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                int64_t M, int64_t N, int64_t K, EpiParams ep, uint32_t idesc, int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // align the working area to 1024 B (the swizzle atom)
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto& S = *reinterpret_cast<Smem<T, BN, STAGES>*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m_tiles = (M + BM - 1) / BM;
+  const int64_t n_tiles = (N + BN - 1) / BN;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (int)((K + BK - 1) / BK);
+  volatile int* abort_flag = &S.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&S.tmem_full[a], 1);
+      mbar_init(&S.tmem_empty[a], 4);
+    }
+    S.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&S.tmem_base)),
+                 "r"(2 * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (int)((tile / n_tiles) * BM);
+        const int n0 = (int)((tile % n_tiles) * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&S.empty[stage], phase ^ 1, abort_flag, err)) break;
+          mbar_expect_tx(&S.full[stage], (uint32_t)((BM + BN) * BK * sizeof(T)));
+          tma_load_2d(S.a[stage], &map_a, &S.full[stage], kb * BK, m0);
+          tma_load_2d(S.b[stage], &map_b, &S.full[stage], kb * BK, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(&S.tmem_empty[acc], acc_phase ^ 1, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&S.full[stage], phase, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t da = smem_desc_sw128(&S.a[stage][k * 16]);
+            const uint64_t db = smem_desc_sw128(&S.b[stage][k * 16]);
+            umma_f16(d_tmem, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&S.tmem_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
+      tc_fence_after();
+      const int64_t m0 = (tile / n_tiles) * BM;
+      const int64_t n0 = (tile % n_tiles) * BN;
+      const int64_t row = m0 + q * 32 + lane;
+      const bool row_ok = row < ep.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + (uint32_t)(c * 32), r);
+        const int64_t nb = n0 + c * 32;
+        if (!row_ok || nb >= ep.N) continue;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) * ep.alpha;
+        const bool full = nb + 32 <= ep.N;
+        if (ep.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (full || nb + j < ep.N) f[j] += ep.bias[nb + j];
+        }
+        if (ep.preact) {
+          T* pp = reinterpret_cast<T*>(ep.preact) + row * ep.ldd + nb;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(pp)[v] = pack8<T>(&f[8 * v]);
+          } else {
+            for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(f[j]);
+          }
+        }
+        if (ep.act == 1) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = gelu_f(f[j]);
+        }
+        if (ep.residual) {
+          const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float rr[8];
+              unpack8<T>(reinterpret_cast<const uint4*>(rp)[v], rr);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[8 * v + j] += rr[j];
+            }
+          } else {
+            for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
+          }
+        }
+        if (ep.out_f32) {
+          float* dp = reinterpret_cast<float*>(ep.D) + row * ep.ldd + nb;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float4 o = make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
+              if (ep.accumulate) {
+                const float4 old = reinterpret_cast<float4*>(dp)[v];
+                o.x += old.x;
+                o.y += old.y;
+                o.z += old.z;
+                o.w += old.w;
+              }
+              reinterpret_cast<float4*>(dp)[v] = o;
+            }
+          } else {
+            for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = ep.accumulate ? dp[j] + f[j] : f[j];
+          }
+        } else {
+          T* dp = reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dp)[v] = pack8<T>(&f[8 * v]);
+          } else {
+            for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = from_f<T>(f[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
+  }
+}
+
+// ---------------------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D K-major operand [rows, K] with leading dimension ld (elements), box [BK, box_rows].
+static bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, int64_t ld,
+                     int box_rows, int dtype) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <typename T, int BN, int STAGES>
+static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
+  if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN, a.dtype)) return cudaErrorInvalidValue;
+  EpiParams ep;
+  ep.D = a.D;
+  ep.M = a.M;
+  ep.N = a.N;
+  ep.ldd = a.ldd;
+  ep.bias = a.bias;
+  ep.residual = a.residual;
+  ep.ldr = a.ldr;
+  ep.res_period = a.res_period > 0 ? a.res_period : a.M;
+  ep.preact = a.preact;
+  ep.act = a.act;
+  ep.out_f32 = a.out_f32;
+  ep.accumulate = a.accumulate;
+  ep.alpha = a.alpha;
+  const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
+  const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
+                         ((uint32_t)(BM >> 4) << 24);
+  const size_t smem = sizeof(Smem<T, BN, STAGES>) + 1024;
+  auto k = gemm_kernel<T, BN, STAGES>;
+  NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+  int grid = sm_count();
+  if (tiles < grid) grid = (int)tiles;
+  k<<<grid, kThreads, smem, s>>>(ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag());
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+int gemm_tcgen05_supported(const GemmArgs& a) {
+  if (a.dtype != kBF16 && a.dtype != kF16) return 0;
+  if (a.K % 8 || a.lda % 8 || a.ldb % 8) return 0;                    // 16-byte TMA strides
+  if ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) return 0;
+  if (a.ldd % 8 || (reinterpret_cast<uintptr_t>(a.D) & 15)) return 0;  // vector stores
+  if (a.residual && (a.ldr % 8 || (reinterpret_cast<uintptr_t>(a.residual) & 15))) return 0;
+  if (a.preact && (reinterpret_cast<uintptr_t>(a.preact) & 15)) return 0;
+  if (a.accumulate && !a.out_f32) return 0;
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  return tc::get_encode() != nullptr;
+}
+
+cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s) {
+  if (!gemm_tcgen05_supported(a)) return cudaErrorInvalidValue;
+  const bool wide = a.N > 128;
+  if (a.dtype == kBF16) {
+    return wide ? tc::launch<__nv_bfloat16, 256, 4>(a, s) : tc::launch<__nv_bfloat16, 128, 6>(a, s);
+  }
+  return wide ? tc::launch<__half, 256, 4>(a, s) : tc::launch<__half, 128, 6>(a, s);
+}
+
+}  // namespace nsw

@@ -1,0 +1,96 @@
+// Host-side launch interface of the sm_100a kernels (no torch types; raw pointers).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nsw {
+
+enum DType : int { kBF16 = 0, kF16 = 1, kF32 = 2 };
+
+int* device_error_flag();  // per-device error word (lazily allocated)
+
+// ---- norms -------------------------------------------------------------------
+cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n,
+                        float eps, int dtype, cudaStream_t s);
+cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                        float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
+                        cudaStream_t s);
+
+// ---- elementwise epilogues -----------------------------------------------------
+// y = act(acc + bias) + residual (residual row index = row % res_period)
+cudaError_t bias_act_residual(const void* acc, int acc_dtype, const float* bias, const void* residual,
+                              int64_t res_period, void* y, void* preact, int64_t rows, int n,
+                              int act, int dtype, cudaStream_t s);
+cudaError_t gelu_bwd(const void* dy, const void* u, void* du, int64_t n, int dtype, cudaStream_t s);
+// column sums of a [rows, n] matrix in fp32 (deterministic two-pass)
+cudaError_t col_sum(const void* x, float* out, float* partial, int partial_rows, int64_t rows, int n,
+                    int dtype, cudaStream_t s);
+
+// ---- patch embed / head layout ------------------------------------------------
+cudaError_t im2col_patch(const void* x, int x_dtype, void* cols, int N, int C, int H, int W, int p,
+                         int dtype, cudaStream_t s);
+cudaError_t col2im_patch(const void* dcols, void* dx, int x_dtype, int N, int C, int H, int W, int p,
+                         int dtype, cudaStream_t s);
+cudaError_t unpatchify(const void* y2, void* out, int BT, int h, int w, int p, int C, int dtype,
+                       cudaStream_t s);
+cudaError_t patchify(const void* dout, void* dy2, int BT, int h, int w, int p, int C, int dtype,
+                     cudaStream_t s);
+
+// ---- losses ----------------------------------------------------------------------
+cudaError_t weighted_sse(const void* x, int x_dtype, const void* y, int y_dtype, const float* area_w,
+                         const float* ch_w, float* partial, int partial_n, float* out, int64_t lead,
+                         int C, int H, int W, cudaStream_t s);
+cudaError_t weighted_sse_bwd(const void* x, int x_dtype, const void* y, int y_dtype,
+                             const float* area_w, const float* ch_w, const float* gscale, void* dx,
+                             int64_t lead, int C, int H, int W, cudaStream_t s);
+cudaError_t weighted_se_per_plane(const void* x, int x_dtype, const void* y, int y_dtype,
+                                  const float* area_w, float* out, int64_t planes, int H, int W,
+                                  cudaStream_t s);
+
+// ---- optimizer -----------------------------------------------------------------
+cudaError_t adamw_step(float* p, const float* g, float* m, float* v, void* shadow, int shadow_dtype,
+                       const float* gscale, const int* skip, int64_t n, float lr, float b1, float b2,
+                       float eps, float wd, float bc1, float bc2, bool decoupled, cudaStream_t s);
+cudaError_t segment_sumsq(const float* x, const int64_t* block_lo, const int64_t* block_hi,
+                          const int* block_cls, int nblocks, int ncls, float* partial, float* out,
+                          cudaStream_t s);
+
+// ---- window attention ------------------------------------------------------------
+struct AttnGeom {
+  int B, T, H, W;      // token grid (local)
+  int nh, hd;          // local heads, head dim
+  int wh, ww;          // window
+  int sh, sw;          // index shift
+  int mask, mask_shift, row_offset, h_global;
+  float scale;
+  int64_t qkv_stride;  // elements between consecutive tokens in qkv (3*nh*hd)
+  int64_t out_stride;  // elements between tokens in out / dout (nh*hd)
+};
+cudaError_t window_attn_fwd(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
+                            const AttnGeom& g, int dtype, cudaStream_t s);
+cudaError_t window_attn_bwd(const void* qkv, const float* qw, const float* kw, const void* out,
+                            const void* dout, const float* lse, void* dqkv, float* dqw_part,
+                            float* dkw_part, const AttnGeom& g, int dtype, cudaStream_t s);
+
+// ---- tcgen05 GEMM ----------------------------------------------------------------
+struct GemmArgs {
+  const void* A;        // [M, K] row-major (K contiguous)
+  const void* B;        // [N, K] row-major (K contiguous)
+  void* D;              // [M, N] row-major output (ldd elements)
+  int64_t M, N, K;
+  int64_t lda, ldb, ldd;
+  const float* bias;    // [N] or null
+  const void* residual; // [*, N] (ldr) or null; row index = m % res_period
+  int64_t ldr, res_period;
+  void* preact;         // optional [M, N] pre-activation output (ldd)
+  int act;              // 0 none, 1 gelu
+  int dtype;            // kBF16 / kF16 (A, B, D, residual, preact)
+  int out_f32;          // D in fp32 instead of dtype
+  float alpha;
+  int accumulate;       // D += result (fp32 output only)
+};
+cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s);
+int gemm_tcgen05_supported(const GemmArgs& a);
+
+}  // namespace nsw

@@ -1,0 +1,317 @@
+"""Autograd functions binding the sm_100a kernels (CUDA tensors only).
+
+Forward GEMMs run on the tcgen05 kernel with their epilogues fused (bias, GELU with the
+pre-activation saved for backward, residual add, broadcast positional-embedding add).
+Backward data-gradient GEMMs also run on the tcgen05 kernel (against a cached
+transposed weight); weight-gradient GEMMs, whose operands are M-major, use cuBLAS with
+fp32 output.  Shapes the tcgen05 kernel cannot take (K or N not a multiple of 8: only
+tiny test models) use cuBLAS plus the fused epilogue kernel.
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import weights as wcache
+from ._ext import require
+from .geometry import WindowGeometry
+
+DT = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def _cdtype(x: torch.Tensor) -> torch.dtype:
+    if torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+
+
+_wt_cache = {}
+
+
+def _weight_t(params: Sequence[torch.Tensor], w: torch.Tensor) -> torch.Tensor:
+    """Cached contiguous transpose of a (concatenated) weight, keyed on versions."""
+    key = tuple(id(p) for p in params)
+    ver = tuple(p._version for p in params)
+    hit = _wt_cache.get(key)
+    if hit is not None and hit[0] == ver and hit[1].dtype == w.dtype:
+        return hit[1]
+    t = w.t().contiguous()
+    _wt_cache[key] = (ver, t)
+    return t
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, residual=None, res_period: int = 0,
+         act: int = 0, preact: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``epilogue(a @ b.T)``; a [M, K], b [N, K] in the compute dtype."""
+    ext = require()
+    a = a.contiguous()
+    if ext.gemm_supported(a, b, False):
+        return ext.gemm(a, b, bias, residual, res_period, act, preact)
+    acc = torch.mm(a, b.t())
+    if bias is None and residual is None and act == 0:
+        return acc
+    y, pre = ext.bias_act_residual(acc, bias, residual, res_period, act, preact is not None, DT[a.dtype])
+    if preact is not None:
+        preact.copy_(pre)
+    return y
+
+
+def wgrad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """fp32 ``dy^T @ x`` (cuBLAS; M-major operands)."""
+    return torch.mm(dy.t(), x, out_dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------- RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        ext = require()
+        dt = _cdtype(x)
+        x2 = x.reshape(-1, x.shape[-1]).to(dt).contiguous()
+        y, rstd = ext.rmsnorm_fwd(x2, w.detach().float().contiguous(), eps)
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shape = x.shape
+        ctx.in_dtype = x.dtype
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        ext = require()
+        x2, w, rstd = ctx.saved_tensors
+        dy2 = dy.reshape(x2.shape).to(x2.dtype).contiguous()
+        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd)
+        return dx.view(ctx.shape).to(ctx.in_dtype), dw.to(w.dtype), None
+
+
+def rms_norm_cuda(x, w, eps=None):
+    eps = float(torch.finfo(torch.float32).eps) if eps is None else float(eps)
+    return _RMSNorm.apply(x, w, eps)
+
+
+# ---------------------------------------------------------------------------- Linear
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, residual, act, nw, nb, *params):
+        ws, bs = params[:nw], params[nw:nw + nb]
+        dt = _cdtype(x)
+        K = x.shape[-1]
+        x2 = x.reshape(-1, K).to(dt)
+        W = wcache.get_cat(ws, dt)
+        if W.dim() != 2:
+            W = W.reshape(W.shape[0], -1)
+        N = W.shape[0]
+        b = None
+        if nb:
+            b = bs[0].detach().float() if nb == 1 else torch.cat([t.detach().float() for t in bs])
+        res2 = residual.reshape(-1, N).to(dt).contiguous() if residual is not None else None
+        needs_grad = ctx.needs_input_grad[0] or any(ctx.needs_input_grad[5:])
+        pre = None
+        if act and needs_grad:
+            pre = torch.empty(x2.shape[0], N, dtype=dt, device=x.device)
+        y = gemm(x2, W, b, res2, 0, act, pre)
+        ctx.save_for_backward(x2, pre)
+        ctx.params = ws
+        ctx.W = W
+        ctx.act, ctx.nw, ctx.nb = act, nw, nb
+        ctx.shapes = [w.shape for w in ws]
+        ctx.bsizes = [t.numel() for t in bs]
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        ctx.has_res = residual is not None
+        ctx.res_dtype = residual.dtype if residual is not None else None
+        return y.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        ext = require()
+        x2, pre = ctx.saved_tensors
+        W = ctx.W
+        N = W.shape[0]
+        dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
+        du = ext.gelu_bwd(dy2, pre) if ctx.act else dy2
+        dx = None
+        if ctx.needs_input_grad[0]:
+            Wt = _weight_t(ctx.params, W)
+            dx = gemm(du, Wt).view(ctx.x_shape).to(ctx.x_dtype)
+        dW = wgrad(du, x2)
+        grads_w: List[torch.Tensor] = []
+        off = 0
+        for shp in ctx.shapes:
+            n = shp[0]
+            grads_w.append(dW[off:off + n].reshape(shp))
+            off += n
+        grads_b: List[torch.Tensor] = []
+        if ctx.nb:
+            db = ext.col_sum(du)
+            off = 0
+            for n in ctx.bsizes:
+                grads_b.append(db[off:off + n])
+                off += n
+        dres = dy.to(ctx.res_dtype) if ctx.has_res else None
+        return (dx, dres, None, None, None, *grads_w, *grads_b)
+
+
+def _as_list(t):
+    if t is None:
+        return []
+    if isinstance(t, torch.Tensor):
+        return [t]
+    return list(t)
+
+
+def linear_cuda(x, weight, bias=None, residual=None, activation=None):
+    ws = _as_list(weight)
+    bs = _as_list(bias)
+    act = {None: 0, "gelu": 1}[activation]
+    return _Linear.apply(x, residual, act, len(ws), len(bs), *ws, *bs)
+
+
+# ---------------------------------------------------------------------------- attention
+def _geom_ints(B, T, H, W, nh, hd, g: WindowGeometry):
+    return [B, T, H, W, nh, hd, g.window[0], g.window[1], g.shift[0], g.shift[1], int(g.mask),
+            int(g.mask_shift), int(g.row_offset), int(g.h_global if g.h_global else H)]
+
+
+class _WindowAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, qw, kw, gi, scale):
+        ext = require()
+        qkv2 = qkv.contiguous()
+        out, lse = ext.window_attn_fwd(qkv2, qw.detach().float().contiguous(),
+                                       kw.detach().float().contiguous(), gi, scale)
+        ctx.save_for_backward(qkv2, qw, kw, out, lse)
+        ctx.gi, ctx.scale = gi, scale
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        ext = require()
+        qkv, qw, kw, out, lse = ctx.saved_tensors
+        dqkv, dqw, dkw = ext.window_attn_bwd(qkv, qw.detach().float().contiguous(),
+                                             kw.detach().float().contiguous(), out,
+                                             dout.to(qkv.dtype).contiguous(), lse, ctx.gi, ctx.scale)
+        return dqkv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None
+
+
+def window_attention_cuda(qkv, q_norm_w, k_norm_w, num_heads, head_dim, geom: WindowGeometry, scale):
+    B, T, H, W, C3 = qkv.shape
+    dt = _cdtype(qkv)
+    gi = _geom_ints(B, T, H, W, num_heads, head_dim, geom)
+    out = _WindowAttn.apply(qkv.to(dt), q_norm_w, k_norm_w, gi, float(scale))
+    return out.view(B, T, H, W, num_heads * head_dim)
+
+
+# ---------------------------------------------------------------------------- patch embed
+class _PatchEmbed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, add, p):
+        ext = require()
+        dt = _cdtype(x)
+        N, C, H, Wd = x.shape
+        h, wn = H // p, Wd // p
+        E = w.shape[0]
+        cols = ext.im2col(x.contiguous(), p, DT[dt])
+        W2 = wcache.get(w, dt).reshape(E, -1)
+        res, period = None, 0
+        if add is not None:
+            res = add.reshape(-1, E).to(dt).contiguous()
+            period = res.shape[0]
+        y = gemm(cols, W2, b.detach().float() if b is not None else None, res, period)
+        ctx.save_for_backward(cols)
+        ctx.w_param, ctx.W2 = w, W2
+        ctx.meta = (N, C, H, Wd, p, h, wn, E, x.dtype, add is not None,
+                    add.dtype if add is not None else None, period)
+        ctx.has_b = b is not None
+        return y.view(N, h, wn, E)
+
+    @staticmethod
+    def backward(ctx, dy):
+        ext = require()
+        (cols,) = ctx.saved_tensors
+        N, C, H, Wd, p, h, wn, E, xdt, has_add, add_dt, period = ctx.meta
+        dy2 = dy.reshape(-1, E).to(cols.dtype).contiguous()
+        dW = wgrad(dy2, cols).view(ctx.w_param.shape)
+        db = ext.col_sum(dy2) if ctx.has_b else None
+        dadd = None
+        if has_add:
+            dadd = dy2.float().view(-1, period, E).sum(0).view(-1, h, wn, E).to(add_dt)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            Wt = _weight_t([ctx.w_param], ctx.W2)
+            dcols = gemm(dy2, Wt)
+            dx = ext.col2im(dcols, N, C, H, Wd, p, DT[xdt])
+        return dx, dW, db, dadd, None
+
+
+def patch_embed_cuda(x, weight, bias, patch_size, add=None):
+    return _PatchEmbed.apply(x, weight, bias, add, int(patch_size))
+
+
+# ---------------------------------------------------------------------------- head
+class _Head(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, p, C):
+        ext = require()
+        dt = _cdtype(x)
+        B, T, h, wn, E = x.shape
+        x2 = x.reshape(-1, E).to(dt).contiguous()
+        W = wcache.get(w, dt)
+        y2 = gemm(x2, W)
+        out = ext.unpatchify(y2, B, T, h, wn, p, C)
+        ctx.save_for_backward(x2)
+        ctx.w_param, ctx.W = w, W
+        ctx.meta = (B, T, h, wn, E, p, C, x.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        ext = require()
+        (x2,) = ctx.saved_tensors
+        B, T, h, wn, E, p, C, xdt = ctx.meta
+        dy2 = ext.patchify(dout.to(x2.dtype).contiguous(), h, wn, p, C)
+        dW = wgrad(dy2, x2)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            Wt = _weight_t([ctx.w_param], ctx.W)
+            dx = gemm(dy2, Wt).view(B, T, h, wn, E).to(xdt)
+        return dx, dW, None, None
+
+
+def head_unpatchify_cuda(x, weight, patch_size, out_chans):
+    return _Head.apply(x, weight, int(patch_size), int(out_chans))
+
+
+# ---------------------------------------------------------------------------- losses
+class _WeightedSSE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, y, aw, cw):
+        ext = require()
+        xc, yc = x.contiguous(), y.contiguous()
+        awc = aw.float().contiguous().view(-1) if aw is not None else None
+        cwc = cw.float().contiguous().view(-1) if cw is not None else None
+        ctx.save_for_backward(xc, yc)
+        ctx.w = (awc, cwc)
+        return ext.weighted_sse(xc, yc, awc, cwc)
+
+    @staticmethod
+    def backward(ctx, g):
+        ext = require()
+        x, y = ctx.saved_tensors
+        awc, cwc = ctx.w
+        gs = g.detach().float().reshape(1).contiguous()
+        dx = ext.weighted_sse_bwd(x, y, awc, cwc, gs) if ctx.needs_input_grad[0] else None
+        dy = None
+        if ctx.needs_input_grad[1]:
+            dy = -ext.weighted_sse_bwd(x, y, awc, cwc, gs).to(y.dtype)
+        return dx, dy, None, None
+
+
+def weighted_sse_cuda(x, y, area_w=None, ch_w=None):
+    return _WeightedSSE.apply(x, y, area_w, ch_w)
+
+
+def weighted_se_per_channel_cuda(x, y, area_w):
+    ext = require()
+    return ext.weighted_se_per_plane(x.detach().contiguous(), y.detach().contiguous(),
+                                     area_w.detach().float().contiguous().view(-1))

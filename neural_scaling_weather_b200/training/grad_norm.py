@@ -33,15 +33,23 @@ class ShardedNorm:
             seg_hi.append(lo + p.numel())
             seg_cls.append(c)
         self.classes = sorted(classes, key=classes.get)
-        dev = space.data.device
-        self.seg_lo = torch.tensor(seg_lo, dtype=torch.int64, device=dev)
-        self.seg_hi = torch.tensor(seg_hi, dtype=torch.int64, device=dev)
-        self.seg_cls = torch.tensor(seg_cls, dtype=torch.int32, device=dev)
         self._lo, self._hi, self._cls = seg_lo, seg_hi, seg_cls
+        # fixed work split for the kernel: blocks of <= 64K elements inside one segment
+        blo, bhi, bcls = [], [], []
+        chunk = 1 << 16
+        for lo, hi, c in zip(seg_lo, seg_hi, seg_cls):
+            for a in range(lo, hi, chunk):
+                blo.append(a)
+                bhi.append(min(hi, a + chunk))
+                bcls.append(c)
+        dev = space.data.device
+        self.block_lo = torch.tensor(blo, dtype=torch.int64, device=dev)
+        self.block_hi = torch.tensor(bhi, dtype=torch.int64, device=dev)
+        self.block_cls = torch.tensor(bcls, dtype=torch.int32, device=dev)
 
     def _class_sums(self, buf: torch.Tensor) -> torch.Tensor:
         if buf.is_cuda:
-            return _ext.require().segment_sumsq(buf, self.seg_lo, self.seg_hi, self.seg_cls,
+            return _ext.require().segment_sumsq(buf, self.block_lo, self.block_hi, self.block_cls,
                                                 len(self.classes))
         out = torch.zeros(len(self.classes), dtype=torch.float32)
         for lo, hi, c in zip(self._lo, self._hi, self._cls):

@@ -1,0 +1,248 @@
+"""Numerics of every sm_100a kernel against a plain-PyTorch fp32 reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+cuda = pytest.importorskip("torch").cuda
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+from neural_scaling_weather_b200 import ops  # noqa: E402
+from neural_scaling_weather_b200.ops import _ext, reference  # noqa: E402
+from neural_scaling_weather_b200.ops.geometry import WindowGeometry  # noqa: E402
+
+DEV = torch.device("cuda")
+
+
+@pytest.fixture(autouse=True)
+def _ext_loaded():
+    ext = _ext.require()
+    yield ext
+    assert ext.read_error_flag(True) == 0
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+# --------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (300, 1120, 1168), (1000, 3072, 1024),
+                                   (777, 128, 64), (129, 40, 96), (4096, 4096, 1024)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_plain(M, N, K, dtype, _ext_loaded):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device=DEV, dtype=dtype)
+    b = torch.randn(N, K, device=DEV, dtype=dtype)
+    d = _ext_loaded.gemm(a, b)
+    ref = a.float() @ b.float().t()
+    assert rel(d, ref) < 1e-2
+
+
+def test_gemm_epilogues(_ext_loaded):
+    torch.manual_seed(1)
+    M, N, K = 515, 512, 256
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.1
+    bias = torch.randn(N, device=DEV)
+    res = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    pre = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    y = _ext_loaded.gemm(a, b, bias, None, 0, 1, pre)
+    u = a.float() @ b.float().t() + bias
+    assert rel(pre, u) < 1e-2
+    assert rel(y, torch.nn.functional.gelu(u)) < 1e-2
+    y2 = _ext_loaded.gemm(a, b, bias, res)
+    assert rel(y2, u + res.float()) < 1e-2
+    # broadcast residual (period)
+    pos = torch.randn(128, N, device=DEV, dtype=torch.bfloat16)
+    a3 = a[:512].contiguous()
+    y3 = _ext_loaded.gemm(a3, b, None, pos, 128)
+    ref3 = (a3.float() @ b.float().t()).view(4, 128, N) + pos.float()
+    assert rel(y3, ref3.view(512, N)) < 1e-2
+    # fp32 output with accumulation
+    out = torch.randn(M, N, device=DEV)
+    base = out.clone()
+    _ext_loaded.gemm(a, b, None, None, 0, 0, None, True, 0.5, out, True)
+    assert rel(out, base + 0.5 * (a.float() @ b.float().t())) < 1e-3
+
+
+# --------------------------------------------------------------------------- RMSNorm
+@pytest.mark.parametrize("n", [64, 1024, 2048])
+def test_rmsnorm(n):
+    torch.manual_seed(0)
+    x = torch.randn(333, n, device=DEV).bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(n, device=DEV)).requires_grad_()
+    y = ops.rms_norm(x, w)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().clone().requires_grad_()
+    yr = reference.rms_norm(xr, wr)
+    assert rel(y, yr) < 1e-2
+    g = torch.randn_like(yr)
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    assert rel(x.grad, xr.grad) < 2e-2
+    assert rel(w.grad, wr.grad) < 2e-2
+
+
+# --------------------------------------------------------------------------- attention
+ATTN_CASES = [
+    # B, T, H, W, nh, hd, window, shift, mask
+    (1, 1, 18, 36, 2, 64, (9, 18), (0, 0), False),
+    (1, 1, 18, 36, 2, 64, (9, 18), (4, 9), True),
+    (2, 1, 8, 16, 4, 16, (4, 8), (2, 4), True),
+    (1, 2, 8, 16, 2, 32, (4, 8), (2, 4), True),
+    (1, 1, 12, 24, 2, 128, (4, 8), (2, 4), True),
+]
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_window_attention(case):
+    B, T, H, W, nh, hd, win, shift, mask = case
+    torch.manual_seed(0)
+    C = nh * hd
+    geom = WindowGeometry(window=win, shift=shift, mask=mask, mask_shift=shift[0], row_offset=0,
+                          h_global=H)
+    qkv = torch.randn(B, T, H, W, 3 * C, device=DEV).bfloat16().requires_grad_()
+    qw = (1 + 0.1 * torch.randn(hd, device=DEV)).requires_grad_()
+    kw = (1 + 0.1 * torch.randn(hd, device=DEV)).requires_grad_()
+    scale = hd ** -0.5
+    out = ops.window_attention(qkv, qw, kw, nh, hd, geom, scale)
+    qr = qkv.detach().float().requires_grad_()
+    qwr = qw.detach().clone().requires_grad_()
+    kwr = kw.detach().clone().requires_grad_()
+    ref = reference.window_attention(qr, qwr, kwr, nh, hd, geom, scale)
+    assert rel(out, ref) < 2e-2
+    g = torch.randn_like(ref)
+    out.backward(g.bfloat16())
+    ref.backward(g)
+    assert rel(qkv.grad, qr.grad) < 4e-2
+    assert rel(qw.grad, qwr.grad) < 4e-2
+    assert rel(kw.grad, kwr.grad) < 4e-2
+
+
+# --------------------------------------------------------------------------- linear op
+@pytest.mark.parametrize("act,residual", [(None, False), ("gelu", False), (None, True)])
+def test_linear_op(act, residual):
+    torch.manual_seed(0)
+    x = torch.randn(2, 3, 40, 64, device=DEV).bfloat16().requires_grad_()
+    w1 = (0.05 * torch.randn(96, 64, device=DEV)).requires_grad_()
+    w2 = (0.05 * torch.randn(32, 64, device=DEV)).requires_grad_()
+    b1 = torch.randn(96, device=DEV).requires_grad_()
+    b2 = torch.randn(32, device=DEV).requires_grad_()
+    res = torch.randn(2, 3, 40, 128, device=DEV).bfloat16().requires_grad_() if residual else None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = ops.linear(x, [w1, w2], [b1, b2], residual=res, activation=act)
+    xr = x.detach().float().requires_grad_()
+    ws = [t.detach().clone().requires_grad_() for t in (w1, w2, b1, b2)]
+    rr = res.detach().float().requires_grad_() if residual else None
+    yr = reference.linear(xr, torch.cat(ws[:2]), torch.cat(ws[2:]), rr, act)
+    assert rel(y, yr) < 2e-2
+    g = torch.randn_like(yr)
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    assert rel(x.grad, xr.grad) < 3e-2
+    for a, b in zip((w1, w2, b1, b2), ws):
+        assert rel(a.grad, b.grad) < 3e-2
+    if residual:
+        assert rel(res.grad, rr.grad) < 1e-2
+
+
+# --------------------------------------------------------------------------- patch embed / head
+def test_patch_embed_and_head():
+    torch.manual_seed(0)
+    N, C, H, W, p, E = 2, 13, 24, 48, 4, 64
+    x = torch.randn(N, C, H, W, device=DEV).requires_grad_()
+    w = (0.05 * torch.randn(E, C, p, p, device=DEV)).requires_grad_()
+    b = torch.randn(E, device=DEV).requires_grad_()
+    add = torch.randn(1, H // p, W // p, E, device=DEV).bfloat16().requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = ops.patch_embed(x, w, b, p, add=add)
+    xr = x.detach().clone().requires_grad_()
+    wr, br = w.detach().clone().requires_grad_(), b.detach().clone().requires_grad_()
+    ar = add.detach().float().requires_grad_()
+    yr = reference.patch_embed(xr, wr, br, p, add=ar)
+    assert rel(y, yr) < 2e-2
+    g = torch.randn_like(yr)
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    for a, r in ((x, xr), (w, wr), (b, br), (add, ar)):
+        assert rel(a.grad, r.grad) < 3e-2
+
+    Co = 10
+    t = torch.randn(N, 1, H // p, W // p, E, device=DEV).bfloat16().requires_grad_()
+    hw = (0.05 * torch.randn(Co * p * p, E, device=DEV)).requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        o = ops.head_unpatchify(t, hw, p, Co)
+    tr = t.detach().float().requires_grad_()
+    hwr = hw.detach().clone().requires_grad_()
+    orf = reference.head_unpatchify(tr, hwr, p, Co)
+    assert o.shape == orf.shape
+    assert rel(o, orf) < 2e-2
+    g = torch.randn_like(orf)
+    o.backward(g.bfloat16())
+    orf.backward(g)
+    assert rel(t.grad, tr.grad) < 3e-2
+    assert rel(hw.grad, hwr.grad) < 3e-2
+
+
+# --------------------------------------------------------------------------- losses
+def test_weighted_sse():
+    torch.manual_seed(0)
+    x = torch.randn(2, 1, 7, 33, 65, device=DEV).bfloat16().requires_grad_()
+    y = torch.randn(2, 1, 7, 33, 65, device=DEV)
+    aw = torch.rand(33, 1, device=DEV)
+    cw = torch.rand(7, 1, 1, device=DEV)
+    s = ops.weighted_sse(x, y, aw, cw)
+    xr = x.detach().float().requires_grad_()
+    sr = reference.weighted_sse(xr, y, aw, cw)
+    assert abs(s.item() - sr.item()) / sr.item() < 1e-4
+    (3 * s).backward()
+    (3 * sr).backward()
+    assert rel(x.grad, xr.grad) < 1e-2
+    pc = ops.weighted_se_per_channel(x.detach(), y, aw)
+    pcr = reference.weighted_se_per_channel(x.detach().float(), y, aw)
+    assert rel(pc, pcr) < 1e-4
+
+
+# --------------------------------------------------------------------------- optimizer and norm
+def test_fused_adamw_matches_torch():
+    from neural_scaling_weather_b200.training.optimizer import FusedAdamW
+
+    torch.manual_seed(0)
+    shapes = [(33, 17), (64,), (5, 3, 2)]
+    ps = [torch.nn.Parameter(torch.randn(*s, device=DEV)) for s in shapes]
+    qs = [torch.nn.Parameter(p.detach().clone()) for p in ps]
+    opt = FusedAdamW(ps, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, shadow_dtype=torch.bfloat16)
+    ref = torch.optim.AdamW(qs, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1)
+    for _ in range(5):
+        for p, q in zip(ps, qs):
+            g = torch.randn_like(p)
+            p.grad.copy_(g)
+            q.grad = g.clone()
+        opt.step()
+        ref.step()
+    for p, q in zip(ps, qs):
+        assert torch.allclose(p, q, atol=1e-5, rtol=1e-5)
+    sd = opt.state_dict()
+    assert set(sd["state"][0].keys()) == {"step", "exp_avg", "exp_avg_sq"}
+    assert torch.allclose(opt.space.shadow.float(), opt.space.data, atol=1e-2, rtol=1e-2)
+
+
+def test_sharded_norm_kernel():
+    from neural_scaling_weather_b200.training.grad_norm import ShardedNorm
+    from neural_scaling_weather_b200.training.optimizer import FlatParamSpace
+
+    torch.manual_seed(0)
+    ps = [torch.nn.Parameter(torch.randn(s, device=DEV)) for s in (100000, 7, 70000)]
+    for p in ps:
+        p.comm_metadata = {"sharded": [], "shared": [], "reduce": []}
+    space = FlatParamSpace(ps)
+    for p in ps:
+        p.grad.copy_(torch.randn_like(p))
+    n = ShardedNorm(space).norm("grad")
+    ref = torch.sqrt(sum((p.grad.double() ** 2).sum() for p in ps))
+    assert abs(n.item() - ref.item()) / ref.item() < 1e-5
