@@ -168,6 +168,7 @@ def native(args, rank, world, local):
     ]
     cfg = C.compose("default", overrides)
     tr = Trainer(cfg)
+    tr.init_exp_dir(tr.exp_dir)
     tr.build()
     accum = tr.gradient_accum_steps
     _, batches, _ = make_batches(2, "cuda")

@@ -82,9 +82,9 @@ class WindowMultiHeadAttention(nn.Module):
         self.biasproj = BiasLayer(dim, comm_metadata=_meta([], ["tp-sp1-sp2"], ["sp1-sp2"]))
 
     def qkv_params(self):
-        w = torch.cat([self.q.weight, self.k.weight, self.v.weight], dim=0)
-        b = torch.cat([self.biasq.bias, self.biask.bias, self.biasv.bias], dim=0)
-        return w, b
+        """q/k/v weights and biases; the fused GEMM concatenates them along N."""
+        return ([self.q.weight, self.k.weight, self.v.weight],
+                [self.biasq.bias, self.biask.bias, self.biasv.bias])
 
 
 class MLP(nn.Module):

@@ -1,0 +1,176 @@
+"""Kernel microbenchmarks with roofline fractions.
+
+``python -m neural_scaling_weather_b200.ops.bench_kernels <kernel> [--iters N] [shape flags]``
+
+Each kernel is timed with CUDA events on the launching stream after warm-up, with a
+synchronize on both sides; the inputs of the default shapes are larger than the 126 MB L2.
+The fraction is taken against ``MEASURED_PEAKS.json`` when present (copy bandwidth and
+cuBLAS bf16 throughput measured on this pool), otherwise against fixed fallback peaks.
+Also used, with a small ``--iters``, as the command profiled by ``ncu``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from . import _ext
+from .geometry import WindowGeometry
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "of measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "of fallback"}
+
+
+def timeit(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def report(name, ms, flops=None, nbytes=None, extra=None):
+    pk = peaks()
+    out = {"kernel": name, "ms": round(ms, 4)}
+    if flops:
+        tf = flops / ms / 1e9
+        out["tflops"] = round(tf, 1)
+        out["frac_tensor"] = f"{tf / pk['bf16_tflops']:.3f} {pk['src']}"
+    if nbytes:
+        gbs = nbytes / ms / 1e6
+        out["gbs"] = round(gbs, 1)
+        out["frac_hbm"] = f"{gbs / pk['hbm_gbs']:.3f} {pk['src']}"
+    if extra:
+        out.update(extra)
+    print(json.dumps(out))
+    return out
+
+
+def bench_gemm(a):
+    ext = _ext.require()
+    M, N, K = a.M, a.N, a.K
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    bias = torch.randn(N, device="cuda") if a.epilogue in ("bias", "gelu") else None
+    pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16) if a.epilogue == "gelu" else None
+    res = torch.randn(M, N, device="cuda", dtype=torch.bfloat16) if a.epilogue == "residual" else None
+    act = 1 if a.epilogue == "gelu" else 0
+    fn = lambda: ext.gemm(A, B, bias, res, 0, act, pre)  # noqa: E731
+    ms = timeit(fn, a.iters)
+    nbytes = 2 * (M * K + N * K + M * N * (1 + (pre is not None) + (res is not None)))
+    r = report(f"gemm_tcgen05[{a.epilogue}] {M}x{N}x{K}", ms, 2.0 * M * N * K, nbytes)
+    if a.compare:
+        ms2 = timeit(lambda: torch.mm(A, B.t()), a.iters)
+        report(f"cublas torch.mm {M}x{N}x{K}", ms2, 2.0 * M * N * K, 2 * (M * K + N * K + M * N))
+    return r
+
+
+def bench_attention(a):
+    from . import window_attention
+
+    B, H, W, nh, hd = 1, a.H, a.W, a.heads, 64
+    C = nh * hd
+    geom = WindowGeometry(window=(9, 18), shift=(4, 9), mask=True, mask_shift=4, row_offset=0, h_global=H)
+    qkv = torch.randn(B, 1, H, W, 3 * C, device="cuda", dtype=torch.bfloat16)
+    qw = torch.ones(hd, device="cuda")
+    kw = torch.ones(hd, device="cuda")
+    ext = _ext.require()
+    gi = [B, 1, H, W, nh, hd, 9, 18, 4, 9, 1, 4, 0, H]
+    out, lse = ext.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5)
+    tokens = B * H * W
+    L = 162
+    flops = 4.0 * tokens * L * hd * nh  # QK^T and PV
+    ms = timeit(lambda: ext.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5), a.iters)
+    report(f"window_attn_fwd tokens={tokens} heads={nh}", ms, flops, 2 * tokens * 4 * C)
+    dout = torch.randn_like(out)
+    ms = timeit(lambda: ext.window_attn_bwd(qkv.view(-1, 3 * C), qw, kw, out, dout, lse, gi, hd ** -0.5),
+                a.iters)
+    report(f"window_attn_bwd tokens={tokens} heads={nh}", ms, 2.5 * flops, 2 * tokens * 8 * C)
+
+
+def bench_rmsnorm(a):
+    ext = _ext.require()
+    x = torch.randn(a.M, a.N, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(a.N, device="cuda")
+    ms = timeit(lambda: ext.rmsnorm_fwd(x, w, 1e-7), a.iters)
+    report(f"rmsnorm_fwd {a.M}x{a.N}", ms, None, 4 * a.M * a.N)
+    y, r = ext.rmsnorm_fwd(x, w, 1e-7)
+    ms = timeit(lambda: ext.rmsnorm_bwd(y, x, w, r), a.iters)
+    report(f"rmsnorm_bwd {a.M}x{a.N}", ms, None, 6 * a.M * a.N)
+
+
+def bench_adamw(a):
+    ext = _ext.require()
+    n = a.M
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    v.abs_()
+    sh = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    one = torch.ones(1, device="cuda")
+    zero = torch.zeros(1, device="cuda", dtype=torch.int32)
+    fn = lambda: ext.adamw_step(p, g, m, v, sh, one, zero, 1e-4, 0.9, 0.95, 1e-8, 1e-4, 0.5, 0.5, True)  # noqa
+    ms = timeit(fn, a.iters)
+    report(f"adamw_step n={n}", ms, None, n * (4 * 4 + 3 * 4 + 2))
+
+
+def bench_sse(a):
+    ext = _ext.require()
+    x = torch.randn(1, 1, 70, 720, 1440, device="cuda", dtype=torch.bfloat16)
+    y = torch.randn(1, 1, 70, 720, 1440, device="cuda")
+    aw = torch.rand(720, device="cuda")
+    ms = timeit(lambda: ext.weighted_sse(x, y, aw, None), a.iters)
+    report("weighted_sse 70x720x1440", ms, None, x.numel() * 6)
+    g = torch.ones(1, device="cuda")
+    ms = timeit(lambda: ext.weighted_sse_bwd(x, y, aw, None, g), a.iters)
+    report("weighted_sse_bwd 70x720x1440", ms, None, x.numel() * 8)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["gemm", "attention", "rmsnorm", "adamw", "sse", "all"])
+    ap.add_argument("--M", type=int, default=64800)
+    ap.add_argument("--N", type=int, default=3072)
+    ap.add_argument("--K", type=int, default=1024)
+    ap.add_argument("--H", type=int, default=180)
+    ap.add_argument("--W", type=int, default=360)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--epilogue", default="bias", choices=["none", "bias", "gelu", "residual"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--compare", action="store_true")
+    a = ap.parse_args()
+    if a.kernel in ("gemm", "all"):
+        bench_gemm(a)
+    if a.kernel in ("attention", "all"):
+        bench_attention(a)
+    if a.kernel in ("rmsnorm", "all"):
+        a2 = argparse.Namespace(**vars(a))
+        if a.kernel == "all":
+            a2.N = 1024
+        bench_rmsnorm(a2)
+    if a.kernel in ("adamw", "all"):
+        a3 = argparse.Namespace(**vars(a))
+        a3.M = 204_000_000 if a.kernel == "all" else a.M
+        bench_adamw(a3)
+    if a.kernel in ("sse", "all"):
+        bench_sse(a)
+    err = _ext.require().read_error_flag(True)
+    if err:
+        raise SystemExit(f"device error flag {err}")
+
+
+if __name__ == "__main__":
+    main()

@@ -101,20 +101,28 @@ __device__ __forceinline__ int win_label(const AttnGeom& g, const WinPos& p, int
   return row_g >= g.h_global - g.mask_shift ? 1 : 0;
 }
 
-// Load rows [0, rows_pad) of one of q/k/v/(a T*HD tensor) into smem (row stride HD+8),
-// zero-filling rows >= L.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+
+// Issue asynchronous 16-byte copies of rows [0, L) of one of q/k/v/dO into smem (row
+// stride HD+8) and zero rows [L, rows_pad); completion is awaited by cp_async_wait_all.
 template <typename T, int HD>
 __device__ __forceinline__ void load_rows(T* s, const T* base, int64_t stride, int64_t col0,
                                           const AttnGeom& g, const WinPos& p, int L, int rows_pad) {
   constexpr int CH = HD / 8;
   for (int idx = threadIdx.x; idx < rows_pad * CH; idx += blockDim.x) {
     const int i = idx / CH, c = idx - i * CH;
-    uint4 v = make_uint4(0, 0, 0, 0);
+    T* dst = s + i * (HD + 8) + c * 8;
     if (i < L) {
       const int64_t tok = win_token(g, p, i);
-      v = *reinterpret_cast<const uint4*>(base + tok * stride + col0 + c * 8);
+      cp_async16(dst, base + tok * stride + col0 + c * 8);
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
-    *reinterpret_cast<uint4*>(s + i * (HD + 8) + c * 8) = v;
   }
 }
 
@@ -146,7 +154,7 @@ __device__ __forceinline__ void norm_rows(T* s, const float* w, int L, float* rs
 
 // ============================================================================= forward
 template <typename T, int HD>
-__global__ void __launch_bounds__(384) fwd_kernel(const T* __restrict__ qkv, const float* __restrict__ qw,
+__global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, const float* __restrict__ qw,
                                                   const float* __restrict__ kw, T* __restrict__ out,
                                                   float* __restrict__ lse, AttnGeom g) {
   constexpr int RS = HD + 8;  // smem row stride (elements); +16 B breaks bank conflicts
@@ -169,6 +177,7 @@ __global__ void __launch_bounds__(384) fwd_kernel(const T* __restrict__ qkv, con
   load_rows<T, HD>(sK, qkv, g.qkv_stride, 1 * C + (int64_t)h * HD, g, p, L, lk);
   load_rows<T, HD>(sV, qkv, g.qkv_stride, 2 * C + (int64_t)h * HD, g, p, L, lk);
   for (int i = threadIdx.x; i < lk; i += blockDim.x) sLab[i] = i < L ? (signed char)win_label(g, p, i) : (signed char)-1;
+  cp_async_wait_all();
   __syncthreads();
   norm_rows<T, HD>(sQ, qw, L, nullptr);
   norm_rows<T, HD>(sK, kw, L, nullptr);
@@ -377,7 +386,7 @@ __device__ __forceinline__ void store_rows_c(float (*acc)[4], int row0, int lane
 }
 
 template <typename T, int HD>
-__global__ void __launch_bounds__(384) bwd_kernel(const T* __restrict__ qkv, const float* __restrict__ qw,
+__global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, const float* __restrict__ qw,
                                                   const float* __restrict__ kw, const T* __restrict__ out,
                                                   const T* __restrict__ dout, const float* __restrict__ lse,
                                                   T* __restrict__ dqkv, float* __restrict__ dqw_part,
@@ -431,6 +440,7 @@ __global__ void __launch_bounds__(384) bwd_kernel(const T* __restrict__ qkv, con
       if (lane == 0) sD[i] = acc;
     }
   }
+  cp_async_wait_all();
   __syncthreads();
   norm_rows<T, HD>(sQ, qw, L, sRq);
   norm_rows<T, HD>(sK, kw, L, sRk);
@@ -643,7 +653,7 @@ static cudaError_t launch_fwd(const void* qkv, const float* qw, const float* kw,
   const int nqt = (L + 15) / 16;
   const int lk = ((L + 63) / 64) * 64;
   const size_t smem = (size_t)(nqt * 16 + 2 * lk) * (HD + 8) * sizeof(T) + lk;
-  int nw = nqt < 12 ? nqt : 12;
+  int nw = nqt < 8 ? nqt : 8;
   if (nw < 1) nw = 1;
   auto k = fwd_kernel<T, HD>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -661,7 +671,7 @@ static cudaError_t launch_bwd(const void* qkv, const float* qw, const float* kw,
   const int lp = nt * 16;
   const size_t smem = (size_t)4 * lp * (HD + 8) * sizeof(T) + (size_t)4 * lp * sizeof(float) +
                       2 * HD * sizeof(float) + lp;
-  int nw = 2 * nt < 12 ? 2 * nt : 12;
+  int nw = 2 * nt < 6 ? 2 * nt : 6;
   auto k = bwd_kernel<T, HD>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid(g.B * (g.H / g.wh) * (g.W / g.ww), g.nh);

@@ -12,8 +12,10 @@
 //           committing each stage back to its empty barrier and each finished tile to
 //           a tmem_full barrier; two accumulators let the epilogue of tile i overlap
 //           the MMAs of tile i+1;
-//   warps 2-5: epilogue, one TMEM lane quadrant (32 rows) each, tcgen05.ld 32 columns
-//           at a time, fused bias/GELU/residual, 16-byte global stores.
+//   warps 2-9: epilogue, two warps per TMEM lane quadrant (32 rows) splitting the
+//           columns; tcgen05.ld 32 columns at a time, fused bias/GELU/residual, and
+//           row-major 32x32 tiles staged in shared memory so that global loads/stores
+//           are coalesced (4 lanes per 64-byte row segment).
 // The CTA grid is the SM count; tiles are walked with N fastest so concurrently
 // running CTAs share the A tile through L2.  Every mbarrier wait is bounded by a
 // %globaltimer budget: on expiry the kernel records kErrWaitTimeout in the device error
@@ -28,7 +30,9 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // bf16: 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                   // 2 warps per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
+constexpr int kStageRow = 40;                   // staging row stride (elements): 32 + 8 pad
 constexpr unsigned long long kWaitBudgetNs = 4000000000ull;  // 4 s
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -152,6 +156,7 @@ struct Smem {
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
+  alignas(16) T stage[kEpiWarps][32 * kStageRow];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&S.tmem_full[a], 1);
-      mbar_init(&S.tmem_empty[a], 4);
+      mbar_init(&S.tmem_empty[a], kEpiWarps);
     }
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -257,7 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int ew = warp - 2;
+    const int q = warp & 3;         // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;       // which half of the BN columns
+    T* stg = S.stage[ew];
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -265,78 +273,128 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t m0 = (tile / n_tiles) * BM;
       const int64_t n0 = (tile % n_tiles) * BN;
-      const int64_t row = m0 + q * 32 + lane;
+      const int64_t row_base = m0 + q * 32;
+      const int64_t row = row_base + lane;
       const bool row_ok = row < ep.M;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
         const int64_t nb = n0 + c * 32;
-        if (!row_ok || nb >= ep.N) continue;
+        if (nb >= ep.N) continue;  // warp-uniform
+        const bool full = nb + 32 <= ep.N;
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) * ep.alpha;
-        const bool full = nb + 32 <= ep.N;
         if (ep.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (full || nb + j < ep.N) f[j] += ep.bias[nb + j];
-        }
-        if (ep.preact) {
-          T* pp = reinterpret_cast<T*>(ep.preact) + row * ep.ldd + nb;
           if (full) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(pp)[v] = pack8<T>(&f[8 * v]);
+            for (int v = 0; v < 8; ++v) {
+              const float4 b4 = __ldg(reinterpret_cast<const float4*>(ep.bias + nb) + v);
+              f[4 * v] += b4.x;
+              f[4 * v + 1] += b4.y;
+              f[4 * v + 2] += b4.z;
+              f[4 * v + 3] += b4.w;
+            }
           } else {
-            for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(f[j]);
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < ep.N) f[j] += ep.bias[nb + j];
           }
+        }
+        if (!full || ep.out_f32) {
+          // ragged column edge or fp32 output: direct per-row stores
+          if (row_ok) {
+            if (ep.preact) {
+              T* pp = reinterpret_cast<T*>(ep.preact) + row * ep.ldd + nb;
+              for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(f[j]);
+            }
+            if (ep.act == 1) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = gelu_f(f[j]);
+            }
+            if (ep.residual) {
+              const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
+              for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
+            }
+            if (ep.out_f32) {
+              float* dp = reinterpret_cast<float*>(ep.D) + row * ep.ldd + nb;
+              if (full) {
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                  float4 o = make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
+                  if (ep.accumulate) {
+                    const float4 old = reinterpret_cast<float4*>(dp)[v];
+                    o.x += old.x;
+                    o.y += old.y;
+                    o.z += old.z;
+                    o.w += old.w;
+                  }
+                  reinterpret_cast<float4*>(dp)[v] = o;
+                }
+              } else {
+                for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = ep.accumulate ? dp[j] + f[j] : f[j];
+              }
+            } else {
+              T* dp = reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb;
+              for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = from_f<T>(f[j]);
+            }
+          }
+          continue;
+        }
+        // ---- full 32-column chunk, 16-bit output: staged, coalesced
+        // lane l moves 16 bytes of row (l / 4 + 8 i), 8-column group (l % 4)
+        const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
+        if (ep.preact) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            *reinterpret_cast<uint4*>(stg + lane * kStageRow + 8 * v) = pack8<T>(&f[8 * v]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = sub_r + 8 * i;
+            if (row_base + rr < ep.M)
+              *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.preact) + (row_base + rr) * ep.ldd + nb + sub_c) =
+                  *reinterpret_cast<const uint4*>(stg + rr * kStageRow + sub_c);
+          }
+          __syncwarp();
         }
         if (ep.act == 1) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = gelu_f(f[j]);
         }
         if (ep.residual) {
-          const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
-          if (full) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              float rr[8];
-              unpack8<T>(reinterpret_cast<const uint4*>(rp)[v], rr);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) f[8 * v + j] += rr[j];
-            }
-          } else {
-            for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
+          for (int i = 0; i < 4; ++i) {
+            const int rr = sub_r + 8 * i;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row_base + rr < ep.M)
+              v = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                  ((row_base + rr) % ep.res_period) * ep.ldr + nb + sub_c);
+            *reinterpret_cast<uint4*>(stg + rr * kStageRow + sub_c) = v;
           }
+          __syncwarp();
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            float rr8[8];
+            unpack8<T>(*reinterpret_cast<const uint4*>(stg + lane * kStageRow + 8 * v), rr8);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
+          }
+          __syncwarp();
         }
-        if (ep.out_f32) {
-          float* dp = reinterpret_cast<float*>(ep.D) + row * ep.ldd + nb;
-          if (full) {
 #pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              float4 o = make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
-              if (ep.accumulate) {
-                const float4 old = reinterpret_cast<float4*>(dp)[v];
-                o.x += old.x;
-                o.y += old.y;
-                o.z += old.z;
-                o.w += old.w;
-              }
-              reinterpret_cast<float4*>(dp)[v] = o;
-            }
-          } else {
-            for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = ep.accumulate ? dp[j] + f[j] : f[j];
-          }
-        } else {
-          T* dp = reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb;
-          if (full) {
+        for (int v = 0; v < 4; ++v)
+          *reinterpret_cast<uint4*>(stg + lane * kStageRow + 8 * v) = pack8<T>(&f[8 * v]);
+        __syncwarp();
 #pragma unroll
-            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dp)[v] = pack8<T>(&f[8 * v]);
-          } else {
-            for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = from_f<T>(f[j]);
-          }
+        for (int i = 0; i < 4; ++i) {
+          const int rr = sub_r + 8 * i;
+          if (row_base + rr < ep.M)
+            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + (row_base + rr) * ep.ldd + nb + sub_c) =
+                *reinterpret_cast<const uint4*>(stg + rr * kStageRow + sub_c);
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();

@@ -32,6 +32,8 @@ _wt_cache = {}
 
 def _weight_t(params: Sequence[torch.Tensor], w: torch.Tensor) -> torch.Tensor:
     """Cached contiguous transpose of a (concatenated) weight, keyed on versions."""
+    if not all(isinstance(p, torch.nn.Parameter) for p in params):
+        return w.t().contiguous()
     key = tuple(id(p) for p in params)
     ver = tuple(p._version for p in params)
     hit = _wt_cache.get(key)

@@ -13,12 +13,20 @@ from typing import Dict, Sequence, Tuple
 
 import torch
 
-_shadows: "weakref.WeakKeyDictionary[torch.Tensor, torch.Tensor]" = weakref.WeakKeyDictionary()
+# id(param) -> (weak reference to param, shadow); tensors cannot be dict keys by value
+_shadows: Dict[int, Tuple["weakref.ref", torch.Tensor]] = {}
 _cache: Dict[Tuple, Tuple[Tuple[int, ...], torch.Tensor]] = {}
 
 
 def register_shadow(param: torch.Tensor, shadow: torch.Tensor) -> None:
-    _shadows[param] = shadow
+    _shadows[id(param)] = (weakref.ref(param), shadow)
+
+
+def _shadow_of(param: torch.Tensor):
+    hit = _shadows.get(id(param))
+    if hit is None or hit[0]() is not param:
+        return None
+    return hit[1]
 
 
 def clear() -> None:
@@ -30,7 +38,9 @@ def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """``param`` in ``dtype`` (a registered shadow, or a version-cached cast)."""
     if param.dtype == dtype:
         return param.detach()
-    sh = _shadows.get(param)
+    if not isinstance(param, torch.nn.Parameter) or param.is_inference():
+        return param.detach().to(dtype)  # temporaries are not cached
+    sh = _shadow_of(param)
     if sh is not None and sh.dtype == dtype:
         return sh
     key = (id(param), dtype)
@@ -47,9 +57,11 @@ def get_cat(params: Sequence[torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
     """Concatenation along dim 0 of several parameters, cached on their versions."""
     if len(params) == 1:
         return get(params[0], dtype)
+    if not all(isinstance(p, torch.nn.Parameter) for p in params):
+        return torch.cat([p.detach().to(dtype) for p in params], dim=0)
     key = (tuple(id(p) for p in params), dtype)
     ver = tuple(p._version for p in params)
-    sh = [_shadows.get(p) for p in params]
+    sh = [_shadow_of(p) for p in params]
     hit = _cache.get(key)
     if hit is not None and hit[0] == ver:
         return hit[1]
