@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--depth", type=int, default=MODEL["depth"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-rollout", action="store_true")
+    ap.add_argument("--breakdown", default=None,
+                    help="write a per-kernel device-time table of one step to this file (not timed)")
     return ap.parse_args()
 
 
@@ -192,6 +194,8 @@ def native(args, rank, world, local):
 
     # launch count (one extra step under the profiler, outside the timed region)
     launches = count_launches(lambda: step(dev_batches, False))
+    if args.breakdown and rank == 0:
+        kernel_breakdown(lambda: step(dev_batches, False), args.breakdown)
 
     sampler = ClockSampler(gpus=list(range(world)) if world > 1 else [torch.cuda.current_device()])
     if rank == 0:
@@ -280,6 +284,33 @@ def count_launches(fn):
         return None, str(e)
 
 
+def kernel_breakdown(fn, path):
+    """Per-kernel device time of one call of ``fn`` (profiler run; for analysis only)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    agg = {}
+    for ev in prof.events():
+        if ev.device_type is not None and "CUDA" in str(ev.device_type):
+            name = ev.name
+            for key in ("gemm_kernel", "fwd_kernel", "bwd_kernel", "rmsnorm", "adamw", "col_sum", "gelu",
+                        "sse", "im2col", "col2im", "unpatchify", "patchify", "sumsq", "nvjet", "gemm",
+                        "elementwise", "reduce", "copy", "fill", "cat"):
+                if key in name:
+                    name = key + ("(own)" if "nsw::" in ev.name else "")
+                    break
+            t = ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
+            c, tt = agg.get(name, (0, 0.0))
+            agg[name] = (c + 1, tt + t)
+    total = sum(v[1] for v in agg.values())
+    with open(path, "w") as f:
+        f.write(f"total device time of one step: {total / 1000:.1f} ms\n")
+        for name, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+            f.write(f"{t / 1000:10.2f} ms {100 * t / total:5.1f}% {c:6d}x  {name[:110]}\n")
+
+
 # ----------------------------------------------------------------------------- reference arm
 def reference(args, rank, world, local):
     sys.path.insert(0, os.path.join(HERE, "baseline"))
@@ -313,16 +344,21 @@ def reference(args, rank, world, local):
         comm.init_model_parallel_info(tp=1, sp1=1, sp2=1, dp=1, pp=1, order="sp1-sp2-tp-pp-dp")
     lat = np.linspace(90, -90, NLAT + 1)[:-1]
     lon = np.arange(NLON) * 360.0 / NLON
+    device = torch.device("cuda", local)
     md = {
         "sp_shapes": [[NLAT], [NLON]], "sp_slices": [slice(0, NLAT), slice(0, NLON)],
         "spatial_dims": [NLAT, NLON], "n_channels": N_CH, "channels": [f"c{i}" for i in range(N_CH)],
-        "coords": ns.misc_utils.get_spatial_coords((lat, lon)).float(),
-        "area_weights": ns.misc_utils.build_spherical_area_weights(lat)[:, None].float(),
+        "coords": ns.misc_utils.get_spatial_coords((lat, lon)).float().to(device),
+        "area_weights": ns.misc_utils.build_spherical_area_weights(lat)[:, None].float().to(device),
         "global_latitudes": lat, "global_longitudes": lon,
     }
-    device = torch.device("cuda", local)
     torch.manual_seed(0)
-    model = ns.model_helpers.get_model(cfg, md).to(device)
+    # Build on the GPU (default-device context): the model's constructor runs its
+    # torch.compile'd window_partition while building the shift mask, and Inductor's
+    # CPU backend cannot compile on this image (OpenMP spec file missing); on CUDA the
+    # same stock code compiles through Triton.
+    with torch.device(device):
+        model = ns.model_helpers.get_model(cfg, md).to(device)
     model = ns.mappings.init_ddp_model_and_reduction_hooks(model, device_ids=[local], output_device=[local],
                                                            backend="nccl")
     opt = ns.optimizer_utils.set_optimizer(cfg, model)
@@ -384,7 +420,8 @@ def main():
             res = reference(args, rank, world, local)
         except Exception as e:  # noqa: BLE001
             if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}))
+                msg = f"{type(e).__name__}: {e}".replace("\n", " ")
+                print(json.dumps({"impl": "reference", "unavailable": (msg[:200] + " ... " + msg[-600:]) if len(msg) > 800 else msg}))
             return
         if res is None:
             if rank == 0:

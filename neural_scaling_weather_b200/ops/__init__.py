@@ -64,6 +64,17 @@ def linear(x: torch.Tensor, weight: TensorOrParts, bias: Optional[TensorOrParts]
     return linear_cuda(x, weight, bias, residual, activation)
 
 
+def mlp(x: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor,
+        residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``fc2(GELU(fc1(x))) + residual`` with biases (fused backward on CUDA)."""
+    if not _use_cuda(x):
+        h = reference.linear(x, w1, b1, activation="gelu")
+        return reference.linear(h, w2, b2, residual=residual)
+    from .fused import mlp_cuda
+
+    return mlp_cuda(x, w1, b1, w2, b2, residual)
+
+
 def window_attention(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
                      num_heads: int, head_dim: int, geom: WindowGeometry, scale: float):
     """Shifted-window attention over (B, T, H, W, 3*nh*hd) -> (B, T, H, W, nh*hd)."""
@@ -118,6 +129,7 @@ __all__ = [
     "extension_available",
     "head_unpatchify",
     "linear",
+    "mlp",
     "patch_embed",
     "reference",
     "rms_norm",

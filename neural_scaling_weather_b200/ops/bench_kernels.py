@@ -80,6 +80,42 @@ def bench_gemm(a):
     return r
 
 
+def bench_block_gemms(a):
+    """The eight tcgen05 GEMMs of one transformer block (forward and data-gradient)."""
+    ext = _ext.require()
+    M, E = a.M, 1024
+    bf = dict(device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(M, E, **bf)
+    h4 = torch.randn(M, 4 * E, **bf)
+    u = torch.randn(M, 4 * E, **bf)
+    res = torch.randn(M, E, **bf)
+    W = {n: torch.randn(*shape, **bf) * 0.02 for n, shape in
+         [("qkv", (3 * E, E)), ("proj", (E, E)), ("fc1", (4 * E, E)), ("fc2", (E, 4 * E))]}
+    Wt = {n: w.t().contiguous() for n, w in W.items()}
+    b = {n: torch.randn(w.shape[0], device="cuda") for n, w in W.items()}
+    g3 = torch.randn(M, 3 * E, **bf)
+    pre = torch.empty(M, 4 * E, **bf)
+    cases = [
+        ("fwd qkv +bias", lambda: ext.gemm(x, W["qkv"], b["qkv"]), M, 3 * E, E),
+        ("fwd proj +bias+res", lambda: ext.gemm(x, W["proj"], b["proj"], res), M, E, E),
+        ("fwd fc1 +bias+gelu(+preact)", lambda: ext.gemm(x, W["fc1"], b["fc1"], None, 0, 1, pre), M, 4 * E, E),
+        ("fwd fc2 +bias+res", lambda: ext.gemm(h4, W["fc2"], b["fc2"], res), M, E, 4 * E),
+        ("dgrad qkv", lambda: ext.gemm(g3, Wt["qkv"]), M, E, 3 * E),
+        ("dgrad proj", lambda: ext.gemm(x, Wt["proj"]), M, E, E),
+        ("dgrad fc2 *gelu'(u)", lambda: ext.gemm(x, Wt["fc2"], None, u, 0, 2), M, 4 * E, E),
+        ("dgrad fc2 plain", lambda: ext.gemm(x, Wt["fc2"]), M, 4 * E, E),
+        ("dgrad fc1", lambda: ext.gemm(h4, Wt["fc1"]), M, E, 4 * E),
+        ("wgrad fc1 cublas", lambda: torch.mm(h4.t(), x, out_dtype=torch.float32), 4 * E, E, M),
+    ]
+    tot = 0.0
+    for name, fn, m, n, k in cases:
+        ms = timeit(fn, a.iters)
+        if "plain" not in name and "wgrad" not in name:
+            tot += ms
+        report(name, ms, 2.0 * m * n * k, None)
+    print(json.dumps({"block_fwd_plus_dgrad_ms": round(tot, 3)}))
+
+
 def bench_attention(a):
     from . import window_attention
 
@@ -141,7 +177,7 @@ def bench_sse(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "rmsnorm", "adamw", "sse", "all"])
+    ap.add_argument("kernel", choices=["gemm", "block", "attention", "rmsnorm", "adamw", "sse", "colsum", "all"])
     ap.add_argument("--M", type=int, default=64800)
     ap.add_argument("--N", type=int, default=3072)
     ap.add_argument("--K", type=int, default=1024)
@@ -154,6 +190,14 @@ def main():
     a = ap.parse_args()
     if a.kernel in ("gemm", "all"):
         bench_gemm(a)
+    if a.kernel == "block":
+        bench_block_gemms(a)
+    if a.kernel in ("colsum", "all"):
+        ext = _ext.require()
+        for n in (1024, 3072, 4096):
+            t = torch.randn(a.M, n, device="cuda", dtype=torch.bfloat16)
+            ms = timeit(lambda: ext.col_sum(t), a.iters)
+            report(f"col_sum {a.M}x{n}", ms, None, 2 * a.M * n)
     if a.kernel in ("attention", "all"):
         bench_attention(a)
     if a.kernel in ("rmsnorm", "all"):

@@ -62,10 +62,26 @@ __device__ __forceinline__ void mma16816<__half>(float* c, const uint32_t* a, ui
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Two floats -> one packed pair of 16-bit values in a single conversion instruction.
 template <typename T>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  T a = from_f<T>(lo), b = from_f<T>(hi);
-  return (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Hardware base-2 exponential (ex2.approx.ftz: ~2 ulp), ample for probabilities that are
+// rounded to 16 bits before the P.V product.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 struct WinPos {
@@ -108,17 +124,33 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
 }
 
+// Grid-token index and region label of every window position (the only place with
+// integer division).  Returns, to every thread, whether the window mixes two regions
+// (only then does the -100 mask apply anywhere in it).
+__device__ __forceinline__ bool fill_tokens(int* sTok, signed char* sLab, const AttnGeom& g, const WinPos& p,
+                                            int L, int rows_pad) {
+  const int lab0 = win_label(g, p, 0);
+  int mixed = 0;
+  for (int i = threadIdx.x; i < rows_pad; i += blockDim.x) {
+    sTok[i] = i < L ? (int)win_token(g, p, i) : 0;
+    const int lab = i < L ? win_label(g, p, i) : -1;
+    sLab[i] = (signed char)lab;
+    mixed |= (i < L && lab != lab0);
+  }
+  return __syncthreads_or(mixed) != 0;
+}
+
 // Issue asynchronous 16-byte copies of rows [0, L) of one of q/k/v/dO into smem (row
 // stride HD+8) and zero rows [L, rows_pad); completion is awaited by cp_async_wait_all.
 template <typename T, int HD>
 __device__ __forceinline__ void load_rows(T* s, const T* base, int64_t stride, int64_t col0,
-                                          const AttnGeom& g, const WinPos& p, int L, int rows_pad) {
+                                          const int* sTok, int L, int rows_pad) {
   constexpr int CH = HD / 8;
   for (int idx = threadIdx.x; idx < rows_pad * CH; idx += blockDim.x) {
     const int i = idx / CH, c = idx - i * CH;
     T* dst = s + i * (HD + 8) + c * 8;
     if (i < L) {
-      const int64_t tok = win_token(g, p, i);
+      const int64_t tok = sTok[i];
       cp_async16(dst, base + tok * stride + col0 + c * 8);
     } else {
       *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
@@ -168,15 +200,16 @@ __global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, 
   T* sQ = reinterpret_cast<T*>(smem);
   T* sK = sQ + lq * RS;
   T* sV = sK + lk * RS;
-  signed char* sLab = reinterpret_cast<signed char*>(sV + lk * RS);
+  int* sTok = reinterpret_cast<int*>(sV + lk * RS);
+  signed char* sLab = reinterpret_cast<signed char*>(sTok + lk);
 
   const int bw = blockIdx.x, h = blockIdx.y;
   const WinPos p = win_pos(g, bw);
   const int64_t C = (int64_t)g.nh * HD;
-  load_rows<T, HD>(sQ, qkv, g.qkv_stride, 0 * C + (int64_t)h * HD, g, p, L, lq);
-  load_rows<T, HD>(sK, qkv, g.qkv_stride, 1 * C + (int64_t)h * HD, g, p, L, lk);
-  load_rows<T, HD>(sV, qkv, g.qkv_stride, 2 * C + (int64_t)h * HD, g, p, L, lk);
-  for (int i = threadIdx.x; i < lk; i += blockDim.x) sLab[i] = i < L ? (signed char)win_label(g, p, i) : (signed char)-1;
+  const bool mixed = fill_tokens(sTok, sLab, g, p, L, lk);
+  load_rows<T, HD>(sQ, qkv, g.qkv_stride, 0 * C + (int64_t)h * HD, sTok, L, lq);
+  load_rows<T, HD>(sK, qkv, g.qkv_stride, 1 * C + (int64_t)h * HD, sTok, L, lk);
+  load_rows<T, HD>(sV, qkv, g.qkv_stride, 2 * C + (int64_t)h * HD, sTok, L, lk);
   cp_async_wait_all();
   __syncthreads();
   norm_rows<T, HD>(sQ, qw, L, nullptr);
@@ -221,24 +254,38 @@ __global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, 
         }
       }
       float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (!mixed && kc + 64 <= L) {
+        // no mask and no padding in this chunk (the common case)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 8; ++j) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int col = kc + j * 8 + 2 * tq + e;
-          const int lc = sLab[col];
-          float v0 = s[j][e] * sl2, v1 = s[j][2 + e] * sl2;
-          if (lc < 0) {
-            v0 = -INFINITY;
-            v1 = -INFINITY;
-          } else {
-            if (lc != lab0) v0 += ml2;
-            if (lc != lab1) v1 += ml2;
+          for (int e = 0; e < 2; ++e) {
+            s[j][e] *= sl2;
+            s[j][2 + e] *= sl2;
+            mx0 = fmaxf(mx0, s[j][e]);
+            mx1 = fmaxf(mx1, s[j][2 + e]);
           }
-          s[j][e] = v0;
-          s[j][2 + e] = v1;
-          mx0 = fmaxf(mx0, v0);
-          mx1 = fmaxf(mx1, v1);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = kc + j * 8 + 2 * tq + e;
+            const int lc = sLab[col];
+            float v0 = s[j][e] * sl2, v1 = s[j][2 + e] * sl2;
+            if (lc < 0) {
+              v0 = -INFINITY;
+              v1 = -INFINITY;
+            } else {
+              if (lc != lab0) v0 += ml2;
+              if (lc != lab1) v1 += ml2;
+            }
+            s[j][e] = v0;
+            s[j][2 + e] = v1;
+            mx0 = fmaxf(mx0, v0);
+            mx1 = fmaxf(mx1, v1);
+          }
         }
       }
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -246,7 +293,7 @@ __global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, 
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
       const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+      const float c0 = fast_exp2(m0 - mn0), c1 = fast_exp2(m1 - mn1);
       m0 = mn0;
       m1 = mn1;
       l0 *= c0;
@@ -260,10 +307,10 @@ __global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, 
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        s[j][0] = exp2f(s[j][0] - mn0);
-        s[j][1] = exp2f(s[j][1] - mn0);
-        s[j][2] = exp2f(s[j][2] - mn1);
-        s[j][3] = exp2f(s[j][3] - mn1);
+        s[j][0] = fast_exp2(s[j][0] - mn0);
+        s[j][1] = fast_exp2(s[j][1] - mn0);
+        s[j][2] = fast_exp2(s[j][2] - mn1);
+        s[j][3] = fast_exp2(s[j][3] - mn1);
         l0 += s[j][0] + s[j][1];
         l1 += s[j][2] + s[j][3];
       }
@@ -308,7 +355,7 @@ __global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, 
       const int rr = idx / DT, cc = idx - rr * DT;
       const int i = qt * 16 + rr;
       if (i < L) {
-        const int64_t tok = win_token(g, p, i);
+        const int64_t tok = sTok[i];
         *reinterpret_cast<uint4*>(out + tok * g.out_stride + (int64_t)h * HD + cc * 8) =
             *reinterpret_cast<const uint4*>(sQ + i * RS + cc * 8);
       }
@@ -320,8 +367,8 @@ __global__ void __launch_bounds__(256, 2) fwd_kernel(const T* __restrict__ qkv, 
 template <typename T, int HD>
 __device__ __forceinline__ void norm_backward_store(
     float (*acc)[4], int row0, int lane, const T* __restrict__ raw_base, int64_t stride,
-    int64_t col0, const float* __restrict__ w, const float* s_rstd, const AttnGeom& g,
-    const WinPos& p, int L, T* __restrict__ dst, float* wacc) {
+    int64_t col0, const float* __restrict__ w, const float* s_rstd, const int* sTok, int L,
+    T* __restrict__ dst, float* wacc) {
   // acc: gradient w.r.t. the normed rows (16 rows x HD) in mma C layout.
   constexpr int DT = HD / 8;
   const int gq = lane >> 2, tq = lane & 3;
@@ -330,7 +377,7 @@ __device__ __forceinline__ void norm_backward_store(
   for (int half = 0; half < 2; ++half) {
     const int i = rows[half];
     const bool valid = i < L;
-    const int64_t tok = valid ? win_token(g, p, i) : 0;
+    const int64_t tok = valid ? sTok[i] : 0;
     const float rs = valid ? s_rstd[i] : 0.f;
     float xr[DT][2];
     float dot = 0.f;
@@ -367,15 +414,14 @@ __device__ __forceinline__ void norm_backward_store(
 
 template <typename T, int HD>
 __device__ __forceinline__ void store_rows_c(float (*acc)[4], int row0, int lane, int64_t stride,
-                                             int64_t col0, const AttnGeom& g, const WinPos& p, int L,
-                                             T* __restrict__ dst) {
+                                             int64_t col0, const int* sTok, int L, T* __restrict__ dst) {
   constexpr int DT = HD / 8;
   const int gq = lane >> 2, tq = lane & 3;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int i = row0 + gq + 8 * half;
     if (i >= L) continue;
-    const int64_t tok = win_token(g, p, i);
+    const int64_t tok = sTok[i];
 #pragma unroll
     for (int d = 0; d < DT; ++d) {
       const int c = d * 8 + 2 * tq;
@@ -408,20 +454,19 @@ __global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, 
   float* sRk = sRq + lp;
   float* sWq = sRk + lp;  // [HD] partial dqw
   float* sWk = sWq + HD;  // [HD] partial dkw
-  signed char* sLab = reinterpret_cast<signed char*>(sWk + HD);
+  int* sTok = reinterpret_cast<int*>(sWk + HD);
+  signed char* sLab = reinterpret_cast<signed char*>(sTok + lp);
 
   const int bw = blockIdx.x, h = blockIdx.y;
   const WinPos p = win_pos(g, bw);
   const int64_t C = (int64_t)g.nh * HD;
-  load_rows<T, HD>(sQ, qkv, g.qkv_stride, 0 * C + (int64_t)h * HD, g, p, L, lp);
-  load_rows<T, HD>(sK, qkv, g.qkv_stride, 1 * C + (int64_t)h * HD, g, p, L, lp);
-  load_rows<T, HD>(sV, qkv, g.qkv_stride, 2 * C + (int64_t)h * HD, g, p, L, lp);
-  load_rows<T, HD>(sG, dout, g.out_stride, (int64_t)h * HD, g, p, L, lp);
+  const bool mixed = fill_tokens(sTok, sLab, g, p, L, lp);
+  load_rows<T, HD>(sQ, qkv, g.qkv_stride, 0 * C + (int64_t)h * HD, sTok, L, lp);
+  load_rows<T, HD>(sK, qkv, g.qkv_stride, 1 * C + (int64_t)h * HD, sTok, L, lp);
+  load_rows<T, HD>(sV, qkv, g.qkv_stride, 2 * C + (int64_t)h * HD, sTok, L, lp);
+  load_rows<T, HD>(sG, dout, g.out_stride, (int64_t)h * HD, sTok, L, lp);
   const int64_t lse_base = ((int64_t)bw * g.nh + h) * L;
-  for (int i = threadIdx.x; i < lp; i += blockDim.x) {
-    sLab[i] = i < L ? (signed char)win_label(g, p, i) : (signed char)-1;
-    sLse[i] = i < L ? lse[lse_base + i] : INFINITY;
-  }
+  for (int i = threadIdx.x; i < lp; i += blockDim.x) sLse[i] = i < L ? lse[lse_base + i] : INFINITY;
   for (int i = threadIdx.x; i < HD; i += blockDim.x) {
     sWq[i] = 0.f;
     sWk[i] = 0.f;
@@ -431,7 +476,7 @@ __global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, 
     for (int i = warp; i < lp; i += nw) {
       float acc = 0.f;
       if (i < L) {
-        const int64_t tok = win_token(g, p, i);
+        const int64_t tok = sTok[i];
         for (int c = lane; c < HD; c += 32)
           acc += to_f(dout[tok * g.out_stride + (int64_t)h * HD + c]) *
                  to_f(out[tok * g.out_stride + (int64_t)h * HD + c]);
@@ -492,21 +537,28 @@ __global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, 
           mma16816<T>(dpt[1], va[ks], b2, b3);
         }
         // P^T and dS^T (rows = keys, cols = queries)
+        const bool plain = !mixed && qc + 16 <= L && kt * 16 + 16 <= L;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int q = qc + j * 8 + 2 * tq + e;
-            const int ql = sLab[q];
             const float lq = sLse[q];
             const float dq = sD[q];
             float v0 = st[j][e] * sl2, v1 = st[j][2 + e] * sl2;
-            if (ql >= 0) {
-              if (klab0 != ql) v0 += ml2;
-              if (klab1 != ql) v1 += ml2;
+            float p0, p1;
+            if (plain) {
+              p0 = fast_exp2(v0 - lq);
+              p1 = fast_exp2(v1 - lq);
+            } else {
+              const int ql = sLab[q];
+              if (ql >= 0) {
+                if (klab0 != ql) v0 += ml2;
+                if (klab1 != ql) v1 += ml2;
+              }
+              p0 = (klab0 < 0) ? 0.f : fast_exp2(v0 - lq);
+              p1 = (klab1 < 0) ? 0.f : fast_exp2(v1 - lq);
             }
-            const float p0 = (klab0 < 0) ? 0.f : exp2f(v0 - lq);
-            const float p1 = (klab1 < 0) ? 0.f : exp2f(v1 - lq);
             st[j][e] = p0;
             st[j][2 + e] = p1;
             dpt[j][e] = p0 * (dpt[j][e] - dq);
@@ -539,9 +591,9 @@ __global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, 
       for (int d = 0; d < DT; ++d)
 #pragma unroll
         for (int e = 0; e < 4; ++e) dk[d][e] *= g.scale;
-      store_rows_c<T, HD>(dv, kt * 16, lane, g.qkv_stride, 2 * C + (int64_t)h * HD, g, p, L, dqkv);
+      store_rows_c<T, HD>(dv, kt * 16, lane, g.qkv_stride, 2 * C + (int64_t)h * HD, sTok, L, dqkv);
       norm_backward_store<T, HD>(dk, kt * 16, lane, qkv, g.qkv_stride, 1 * C + (int64_t)h * HD, kw,
-                                 sRk, g, p, L, dqkv, wk);
+                                 sRk, sTok, L, dqkv, wk);
     } else {
       // ---------------- phase B: 16 queries -> dQ
       const int qt = task - nt;
@@ -578,19 +630,25 @@ __global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, 
           mma16816<T>(dpm[0], ga[ks], b0, b1);
           mma16816<T>(dpm[1], ga[ks], b2, b3);
         }
+        const bool plain = !mixed && kc + 16 <= L;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int k = kc + j * 8 + 2 * tq + e;
-            const int kl = sLab[k];
             float v0 = s[j][e] * sl2, v1 = s[j][2 + e] * sl2;
             float p0 = 0.f, p1 = 0.f;
-            if (kl >= 0) {
-              if (kl != (qlab0 < 0 ? 0 : qlab0)) v0 += ml2;
-              if (kl != (qlab1 < 0 ? 0 : qlab1)) v1 += ml2;
-              p0 = exp2f(v0 - lq0);
-              p1 = exp2f(v1 - lq1);
+            if (plain) {
+              p0 = fast_exp2(v0 - lq0);
+              p1 = fast_exp2(v1 - lq1);
+            } else {
+              const int k = kc + j * 8 + 2 * tq + e;
+              const int kl = sLab[k];
+              if (kl >= 0) {
+                if (kl != (qlab0 < 0 ? 0 : qlab0)) v0 += ml2;
+                if (kl != (qlab1 < 0 ? 0 : qlab1)) v1 += ml2;
+                p0 = fast_exp2(v0 - lq0);
+                p1 = fast_exp2(v1 - lq1);
+              }
             }
             s[j][e] = p0 * (dpm[j][e] - d0);
             s[j][2 + e] = p1 * (dpm[j][2 + e] - d1);
@@ -616,7 +674,7 @@ __global__ void __launch_bounds__(192, 2) bwd_kernel(const T* __restrict__ qkv, 
 #pragma unroll
         for (int e = 0; e < 4; ++e) dq[d][e] *= g.scale;
       norm_backward_store<T, HD>(dq, qt * 16, lane, qkv, g.qkv_stride, 0 * C + (int64_t)h * HD, qw,
-                                 sRq, g, p, L, dqkv, wq);
+                                 sRq, sTok, L, dqkv, wq);
     }
   }
   // reduce the norm-weight partials: over the 8 row groups of the warp, then the CTA
@@ -652,7 +710,7 @@ static cudaError_t launch_fwd(const void* qkv, const float* qw, const float* kw,
   const int L = g.T * g.wh * g.ww;
   const int nqt = (L + 15) / 16;
   const int lk = ((L + 63) / 64) * 64;
-  const size_t smem = (size_t)(nqt * 16 + 2 * lk) * (HD + 8) * sizeof(T) + lk;
+  const size_t smem = (size_t)(nqt * 16 + 2 * lk) * (HD + 8) * sizeof(T) + (size_t)lk * (sizeof(int) + 1);
   int nw = nqt < 8 ? nqt : 8;
   if (nw < 1) nw = 1;
   auto k = fwd_kernel<T, HD>;
@@ -670,7 +728,7 @@ static cudaError_t launch_bwd(const void* qkv, const float* qw, const float* kw,
   const int nt = (L + 15) / 16;
   const int lp = nt * 16;
   const size_t smem = (size_t)4 * lp * (HD + 8) * sizeof(T) + (size_t)4 * lp * sizeof(float) +
-                      2 * HD * sizeof(float) + lp;
+                      2 * HD * sizeof(float) + (size_t)lp * (sizeof(int) + 1);
   int nw = 2 * nt < 6 ? 2 * nt : 6;
   auto k = bwd_kernel<T, HD>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

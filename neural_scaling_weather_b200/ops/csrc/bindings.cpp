@@ -70,7 +70,7 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
   const int n = (int)x.size(-1);
   const int64_t rows = x.numel() / n;
   auto dx = torch::empty_like(x);
-  int parts = 2 * 148;
+  int parts = 3 * 148;
   if (rows < parts * 8) parts = (int)std::max<int64_t>(1, (rows + 7) / 8);
   auto part = torch::empty({parts, n}, x.options().dtype(at::kFloat));
   check(nsw::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(),
@@ -176,7 +176,8 @@ Tensor col_sum(Tensor x) {
   need_cuda(x, "x");
   const int n = (int)x.size(-1);
   const int64_t rows = x.numel() / n;
-  int parts = 4 * 148;
+  // partial rows: up to 8 blocks per SM for the vector path, 4 for the scalar one
+  int parts = (n % 8 == 0 && x.scalar_type() != at::kFloat) ? 8 * 148 : 4 * 148;
   if (rows < parts) parts = (int)std::max<int64_t>(1, rows);
   auto part = torch::empty({parts, n}, x.options().dtype(at::kFloat));
   auto out = torch::empty({n}, x.options().dtype(at::kFloat));

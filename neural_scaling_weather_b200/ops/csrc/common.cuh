@@ -65,7 +65,7 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Exact (erf-based) GELU, as torch.nn.GELU() with approximate='none'.
+// Exact (erf-based) GELU, as torch.nn.GELU() with approximate='none' (CUDA's erff).
 __device__ __forceinline__ float gelu_f(float u) {
   return 0.5f * u * (1.0f + erff(u * 0.70710678118654752440f));
 }
@@ -73,6 +73,38 @@ __device__ __forceinline__ float gelu_grad_f(float u) {
   const float cdf = 0.5f * (1.0f + erff(u * 0.70710678118654752440f));
   const float pdf = expf(-0.5f * u * u) * 0.39894228040143267794f;
   return cdf + u * pdf;
+}
+
+// Fast erf-based GELU for GEMM epilogues.  erf(z) for z >= 0 uses Abramowitz & Stegun,
+// Handbook of Mathematical Functions, eq. 7.1.26 (Hastings' rational approximation,
+// |error| <= 1.5e-7):  erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
+// t = 1 / (1 + p z); odd symmetry gives z < 0.  With z = u / sqrt(2), exp(-z^2) is also the
+// unnormalised normal density, so GELU'(u) = Phi(u) + u phi(u) reuses it.  Costs one
+// reciprocal and one exponential (hardware approximations) plus a few FMAs.
+struct GeluParts {
+  float cdf;  // Phi(u)
+  float pdf;  // phi(u)
+};
+__device__ __forceinline__ GeluParts gelu_parts_fast(float u) {
+  const float z = fabsf(u) * 0.70710678118654752440f;
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.0f)));
+  float e;  // exp(-z^2) = 2^(-z^2 * log2(e))
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.44269504088896340736f));
+  const float poly =
+      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f),
+               0.254829592f);
+  const float erf_abs = 1.0f - poly * e;
+  const float erf_z = u < 0.f ? -erf_abs : erf_abs;
+  GeluParts r;
+  r.cdf = 0.5f * (1.0f + erf_z);
+  r.pdf = e * 0.39894228040143267794f;
+  return r;
+}
+__device__ __forceinline__ float gelu_fast(float u) { return u * gelu_parts_fast(u).cdf; }
+__device__ __forceinline__ float gelu_grad_fast(float u) {
+  const GeluParts g = gelu_parts_fast(u);
+  return g.cdf + u * g.pdf;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -32,8 +32,9 @@ int* device_error_flag() {
 }
 
 // ============================================================================ RMSNorm
-// One warp per row; each lane owns columns [8*(lane + 32*j), +8).
-template <typename T>
+// One warp per row; lane owns columns [8*(lane + 32*j), +8) and keeps them in registers
+// between the sum of squares and the scaled store (one read, one write per element).
+template <typename T, int NCH>
 __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
                                    T* __restrict__ y, float* __restrict__ rstd, int64_t rows, int n,
                                    float eps) {
@@ -43,26 +44,33 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
        r += warps_total) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + r * n);
+    float f[NCH][8];
     float ss = 0.f;
-    for (int c = lane; c < nvec; c += 32) {
-      float f[8];
-      unpack8<T>(xr[c], f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    for (int j = 0; j < NCH; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nvec) {
+        unpack8<T>(xr[c], f[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += f[j][i] * f[j][i];
+      }
     }
     ss = warp_sum(ss);
     const float rs = rsqrtf(ss / (float)n + eps);
     if (lane == 0 && rstd) rstd[r] = rs;
     uint4* yr = reinterpret_cast<uint4*>(y + r * n);
-    for (int c = lane; c < nvec; c += 32) {
-      float f[8];
-      unpack8<T>(xr[c], f);
-      const float4 w0 = reinterpret_cast<const float4*>(w)[2 * c];
-      const float4 w1 = reinterpret_cast<const float4*>(w)[2 * c + 1];
-      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = f[i] * rs * ww[i];
-      yr[c] = pack8<T>(f);
+    for (int j = 0; j < NCH; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nvec) {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = f[j][i] * rs * ww[i];
+        yr[c] = pack8<T>(o);
+      }
     }
   }
 }
@@ -82,8 +90,16 @@ __global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict
   const int64_t warps_total = (int64_t)gridDim.x * nwarps;
   const int nvec = n >> 3;
   float acc[NCH * 8];
+  float wr[NCH][8];  // this lane's columns of w, constant across rows
 #pragma unroll
-  for (int i = 0; i < NCH * 8; ++i) acc[i] = 0.f;
+  for (int j = 0; j < NCH; ++j) {
+    const int c = lane + 32 * j;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[j * 8 + i] = 0.f;
+      wr[j][i] = c < nvec ? __ldg(w + 8 * c + i) : 0.f;
+    }
+  }
   for (int64_t r = (int64_t)blockIdx.x * nwarps + warp; r < rows; r += warps_total) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + r * n);
     const uint4* dyr = reinterpret_cast<const uint4*>(dy + r * n);
@@ -97,9 +113,10 @@ __global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict
         unpack8<T>(xr[c], fx[j]);
         unpack8<T>(dyr[c], fg[j]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dot += fg[j][i] * w[8 * c + i] * fx[j][i] * rs;
+        for (int i = 0; i < 8; ++i) dot += fg[j][i] * wr[j][i] * fx[j][i];
       }
     }
+    dot *= rs;
     dot = warp_sum(dot) / (float)n;
     uint4* dxr = reinterpret_cast<uint4*>(dx + r * n);
 #pragma unroll
@@ -110,7 +127,7 @@ __global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float xh = fx[j][i] * rs;
-          o[i] = rs * (fg[j][i] * w[8 * c + i] - xh * dot);
+          o[i] = rs * (fg[j][i] * wr[j][i] - xh * dot);
           acc[j * 8 + i] += fg[j][i] * xh;
         }
         dxr[c] = pack8<T>(o);
@@ -135,19 +152,24 @@ __global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict
 
 cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n,
                         float eps, int dtype, cudaStream_t s) {
-  if (n % 8) return cudaErrorInvalidValue;
+  if (n % 8 || n > 2048) return cudaErrorInvalidValue;
   const int threads = 256;
   int64_t blocks = (rows + 7) / 8;
   const int64_t cap = (int64_t)num_sms() * 16;
   if (blocks > cap) blocks = cap;
-  if (dtype == kBF16)
-    rmsnorm_fwd_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(
-        (const __nv_bfloat16*)x, w, (__nv_bfloat16*)y, rstd, rows, n, eps);
-  else if (dtype == kF16)
-    rmsnorm_fwd_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)x, w, (__half*)y, rstd,
-                                                           rows, n, eps);
-  else
-    return cudaErrorInvalidValue;
+  const int nch = (n / 8 + 31) / 32;
+#define NSW_RF(T, NCH) \
+  rmsnorm_fwd_kernel<T, NCH><<<blocks, threads, 0, s>>>((const T*)x, w, (T*)y, rstd, rows, n, eps)
+#define NSW_RF_N(T)                \
+  if (nch <= 1) NSW_RF(T, 1);      \
+  else if (nch <= 2) NSW_RF(T, 2); \
+  else if (nch <= 4) NSW_RF(T, 4); \
+  else NSW_RF(T, 8);
+  if (dtype == kBF16) { NSW_RF_N(__nv_bfloat16) }
+  else if (dtype == kF16) { NSW_RF_N(__half) }
+  else return cudaErrorInvalidValue;
+#undef NSW_RF_N
+#undef NSW_RF
   return cudaGetLastError();
 }
 
@@ -250,8 +272,43 @@ cudaError_t gelu_bwd(const void* dy, const void* u, void* du, int64_t n, int dty
   return cudaGetLastError();
 }
 
-// column sums: block b sums rows [b*chunk, (b+1)*chunk) into partial[b, :]; then one block
-// per column group sums the partials in order.
+// Column sums of [rows, n] (n % 8 == 0 for the vector path): thread owns 8 adjacent
+// columns and walks a chunk of rows with 4 independent accumulators (loads in flight);
+// block (x = column group, y = row chunk) writes partial[y, :], then one pass sums the
+// partial rows in order (deterministic).
+template <typename T>
+__global__ void col_sum_vec_kernel(const T* __restrict__ x, float* __restrict__ partial, int64_t rows, int n,
+                                   int64_t chunk) {
+  const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c8 >= n) return;
+  const int64_t r0 = (int64_t)blockIdx.y * chunk;
+  const int64_t r1 = min(rows, r0 + chunk);
+  float a[4][8];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[u][k] = 0.f;
+  int64_t r = r0;
+  for (; r + 4 <= r1; r += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float f[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(x + (r + u) * n + c8), f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[u][k] += f[k];
+    }
+  }
+  for (; r < r1; ++r) {
+    float f[8];
+    unpack8<T>(*reinterpret_cast<const uint4*>(x + r * n + c8), f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[0][k] += f[k];
+  }
+  float* out = partial + (int64_t)blockIdx.y * n + c8;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) out[k] = (a[0][k] + a[1][k]) + (a[2][k] + a[3][k]);
+}
+
 template <typename T>
 __global__ void col_sum_partial_kernel(const T* __restrict__ x, float* __restrict__ partial,
                                        int64_t rows, int n, int64_t chunk) {
@@ -263,17 +320,44 @@ __global__ void col_sum_partial_kernel(const T* __restrict__ x, float* __restric
     partial[(int64_t)blockIdx.x * n + c] = acc;
   }
 }
+// Sum of the partial rows: a block owns 32 columns; its 8 warps take interleaved
+// partial rows (coalesced 128-byte reads), then combine in shared memory (fixed order).
 __global__ void col_sum_final_kernel(const float* __restrict__ partial, float* __restrict__ out,
                                      int parts, int n) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= n) return;
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
   float acc = 0.f;
-  for (int p = 0; p < parts; ++p) acc += partial[(int64_t)p * n + c];
-  out[c] = acc;
+  if (c < n)
+    for (int p = warp; p < parts; p += 8) acc += partial[(int64_t)p * n + c];
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < n) {
+    float v = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v += red[k][lane];
+    out[c] = v;
+  }
 }
 
 cudaError_t col_sum(const void* x, float* out, float* partial, int partial_rows, int64_t rows, int n,
                     int dtype, cudaStream_t s) {
+  if (n % 8 == 0 && dtype != kF32) {
+    const int threads = n / 8 < 128 ? ((n / 8 + 31) / 32) * 32 : 128;
+    const int gx = (n / 8 + threads - 1) / threads;
+    int gy = partial_rows / gx;
+    if (gy < 1) gy = 1;
+    if (gy > rows) gy = (int)rows;
+    const int64_t chunk = (rows + gy - 1) / gy;
+    gy = (int)((rows + chunk - 1) / chunk);
+    dim3 grid(gx, gy);
+    if (dtype == kBF16)
+      col_sum_vec_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>((const __nv_bfloat16*)x, partial, rows, n, chunk);
+    else
+      col_sum_vec_kernel<__half><<<grid, threads, 0, s>>>((const __half*)x, partial, rows, n, chunk);
+    col_sum_final_kernel<<<(n + 31) / 32, 256, 0, s>>>(partial, out, gy, n);
+    return cudaGetLastError();
+  }
   const int64_t chunk = (rows + partial_rows - 1) / partial_rows;
   const int threads = n < 256 ? ((n + 31) / 32) * 32 : 256;
   if (dtype == kBF16)
@@ -287,7 +371,7 @@ cudaError_t col_sum(const void* x, float* out, float* partial, int partial_rows,
                                                                     chunk);
   else
     return cudaErrorInvalidValue;
-  col_sum_final_kernel<<<(n + 255) / 256, 256, 0, s>>>(partial, out, partial_rows, n);
+  col_sum_final_kernel<<<(n + 31) / 32, 256, 0, s>>>(partial, out, partial_rows, n);
   return cudaGetLastError();
 }
 
@@ -533,6 +617,88 @@ __global__ void se_plane_kernel(const TX* __restrict__ x, const TY* __restrict__
   }
 }
 
+// Plane-structured variants (W % 8 == 0): block (x = row chunk, y = plane); the channel
+// weight is constant per block and rows are walked with 8-element vector accesses.
+template <typename T>
+__device__ __forceinline__ void load8f(const T* p, float* f);
+template <>
+__device__ __forceinline__ void load8f<float>(const float* p, float* f) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8f<__nv_bfloat16>(const __nv_bfloat16* p, float* f) {
+  unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(p), f);
+}
+template <>
+__device__ __forceinline__ void load8f<__half>(const __half* p, float* f) {
+  unpack8<__half>(*reinterpret_cast<const uint4*>(p), f);
+}
+template <typename T>
+__device__ __forceinline__ void store8f(T* p, const float* f);
+template <>
+__device__ __forceinline__ void store8f<float>(float* p, const float* f) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+template <>
+__device__ __forceinline__ void store8f<__nv_bfloat16>(__nv_bfloat16* p, const float* f) {
+  *reinterpret_cast<uint4*>(p) = pack8<__nv_bfloat16>(f);
+}
+template <>
+__device__ __forceinline__ void store8f<__half>(__half* p, const float* f) {
+  *reinterpret_cast<uint4*>(p) = pack8<__half>(f);
+}
+
+template <typename TX, typename TY, bool BWD>
+__global__ void sse_plane_kernel(const TX* __restrict__ x, const TY* __restrict__ y,
+                                 const float* __restrict__ aw, const float* __restrict__ cw,
+                                 const float* __restrict__ gscale, TX* __restrict__ dx,
+                                 float* __restrict__ partial, int C, int H, int W, int rows_per_block) {
+  const int plane = blockIdx.y;
+  const int c = plane % C;
+  const float wc = cw ? cw[c] : 1.f;
+  const int64_t base = (int64_t)plane * H * W;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(H, r0 + rows_per_block);
+  const int wv = W >> 3;
+  const float g2 = BWD ? 2.f * gscale[0] * wc : 0.f;
+  float acc = 0.f;
+  for (int idx = threadIdx.x; idx < (r1 - r0) * wv; idx += blockDim.x) {
+    const int rr = r0 + idx / wv;
+    const int64_t off = base + (int64_t)rr * W + (int64_t)(idx % wv) * 8;
+    float fx[8], fy[8];
+    load8f<TX>(x + off, fx);
+    load8f<TY>(y + off, fy);
+    const float wr = aw ? aw[rr] : 1.f;
+    if (BWD) {
+      float o[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = g2 * wr * (fx[k] - fy[k]);
+      store8f<TX>(dx + off, o);
+    } else {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float d = fx[k] - fy[k];
+        t += d * d;
+      }
+      acc += wr * t;
+    }
+  }
+  if (BWD) return;
+  acc *= wc;
+  acc = warp_sum(acc);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) partial[(int64_t)blockIdx.y * gridDim.x + blockIdx.x] = v;
+  }
+}
+
 #define NSW_DISPATCH_XY(XD, YD, MACRO)                                                 \
   if ((XD) == kBF16 && (YD) == kF32) { MACRO(__nv_bfloat16, float); }                  \
   else if ((XD) == kBF16 && (YD) == kBF16) { MACRO(__nv_bfloat16, __nv_bfloat16); }    \
@@ -541,10 +707,30 @@ __global__ void se_plane_kernel(const TX* __restrict__ x, const TY* __restrict__
   else if ((XD) == kF32 && (YD) == kF32) { MACRO(float, float); }                      \
   else return cudaErrorInvalidValue;
 
+static int sse_rows_per_block(int H, int64_t planes, int partial_n) {
+  // enough blocks to fill the GPU while keeping planes * blocks_per_plane <= partial_n
+  int64_t per_plane = partial_n / (planes > 0 ? planes : 1);
+  if (per_plane < 1) per_plane = 1;
+  int rpb = (int)((H + per_plane - 1) / per_plane);
+  return rpb < 1 ? 1 : rpb;
+}
+
 cudaError_t weighted_sse(const void* x, int x_dtype, const void* y, int y_dtype, const float* area_w,
                          const float* ch_w, float* partial, int partial_n, float* out, int64_t lead,
                          int C, int H, int W, cudaStream_t s) {
   const int64_t total = lead * C * (int64_t)H * W;
+  const int64_t planes = lead * C;
+  if (W % 8 == 0 && planes <= 65535 && planes <= partial_n) {
+    const int rpb = sse_rows_per_block(H, planes, partial_n);
+    dim3 grid((H + rpb - 1) / rpb, (unsigned)planes);
+#define NSW_SSEP(TX, TY)                                                                               \
+  sse_plane_kernel<TX, TY, false><<<grid, 256, 0, s>>>((const TX*)x, (const TY*)y, area_w, ch_w, nullptr, \
+                                                       nullptr, partial, C, H, W, rpb)
+    NSW_DISPATCH_XY(x_dtype, y_dtype, NSW_SSEP)
+#undef NSW_SSEP
+    sum_partials_kernel<<<1, 1024, 0, s>>>(partial, (int)(grid.x * grid.y), out);
+    return cudaGetLastError();
+  }
 #define NSW_SSE(TX, TY)                                                                         \
   sse_partial_kernel<TX, TY><<<partial_n, 256, 0, s>>>((const TX*)x, (const TY*)y, area_w, ch_w, \
                                                        partial, total, C, H, W)
@@ -558,6 +744,17 @@ cudaError_t weighted_sse_bwd(const void* x, int x_dtype, const void* y, int y_dt
                              const float* area_w, const float* ch_w, const float* gscale, void* dx,
                              int64_t lead, int C, int H, int W, cudaStream_t s) {
   const int64_t total = lead * C * (int64_t)H * W;
+  const int64_t planes = lead * C;
+  if (W % 8 == 0 && planes <= 65535) {
+    const int rpb = sse_rows_per_block(H, planes, 4 * num_sms());
+    dim3 grid((H + rpb - 1) / rpb, (unsigned)planes);
+#define NSW_SSEPB(TX, TY)                                                                              \
+  sse_plane_kernel<TX, TY, true><<<grid, 256, 0, s>>>((const TX*)x, (const TY*)y, area_w, ch_w, gscale, \
+                                                      (TX*)dx, nullptr, C, H, W, rpb)
+    NSW_DISPATCH_XY(x_dtype, y_dtype, NSW_SSEPB)
+#undef NSW_SSEPB
+    return cudaGetLastError();
+  }
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 32;
   if (blocks > cap) blocks = cap;

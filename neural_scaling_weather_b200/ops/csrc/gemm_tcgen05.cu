@@ -2,6 +2,7 @@
 //
 //   D[m, n] = epilogue( alpha * sum_k A[m, k] * B[n, k] )
 //   epilogue: (+ bias[n]) -> (store pre-activation) -> (GELU) -> (+ residual[m % P, n])
+//             or, with act == 2, (* GELU'(aux[m, n])) for the MLP backward (aux in `residual`)
 //             -> bf16/fp16 store, or fp32 store / fp32 accumulate (D += ...)
 //
 // A [M, K] and B [N, K] are K-major (row-major with K contiguous), bf16 or fp16.
@@ -269,16 +270,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
-      tc_fence_after();
       const int64_t m0 = (tile / n_tiles) * BM;
       const int64_t n0 = (tile % n_tiles) * BN;
       const int64_t row_base = m0 + q * 32;
       const int64_t row = row_base + lane;
       const bool row_ok = row < ep.M;
+      // Prefetch this warp's residual/aux strip (32 rows x BN/2 columns) into registers in
+      // the coalesced layout (lane -> row sub_r + 8 i, 8-column group sub_c) BEFORE waiting
+      // for the accumulator, so the global latency hides behind this tile's MMAs.
+      constexpr int kChunks = BN / 64;
+      const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
+      uint4 pre_res[kChunks][4];
+      const bool res_vec = ep.residual != nullptr && !ep.out_f32;
+      if (res_vec) {
+#pragma unroll
+        for (int cc = 0; cc < kChunks; ++cc) {
+          const int64_t nbp = n0 + (half * kChunks + cc) * 32;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int64_t rr = row_base + sub_r + 8 * i;
+            pre_res[cc][i] = make_uint4(0, 0, 0, 0);
+            if (rr < ep.M && nbp + 32 <= ep.N)
+              pre_res[cc][i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                              (rr % ep.res_period) * ep.ldr + nbp + sub_c);
+          }
+        }
+      }
+      if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
+      tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+#pragma unroll
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = half * kChunks + cc;
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
         const int64_t nb = n0 + c * 32;
@@ -311,11 +334,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (ep.act == 1) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) f[j] = gelu_f(f[j]);
+              for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
             }
             if (ep.residual) {
               const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
-              for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
+              if (ep.act == 2) {
+                for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] *= gelu_grad_fast(to_f(rp[j]));
+              } else {
+                for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
+              }
             }
             if (ep.out_f32) {
               float* dp = reinterpret_cast<float*>(ep.D) + row * ep.ldd + nb;
@@ -344,7 +371,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ---- full 32-column chunk, 16-bit output: staged, coalesced
         // lane l moves 16 bytes of row (l / 4 + 8 i), 8-column group (l % 4)
-        const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
         if (ep.preact) {
 #pragma unroll
           for (int v = 0; v < 4; ++v)
@@ -361,25 +387,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ep.act == 1) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = gelu_f(f[j]);
+          for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
         }
         if (ep.residual) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int rr = sub_r + 8 * i;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (row_base + rr < ep.M)
-              v = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
-                                                  ((row_base + rr) % ep.res_period) * ep.ldr + nb + sub_c);
-            *reinterpret_cast<uint4*>(stg + rr * kStageRow + sub_c) = v;
-          }
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint4*>(stg + (sub_r + 8 * i) * kStageRow + sub_c) = pre_res[cc][i];
           __syncwarp();
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             float rr8[8];
             unpack8<T>(*reinterpret_cast<const uint4*>(stg + lane * kStageRow + 8 * v), rr8);
+            if (ep.act == 2) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
+              for (int j = 0; j < 8; ++j) f[8 * v + j] *= gelu_grad_fast(rr8[j]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
+            }
           }
           __syncwarp();
         }

@@ -169,6 +169,63 @@ def linear_cuda(x, weight, bias=None, residual=None, activation=None):
     return _Linear.apply(x, residual, act, len(ws), len(bs), *ws, *bs)
 
 
+# ---------------------------------------------------------------------------- MLP
+class _MLP(torch.autograd.Function):
+    """fc1 + bias + GELU -> fc2 + bias (+ residual) with a fused backward.
+
+    Forward: two tcgen05 GEMMs (the first saves the pre-activation u and the GELU output h).
+    Backward: du = (dy @ W2) * GELU'(u) in ONE GEMM epilogue (no separate GELU-backward pass),
+    dx = du @ W1; weight gradients by cuBLAS with fp32 output.
+    """
+
+    @staticmethod
+    def forward(ctx, x, residual, w1, b1, w2, b2):
+        ext = require()
+        dt = _cdtype(x)
+        K = x.shape[-1]
+        x2 = x.reshape(-1, K).to(dt)
+        W1 = wcache.get(w1, dt)
+        W2 = wcache.get(w2, dt)
+        N = W2.shape[0]
+        H = W1.shape[0]
+        needs_grad = any(ctx.needs_input_grad)
+        u = torch.empty(x2.shape[0], H, dtype=dt, device=x.device) if needs_grad else None
+        h = gemm(x2, W1, b1.detach().float(), None, 0, 1, u)
+        res2 = residual.reshape(-1, N).to(dt).contiguous() if residual is not None else None
+        y = gemm(h, W2, b2.detach().float(), res2)
+        ctx.save_for_backward(x2, u, h)
+        ctx.w1, ctx.w2, ctx.W1, ctx.W2 = w1, w2, W1, W2
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        ctx.res_dtype = residual.dtype if residual is not None else None
+        return y.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        ext = require()
+        x2, u, h = ctx.saved_tensors
+        N = ctx.W2.shape[0]
+        dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
+        dW2 = wgrad(dy2, h)
+        db2 = ext.col_sum(dy2)
+        W2t = _weight_t([ctx.w2], ctx.W2)
+        if ext.gemm_supported(dy2, W2t, False):
+            du = ext.gemm(dy2, W2t, None, u, 0, 2)  # epilogue: * GELU'(u)
+        else:
+            du = ext.gelu_bwd(gemm(dy2, W2t).contiguous(), u)
+        dW1 = wgrad(du, x2)
+        db1 = ext.col_sum(du)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            W1t = _weight_t([ctx.w1], ctx.W1)
+            dx = gemm(du, W1t).view(ctx.x_shape).to(ctx.x_dtype)
+        dres = dy.to(ctx.res_dtype) if ctx.res_dtype is not None else None
+        return dx, dres, dW1, db1, dW2, db2
+
+
+def mlp_cuda(x, w1, b1, w2, b2, residual=None):
+    return _MLP.apply(x, residual, w1, b1, w2, b2)
+
+
 # ---------------------------------------------------------------------------- attention
 def _geom_ints(B, T, H, W, nh, hd, g: WindowGeometry):
     return [B, T, H, W, nh, hd, g.window[0], g.window[1], g.shift[0], g.shift[1], int(g.mask),

@@ -246,3 +246,30 @@ def test_sharded_norm_kernel():
     n = ShardedNorm(space).norm("grad")
     ref = torch.sqrt(sum((p.grad.double() ** 2).sum() for p in ps))
     assert abs(n.item() - ref.item()) / ref.item() < 1e-5
+
+
+# --------------------------------------------------------------------------- fused MLP
+@pytest.mark.parametrize("residual", [False, True])
+def test_fused_mlp(residual):
+    torch.manual_seed(0)
+    x = torch.randn(3, 100, 64, device=DEV).bfloat16().requires_grad_()
+    w1 = (0.05 * torch.randn(256, 64, device=DEV)).requires_grad_()
+    b1 = (0.1 * torch.randn(256, device=DEV)).requires_grad_()
+    w2 = (0.05 * torch.randn(64, 256, device=DEV)).requires_grad_()
+    b2 = (0.1 * torch.randn(64, device=DEV)).requires_grad_()
+    res = torch.randn(3, 100, 64, device=DEV).bfloat16().requires_grad_() if residual else None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = ops.mlp(x, w1, b1, w2, b2, res)
+    xr = x.detach().float().requires_grad_()
+    ps = [t.detach().clone().requires_grad_() for t in (w1, b1, w2, b2)]
+    rr = res.detach().float().requires_grad_() if residual else None
+    yr = reference.linear(reference.linear(xr, ps[0], ps[1], activation="gelu"), ps[2], ps[3], residual=rr)
+    assert rel(y, yr) < 2e-2
+    g = torch.randn_like(yr)
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    assert rel(x.grad, xr.grad) < 3e-2
+    for a, b in zip((w1, b1, w2, b2), ps):
+        assert rel(a.grad, b.grad) < 3e-2
+    if residual:
+        assert rel(res.grad, rr.grad) < 1e-2
