@@ -371,6 +371,10 @@ def reference(args, rank, world, local):
 
     fake = _T()
     fake.device = device
+    if tr_cls is not None:
+        import types
+
+        fake.get_norm = types.MethodType(tr_cls.get_norm, fake)
     _, batches, inv = make_batches(2, "cuda")
     from contextlib import nullcontext
 
