@@ -131,8 +131,9 @@ def bench_attention(a):
     tokens = B * H * W
     L = 162
     flops = 4.0 * tokens * L * hd * nh  # QK^T and PV
-    ms = timeit(lambda: ext.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5), a.iters)
-    report(f"window_attn_fwd tokens={tokens} heads={nh}", ms, flops, 2 * tokens * 4 * C)
+    for impl, tag in ((1, "mma.sync"), (2, "tcgen05")):
+        ms = timeit(lambda: ext.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, impl), a.iters)
+        report(f"window_attn_fwd[{tag}] tokens={tokens} heads={nh}", ms, flops, 2 * tokens * 4 * C)
     dout = torch.randn_like(out)
     ms = timeit(lambda: ext.window_attn_bwd(qkv.view(-1, 3 * C), qw, kw, out, dout, lse, gi, hd ** -0.5),
                 a.iters)

@@ -317,7 +317,8 @@ nsw::AttnGeom make_geom(const std::vector<int64_t>& gi, double scale) {
   return g;
 }
 
-std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vector<int64_t> gi, double scale) {
+std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vector<int64_t> gi, double scale,
+                                    int64_t impl) {
   need_cuda(qkv, "qkv");
   auto g = make_geom(gi, scale);
   const int64_t tokens = (int64_t)g.B * g.T * g.H * g.W;
@@ -326,9 +327,18 @@ std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vecto
   const int L = g.T * g.wh * g.ww;
   const int64_t nwin = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww);
   auto lse = torch::empty({nwin * g.nh * L}, qkv.options().dtype(at::kFloat));
-  check(nsw::window_attn_fwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
-                             lse.data_ptr<float>(), g, dt_code(qkv), stream()),
-        "window_attn_fwd");
+  // impl: 0 = default (mma.sync: faster than the one-window-per-CTA tcgen05 kernel at the
+  // production shape), 1 = mma.sync, 2 = tcgen05/TMEM
+  const bool tc_ok = nsw::window_attn_fwd_tc_supported(g, dt_code(qkv));
+  TORCH_CHECK(impl != 2 || tc_ok, "window_attn_fwd: tcgen05 path needs bf16, head_dim 64, window <= 176 tokens");
+  if (tc_ok && impl == 2)
+    check(nsw::window_attn_fwd_tc(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                                  lse.data_ptr<float>(), g, stream()),
+          "window_attn_fwd_tc");
+  else
+    check(nsw::window_attn_fwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                               lse.data_ptr<float>(), g, dt_code(qkv), stream()),
+          "window_attn_fwd");
   return {out, lse};
 }
 
@@ -371,6 +381,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("weighted_se_per_plane", &weighted_se_per_plane);
   m.def("adamw_step", &adamw_step);
   m.def("segment_sumsq", &segment_sumsq);
-  m.def("window_attn_fwd", &window_attn_fwd);
+  m.def("window_attn_fwd", &window_attn_fwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("geom"),
+        py::arg("scale"), py::arg("impl") = 0);
   m.def("window_attn_bwd", &window_attn_bwd);
 }

@@ -69,6 +69,10 @@ struct AttnGeom {
 };
 cudaError_t window_attn_fwd(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
                             const AttnGeom& g, int dtype, cudaStream_t s);
+// tcgen05/TMEM forward (bf16, head_dim 64, T*wh*ww <= 176); same outputs as window_attn_fwd
+bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype);
+cudaError_t window_attn_fwd_tc(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
+                               const AttnGeom& g, cudaStream_t s);
 cudaError_t window_attn_bwd(const void* qkv, const float* qw, const float* kw, const void* out,
                             const void* dout, const float* lse, void* dqkv, float* dqw_part,
                             float* dkw_part, const AttnGeom& g, int dtype, cudaStream_t s);

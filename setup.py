@@ -16,6 +16,7 @@ SOURCES = [
     os.path.join(CSRC, "bindings.cpp"),
     os.path.join(CSRC, "elementwise.cu"),
     os.path.join(CSRC, "attention.cu"),
+    os.path.join(CSRC, "attention_tc.cu"),
     os.path.join(CSRC, "gemm_tcgen05.cu"),
     os.path.join(CSRC, "noalloc_rmsnorm.cu"),
 ]

@@ -273,3 +273,32 @@ def test_fused_mlp(residual):
         assert rel(a.grad, b.grad) < 3e-2
     if residual:
         assert rel(res.grad, rr.grad) < 1e-2
+
+
+# --------------------------------------------------------------------------- tcgen05 attention forward
+TC_CASES = [
+    (1, 1, 18, 36, 2, (9, 18), (0, 0), False),
+    (1, 1, 18, 36, 2, (9, 18), (4, 9), True),
+    (2, 1, 27, 36, 3, (9, 18), (4, 9), True),
+    (1, 1, 16, 32, 2, (8, 16), (4, 8), True),
+    (1, 2, 8, 16, 2, (4, 8), (2, 4), True),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES)
+def test_window_attention_tcgen05_forward(case, _ext_loaded):
+    B, T, H, W, nh, win, shift, mask = case
+    hd = 64
+    torch.manual_seed(0)
+    C = nh * hd
+    geom = WindowGeometry(window=win, shift=shift, mask=mask, mask_shift=shift[0], row_offset=0, h_global=H)
+    qkv = torch.randn(B, T, H, W, 3 * C, device=DEV).bfloat16()
+    qw = 1 + 0.1 * torch.randn(hd, device=DEV)
+    kw = 1 + 0.1 * torch.randn(hd, device=DEV)
+    gi = [B, T, H, W, nh, hd, win[0], win[1], shift[0], shift[1], int(mask), shift[0], 0, H]
+    out_tc, lse_tc = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 2)
+    out_mma, lse_mma = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 1)
+    ref = reference.window_attention(qkv.float(), qw, kw, nh, hd, geom, hd ** -0.5)
+    assert rel(out_tc.view_as(ref), ref) < 2e-2
+    assert rel(out_tc, out_mma) < 1e-2
+    assert torch.allclose(lse_tc, lse_mma, atol=2e-2, rtol=1e-3)
