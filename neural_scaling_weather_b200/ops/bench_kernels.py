@@ -131,13 +131,15 @@ def bench_attention(a):
     tokens = B * H * W
     L = 162
     flops = 4.0 * tokens * L * hd * nh  # QK^T and PV
-    for impl, tag in ((1, "mma.sync"), (2, "tcgen05")):
+    impls = [(i, t) for i, t in ((1, "mma.sync"), (2, "tcgen05")) if a.impl in (0, i)]
+    for impl, tag in impls:
         ms = timeit(lambda: ext.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, impl), a.iters)
         report(f"window_attn_fwd[{tag}] tokens={tokens} heads={nh}", ms, flops, 2 * tokens * 4 * C)
     dout = torch.randn_like(out)
-    ms = timeit(lambda: ext.window_attn_bwd(qkv.view(-1, 3 * C), qw, kw, out, dout, lse, gi, hd ** -0.5),
-                a.iters)
-    report(f"window_attn_bwd tokens={tokens} heads={nh}", ms, 2.5 * flops, 2 * tokens * 8 * C)
+    for impl, tag in impls:
+        ms = timeit(lambda: ext.window_attn_bwd(qkv.view(-1, 3 * C), qw, kw, out, dout, lse, gi, hd ** -0.5,
+                                                impl), a.iters)
+        report(f"window_attn_bwd[{tag}] tokens={tokens} heads={nh}", ms, 2.5 * flops, 2 * tokens * 8 * C)
 
 
 def bench_rmsnorm(a):
@@ -188,6 +190,7 @@ def main():
     ap.add_argument("--epilogue", default="bias", choices=["none", "bias", "gelu", "residual"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true")
+    ap.add_argument("--impl", type=int, default=0, help="attention: 1 = mma.sync only, 2 = tcgen05 only")
     a = ap.parse_args()
     if a.kernel in ("gemm", "all"):
         bench_gemm(a)

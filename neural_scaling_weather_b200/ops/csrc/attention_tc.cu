@@ -23,6 +23,8 @@
 #include <float.h>
 
 #include "common.cuh"
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace nsw {
@@ -370,11 +372,645 @@ __global__ void __launch_bounds__(128, 2)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
 }
 
+
+// ============================================================================ backward
+// Persistent: one CTA (16 warps) per SM walks a contiguous range of (window, head) items, heads
+// fastest, so the token table is rebuilt only when the window changes and the next item's rows
+// are prefetched into L2 while the current item computes.  Warp w reads TMEM lanes 32*(w%4)..
+// (its lane quarter) and column group w/4: four warps share every row and split its columns.
+// Query tile 0 is rows [0,128); tile 1 is rows [NK-128, NK) with rows < 128 masked, so every
+// row buffer holds NK <= 176 rows.  Key tile 1 starts at key 64 (a 64-key block boundary, as
+// the MN-major operand needs) and only its keys >= 128 are used.  Per query tile t:
+//   S   = Qhat_t Khat^T   -> TMEM R            (A, B K-major)
+//   P   = exp2(S*scale*log2e + mask - lse)     bf16 into smem `ps` ([128 rows x 64 keys] SW128
+//                                              blocks)
+//   dP  = dO_t V^T       -> TMEM R            (A, B K-major)
+//   dV += P^T dO_t       -> TMEM dV[kt]       (A = ps read MN-major, B = dO MN-major)
+//   dS  = P * (dP - D) * scale                 written over P in `ps`
+//   dK += dS^T Qhat_t    -> TMEM dK[kt]       (A = ps MN-major, B = Qhat MN-major)
+//   dQ  = dS Khat        -> TMEM dQ           (A = ps K-major, B = Khat MN-major)
+//   dQ epilogue: QK-RMSNorm backward from the raw q rows kept in smem; weight-gradient partial.
+// After both tiles: dV and dK (with the k-norm backward) per key row.
+// The same computation, on CUDA cores, is the mma.sync backward in attention.cu.
+constexpr int DQ_COL = 192, DV_COL = 256, DK_COL = 384, BWD_TMEM_COLS = 512;
+constexpr int PS_BLOCK = 128 * ROW_B;  // one 64-key block of the P/dS tile (16 KB)
+constexpr int BWD_THREADS = 512;
+constexpr int KT1 = 64;  // first key of key tile 1
+constexpr int ROWBUF = MAXL * ROW_B;
+static_assert(BWD_THREADS >= 2 * MAXL, "D is computed by two threads per row");
+
+struct __align__(1024) SmemB {
+  unsigned char q[ROWBUF];   // normalized q (MMA operand)
+  unsigned char k[ROWBUF];   // normalized k
+  unsigned char v[ROWBUF];
+  unsigned char dO[ROWBUF];
+  unsigned char ps[3 * PS_BLOCK];  // P, then dS, of the current query tile (keys < 192)
+  unsigned char xq[ROWBUF];  // raw q rows (norm backward)
+  unsigned char xk[ROWBUF];  // raw k rows
+  int tok[MAXL];
+  signed char lab[MAXL];
+  float lse[MAXL];
+  float D[MAXL];
+  float rq[MAXL];
+  float rk[MAXL];
+  float red[4][128];  // per-column-group partial dot products of the norm backward
+  float wq[HD];     // weight-gradient partials of the current item
+  float wk[HD];
+  float qwv[HD];    // norm weights
+  float kwv[HD];
+  uint64_t bar;     // MMA completion
+  uint64_t bar_ld;  // TMA gather completion
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint64_t desc_mn(const void* p, uint32_t lbo_bytes) {
+  const uint32_t a = smem_u32(p);
+  return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// byte offset of (row, key) in the P/dS tile (16-byte chunk granularity)
+__device__ __forceinline__ uint32_t ps_off(int row, int key) {
+  return (uint32_t)((key >> 6) * PS_BLOCK) + swz(row, (key & 63) >> 3);
+}
+
+// Only warp 0 polls an mbarrier; the other warps wait in the block barrier that follows, so
+// 500 threads do not spin on shared memory while the tensor core reads its operands there.
+
+// Sum v[0..15] over the warp by recursive halving (16 shuffles instead of 80): afterwards
+// lanes 2m and 2m+1 hold the warp total of element e(lane) returned by this function.
+__device__ __forceinline__ int warp_reduce16(float* v, int lane) {
+#pragma unroll
+  for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+    const bool up = lane & bit;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = up ? v[i] : v[i + half];
+      const float keep = up ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+
+// QK-RMSNorm backward of 16 columns [16*cg, 16*cg+16) of one row, split over four threads.
+// y = x * rs * w  =>  dx = rs*w*g - x * rs^3 * sum_j(w_j g_j x_j) / HD;  dw_j += g_j x_j rs.
+// Phase 1 (before a block barrier): partial dot.  Phase 2: output + dw partial.
+struct NormRow {
+  float x[16];
+  float dot;
+};
+__device__ __forceinline__ void norm_bwd_phase1(NormRow& nr, const float* g, const unsigned char* xrow_buf, int r,
+                                                int cg, const float* w, bool valid) {
+  nr.dot = 0.f;
+  if (!valid) return;
+  unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(xrow_buf + swz(r, 2 * cg)), nr.x);
+  unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(xrow_buf + swz(r, 2 * cg + 1)), nr.x + 8);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) nr.dot += w[i] * g[i] * nr.x[i];
+}
+__device__ __forceinline__ void norm_bwd_phase2(const NormRow& nr, const float* g, const float* w, float rs,
+                                                float dot, __nv_bfloat16* dst, float* wpart, bool valid) {
+  if (!valid) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) wpart[i] = 0.f;
+    return;
+  }
+  const float k3 = rs * rs * rs * dot * (1.f / HD);
+  float o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    o[i] = rs * w[i] * g[i] - nr.x[i] * k3;
+    wpart[i] = g[i] * nr.x[i] * rs;
+  }
+  reinterpret_cast<uint4*>(dst)[0] = pack8<__nv_bfloat16>(o);
+  reinterpret_cast<uint4*>(dst)[1] = pack8<__nv_bfloat16>(o + 8);
+}
+
+
+// Load 16*NCH consecutive TMEM columns of this warp's lane quarter (one wait for all).
+template <int NCH>
+__device__ __forceinline__ void ld_cols(uint32_t taddr, float* f);
+template <>
+__device__ __forceinline__ void ld_cols<1>(uint32_t taddr, float* f) {
+  ld16(taddr, f);
+}
+template <>
+__device__ __forceinline__ void ld_cols<2>(uint32_t taddr, float* f) {
+  ld32(taddr, f);
+}
+template <>
+__device__ __forceinline__ void ld_cols<3>(uint32_t taddr, float* f) {
+  uint32_t r[48];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%48];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47},"
+      " [%49];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
+      : "r"(taddr), "r"(taddr + 32)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 48; ++i) f[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// P = exp2(S * scale * log2e + mask - lse) for keys [16 c0, 16 (c0 + NCH)) of one row, packed
+// to bf16 into `ps`.  Chunks fully inside [0, L) of a window with one mask label take the fast
+// path (one FMA + one ex2 per element); others add the -100 mask of mismatched labels and
+// give padding keys (label -1) P = 0.
+template <int NCH>
+__device__ __forceinline__ void p_chunks(uint32_t trow, SmemB& S, int rt, int c0, float lse_r, int lr, float sl2,
+                                         float ml2, int mixed, int L) {
+  float v[16 * NCH];
+  ld_cols<NCH>(trow + 16 * c0, v);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int j = c0 + c;
+    uint32_t pk[8];
+    if (!mixed && 16 * j + 16 <= L) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        pk[i] = pack_bf16(ex2(fmaf(v[16 * c + 2 * i], sl2, -lse_r)), ex2(fmaf(v[16 * c + 2 * i + 1], sl2, -lse_r)));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float pr[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int lk = S.lab[16 * j + 2 * i + e];
+          const float s = fmaf(v[16 * c + 2 * i + e], sl2, (lk != lr ? ml2 : 0.f) - lse_r);
+          pr[e] = lk >= 0 ? ex2(s) : 0.f;
+        }
+        pk[i] = pack_bf16(pr[0], pr[1]);
+      }
+    }
+    *reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    *reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+}
+
+// dS = P * (dP - D) * scale = P * fma(dP, scale, -D*scale), written over P.
+template <int NCH>
+__device__ __forceinline__ void ds_chunks(uint32_t trow, SmemB& S, int rt, int c0, float scale, float Ds) {
+  float v[16 * NCH];
+  ld_cols<NCH>(trow + 16 * c0, v);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int j = c0 + c;
+    uint4* p0 = reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j));
+    uint4* p1 = reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j + 8));
+    const uint4 a = *p0, b = *p1;
+    const uint32_t pin[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      pk[i] = pack_bf16(bf16_lo(pin[i]) * fmaf(v[16 * c + 2 * i], scale, -Ds),
+                        bf16_hi(pin[i]) * fmaf(v[16 * c + 2 * i + 1], scale, -Ds));
+    *p0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    *p1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// TMA row gather: four 128-byte rows (one-row box of 64 bf16, SWIZZLE_128B) at row coordinates
+// r0..r3 and column `col` into 512 contiguous bytes of smem; out-of-range rows read as zeros.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int col, int r0,
+                                            int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_dout,
+               const __grid_constant__ CUtensorMap map_out, const __nv_bfloat16* __restrict__ qkv,
+               const float* __restrict__ qw, const float* __restrict__ kw, const __nv_bfloat16* __restrict__ out,
+               const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
+               __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqw_part, float* __restrict__ dkw_part,
+               AttnGeom g, int* err, long long* __restrict__ stamps) {
+  extern __shared__ unsigned char smem_raw[];
+  SmemB& S = *reinterpret_cast<SmemB*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lg = warp & 3;   // TMEM lane quarter
+  const int cg = warp >> 2;  // column group
+  const int L = g.T * g.wh * g.ww;
+  const int NK = (L + 15) & ~15;
+  const int ntiles = (L + 127) / 128;
+  const int nww = g.W / g.ww, nwh = g.H / g.wh;
+  const int64_t C = (int64_t)g.nh * HD;
+  const int64_t n_items = (int64_t)g.B * nwh * nww * g.nh;
+  const int64_t i_begin = n_items * blockIdx.x / gridDim.x;
+  const int64_t i_end = n_items * (blockIdx.x + 1) / gridDim.x;
+  // optional phase timestamps (SM clock) of the third item of the first CTAs; null in production
+  long long* st_base = (stamps && blockIdx.x < 64) ? stamps + 32 * blockIdx.x : nullptr;
+  long long* st = nullptr;
+  int nst = 0;
+#define NSW_STAMP() \
+  do {              \
+    if (st && threadIdx.x == 0 && nst < 32) st[nst++] = clock64(); \
+  } while (0)
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+                 "r"(BWD_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar)));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar_ld)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  const int n_tok = g.B * g.T * g.H * g.W;
+  const int ng4 = (L + 3) / 4;  // gather4 groups per buffer
+  const int pad_rows = max(NK, 128);
+  // rows [L, max(NK,128)) of the operands and all of ps start as zeros; the gathers write only
+  // rows < 4*ng4 (zeros beyond L), so the padding stays zero
+  for (int idx = tid; idx < (pad_rows - L) * 8; idx += BWD_THREADS) {
+    const int r = L + (idx >> 3), c = idx & 7;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(S.q + swz(r, c)) = z;
+    *reinterpret_cast<uint4*>(S.k + swz(r, c)) = z;
+    *reinterpret_cast<uint4*>(S.v + swz(r, c)) = z;
+    *reinterpret_cast<uint4*>(S.dO + swz(r, c)) = z;
+  }
+  for (int idx = tid; idx < 3 * PS_BLOCK / 16; idx += BWD_THREADS)
+    reinterpret_cast<uint4*>(S.ps)[idx] = make_uint4(0, 0, 0, 0);
+  if (tid < HD) {
+    S.qwv[tid] = qw[tid];
+    S.kwv[tid] = kw[tid];
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem_base;
+  const uint32_t trow = tmem + ((uint32_t)(lg * 32) << 16);
+  const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NK >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  const uint32_t id_mn = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                         ((uint32_t)(128 >> 4) << 24);
+  const uint32_t id_q = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                        ((uint32_t)(128 >> 4) << 24);
+  const float sl2 = g.scale * kLog2e;
+  const float ml2 = -100.f * kLog2e;
+  const int rt = lg * 32 + lane;  // row within a 128-row tile
+  const float* wcol_q = S.qwv + 16 * cg;
+  const float* wcol_k = S.kwv + 16 * cg;
+  uint32_t parity = 0, ld_parity = 0;
+  bool ok = true;
+  int64_t cur_win = -1;
+  int mixed = 0;
+
+  for (int64_t item = i_begin; item < i_end && ok; ++item) {
+    st = (st_base && item == i_begin + 2) ? st_base : nullptr;
+    NSW_STAMP();
+    const int64_t win = item / g.nh;
+    const int h = (int)(item - win * g.nh);
+    if (win != cur_win) {
+      cur_win = win;
+      WinPos p;
+      p.wx = (int)(win % nww);
+      p.wy = (int)((win / nww) % nwh);
+      p.b = (int)(win / ((int64_t)nww * nwh));
+      const int lab0 = label(g, p, 0);
+      int mx = 0;
+      for (int i = tid; i < MAXL; i += BWD_THREADS) {
+        S.tok[i] = i < L ? (int)token(g, p, i) : 0;
+        const int lb = i < L ? label(g, p, i) : -1;
+        S.lab[i] = (signed char)lb;
+        mx |= (i < L && lb != lab0);
+      }
+      mixed = __syncthreads_or(mx);
+    }
+    if (tid < HD) {
+      S.wq[tid] = 0.f;
+      S.wk[tid] = 0.f;
+    }
+    // TMA gathers of raw q, raw k, v, dO and O (O into the P/dS area, free until the first tile)
+    if (tid == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.bar_ld)),
+                   "r"(5 * ng4 * 512)
+                   : "memory");
+    __syncthreads();  // token table, expect_tx
+    if (lane == 0 && warp < 5) {
+      const CUtensorMap* map = warp < 3 ? &map_qkv : warp == 3 ? &map_dout : &map_out;
+      unsigned char* buf = warp == 0 ? S.xq : warp == 1 ? S.xk : warp == 2 ? S.v : warp == 3 ? S.dO : S.ps;
+      const int col = (warp < 3 ? warp * (int)C : 0) + h * HD;
+      for (int g4 = 0; g4 < ng4; ++g4) {
+        int rr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rr[i] = 4 * g4 + i < L ? S.tok[4 * g4 + i] : n_tok;
+        tma_gather4(buf + g4 * 512, map, &S.bar_ld, col, rr[0], rr[1], rr[2], rr[3]);
+      }
+    }
+    // L2 prefetch of the next item's rows (q, k, v, dO, O of its head)
+    if (item + 1 < i_end) {
+      const int64_t nwin = (item + 1) / g.nh;
+      const int nh_ = (int)(item + 1 - nwin * g.nh);
+      WinPos pn;
+      pn.wx = (int)(nwin % nww);
+      pn.wy = (int)((nwin / nww) % nwh);
+      pn.b = (int)(nwin / ((int64_t)nww * nwh));
+      for (int idx = tid; idx < 5 * L; idx += BWD_THREADS) {
+        const int i = idx % L, which = idx / L;
+        const int64_t tk = nwin == win ? (int64_t)S.tok[i] : token(g, pn, i);
+        const __nv_bfloat16* ptr = which < 3 ? qkv + tk * g.qkv_stride + which * C + (int64_t)nh_ * HD
+                                   : which == 3 ? dout + tk * g.out_stride + (int64_t)nh_ * HD
+                                                : out + tk * g.out_stride + (int64_t)nh_ * HD;
+        prefetch_l2(ptr);
+      }
+    }
+    const int64_t lse_base = item * L;  // items are (window, head) in the forward's lse order
+    if (tid < L) S.lse[tid] = lse[lse_base + tid];
+    ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar_ld, ld_parity, err) : true);
+    ld_parity ^= 1;
+    if (!ok) break;
+    NSW_STAMP();
+    // D = rowsum(dO * O), two threads per row
+    {
+      const int r = tid >> 1, half = tid & 1;
+      float d = 0.f;
+      if (r < L) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float a8[8], o8[8];
+          unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(S.dO + swz(r, 4 * half + c)), a8);
+          unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(S.ps + swz(r, 4 * half + c)), o8);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d += a8[i] * o8[i];
+        }
+      }
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      if (half == 0 && r < L) S.D[r] = d;
+    }
+    // QK-RMSNorm of the raw rows into the MMA operands (rstd kept for the backward)
+    for (int rr = tid; rr < 2 * L; rr += BWD_THREADS) {
+      const bool isq = rr < L;
+      const int r = isq ? rr : rr - L;
+      const unsigned char* src = isq ? S.xq : S.xk;
+      unsigned char* dst = isq ? S.q : S.k;
+      const float* w = isq ? S.qwv : S.kwv;
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float f[8];
+        unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(src + swz(r, c)), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+      }
+      const float rs = rsqrtf(ss / (float)HD + FLT_EPSILON);
+      if (isq) S.rq[r] = rs;
+      else S.rk[r] = rs;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float f[8];
+        unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(src + swz(r, c)), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] *= rs * w[c * 8 + i];
+        *reinterpret_cast<uint4*>(dst + swz(r, c)) = pack8<__nv_bfloat16>(f);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    fence_before();
+    __syncthreads();
+    fence_after();
+    NSW_STAMP();
+
+    for (int t = 0; t < ntiles; ++t) {
+      const int qb = t == 0 ? 0 : NK - 128;  // first row of the tile
+      const int lo = t * 128;                 // rows below lo belong to tile 0
+      const int r = qb + rt;
+      const bool rvalid = r >= lo && r < L;
+      const bool warp_live = qb + lg * 32 + 31 >= lo && qb + lg * 32 < L;  // warp-uniform
+      // ---- S
+      if (tid == 0) {
+        fence_after();
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_ss(tmem, desc_kmajor(S.q + qb * ROW_B + ks * 32), desc_kmajor(S.k + ks * 32), id_s, ks > 0);
+        commit(&S.bar);
+      }
+      __syncwarp();
+      ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar, parity, err) : true);
+      parity ^= 1;
+      if (!ok) break;
+      NSW_STAMP();
+      fence_after();
+      // ---- P -> ps.  Column group cg owns keys [48 cg, 48 cg + 48) (three 16-key chunks);
+      // rows outside the tile's range get lse = +inf and so P = 0 without a branch.
+      {
+        const int c0 = 3 * cg, nch = max(0, min(3, NK / 16 - c0));
+        if (warp_live) {
+          const float lse_r = rvalid ? S.lse[r] : INFINITY;
+          const int lr = rvalid ? S.lab[r] : 0;
+          if (nch == 3) p_chunks<3>(trow, S, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
+          else if (nch == 2) p_chunks<2>(trow, S, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
+          else if (nch == 1) p_chunks<1>(trow, S, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
+        } else {
+          for (int j = c0; j < c0 + nch; ++j) {
+            *reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j + 8)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_before();
+      __syncthreads();
+      NSW_STAMP();
+      // ---- dP = dO V^T; dV += P^T dO
+      if (tid == 0) {
+        fence_after();
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_ss(tmem, desc_kmajor(S.dO + qb * ROW_B + ks * 32), desc_kmajor(S.v + ks * 32), id_s, ks > 0);
+        NSW_STAMP();
+        for (int kt = 0; kt < ntiles; ++kt)
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ss(tmem + DV_COL + 64 * kt, desc_mn(S.ps + kt * PS_BLOCK + ks * 2048, PS_BLOCK),
+                   desc_mn(S.dO + qb * ROW_B + ks * 2048, 16), id_mn, (t > 0 || ks > 0));
+        commit(&S.bar);
+      }
+      NSW_STAMP();
+      __syncwarp();
+      ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar, parity, err) : true);
+      parity ^= 1;
+      if (!ok) break;
+      NSW_STAMP();
+      fence_after();
+      // ---- dS = P (dP - D) scale, over P (rows of dead warps stay zero)
+      if (warp_live) {
+        const int c0 = 3 * cg, nch = max(0, min(3, NK / 16 - c0));
+        const float Ds = rvalid ? S.D[r] * g.scale : 0.f;
+        if (nch == 3) ds_chunks<3>(trow, S, rt, c0, g.scale, Ds);
+        else if (nch == 2) ds_chunks<2>(trow, S, rt, c0, g.scale, Ds);
+        else if (nch == 1) ds_chunks<1>(trow, S, rt, c0, g.scale, Ds);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_before();
+      __syncthreads();
+      NSW_STAMP();
+      // ---- dK += dS^T Qhat; dQ = dS Khat
+      if (tid == 0) {
+        fence_after();
+        for (int kt = 0; kt < ntiles; ++kt)
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ss(tmem + DK_COL + 64 * kt, desc_mn(S.ps + kt * PS_BLOCK + ks * 2048, PS_BLOCK),
+                   desc_mn(S.q + qb * ROW_B + ks * 2048, 16), id_mn, (t > 0 || ks > 0));
+        for (int ks = 0; ks < NK / 16; ++ks)
+          mma_ss(tmem + DQ_COL, desc_kmajor(S.ps + (ks >> 2) * PS_BLOCK + (ks & 3) * 32),
+                 desc_mn(S.k + ks * 2048, 16), id_q, ks > 0);
+        commit(&S.bar);
+      }
+      __syncwarp();
+      ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar, parity, err) : true);
+      parity ^= 1;
+      if (!ok) break;
+      NSW_STAMP();
+      fence_after();
+      // ---- dQ epilogue (QK-norm backward of q)
+      {
+        float gq[16];
+        NormRow nr;
+        if (warp_live) ld16(trow + DQ_COL + 16 * cg, gq);
+        norm_bwd_phase1(nr, gq, S.xq, r, cg, wcol_q, rvalid);
+        S.red[cg][rt] = nr.dot;
+        __syncthreads();
+        const float dot = S.red[0][rt] + S.red[1][rt] + S.red[2][rt] + S.red[3][rt];
+        float wpart[16];
+        const int64_t off = rvalid ? (int64_t)S.tok[r] * g.qkv_stride + (int64_t)h * HD + 16 * cg : 0;
+        norm_bwd_phase2(nr, gq, wcol_q, rvalid ? S.rq[r] : 0.f, dot, dqkv + off, wpart, rvalid);
+        if (warp_live) {
+          const int e = warp_reduce16(wpart, lane);
+          if ((lane & 1) == 0) atomicAdd(&S.wq[16 * cg + e], wpart[0]);
+        }
+      }
+      fence_before();
+      __syncthreads();  // R, dQ, red and ps are reused by the next tile
+      NSW_STAMP();
+    }
+    if (!ok) break;
+    // ---- dV, dK epilogues (key rows)
+    for (int kt = 0; kt < ntiles; ++kt) {
+      const int kb = kt == 0 ? 0 : KT1;
+      const int lo = kt * 128;
+      const int kr = kb + rt;
+      const bool live = kb + lg * 32 + 31 >= lo && kb + lg * 32 < L;  // warp-uniform
+      const bool kvalid = kr >= lo && kr < L;
+      const int64_t row_off = kvalid ? (int64_t)S.tok[kr] * g.qkv_stride + (int64_t)h * HD + 16 * cg : 0;
+      {
+        float gv[16];
+        if (live) ld16(trow + DV_COL + 64 * kt + 16 * cg, gv);
+        if (kvalid) {
+          uint4* dv = reinterpret_cast<uint4*>(dqkv + row_off + 2 * C);
+          dv[0] = pack8<__nv_bfloat16>(gv);
+          dv[1] = pack8<__nv_bfloat16>(gv + 8);
+        }
+      }
+      float gk[16];
+      if (live) ld16(trow + DK_COL + 64 * kt + 16 * cg, gk);
+      NormRow nr;
+      norm_bwd_phase1(nr, gk, S.xk, kr, cg, wcol_k, kvalid);
+      S.red[cg][rt] = nr.dot;
+      __syncthreads();
+      const float dot = S.red[0][rt] + S.red[1][rt] + S.red[2][rt] + S.red[3][rt];
+      float wpart[16];
+      norm_bwd_phase2(nr, gk, wcol_k, kvalid ? S.rk[kr] : 0.f, dot, dqkv + row_off + C, wpart, kvalid);
+      if (live) {
+        const int e = warp_reduce16(wpart, lane);
+        if ((lane & 1) == 0) atomicAdd(&S.wk[16 * cg + e], wpart[0]);
+      }
+      __syncthreads();  // red is rewritten by the next key tile; wq/wk complete
+    }
+    fence_before();
+    NSW_STAMP();
+    if (tid < HD) {
+      dqw_part[item * HD + tid] = S.wq[tid];
+      dkw_part[item * HD + tid] = S.wk[tid];
+    }
+  }
+#undef NSW_STAMP
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BWD_TMEM_COLS));
+}
+
 }  // namespace attn_tc
 
 bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype) {
   const int L = g.T * g.wh * g.ww;
   return dtype == kBF16 && g.hd == 64 && L >= 1 && L <= attn_tc::MAXL && g.H % g.wh == 0 && g.W % g.ww == 0;
+}
+
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [rows, cols] bf16 row-major with leading dimension ld; box = one row of 64 elements (gather4)
+bool row_gather_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw, const void* out,
+                               const void* dout, const float* lse, void* dqkv, float* dqw_part, float* dkw_part,
+                               const AttnGeom& g, cudaStream_t s, long long* stamps) {
+  const size_t smem = sizeof(attn_tc::SmemB) + 1024;
+  auto k = attn_tc::bwd_kernel;
+  NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int dev = 0, sms = 0;
+  NSW_CUDA_CHECK(cudaGetDevice(&dev));
+  NSW_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t n_tok = (int64_t)g.B * g.T * g.H * g.W;
+  if (n_tok >= (1LL << 31) - 1) return cudaErrorInvalidValue;
+  CUtensorMap m_qkv, m_dout, m_out;
+  if (!row_gather_map(&m_qkv, qkv, n_tok, g.qkv_stride, g.qkv_stride) ||
+      !row_gather_map(&m_dout, dout, n_tok, g.out_stride, g.out_stride) ||
+      !row_gather_map(&m_out, out, n_tok, g.out_stride, g.out_stride))
+    return cudaErrorInvalidValue;
+  const int64_t items = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww) * g.nh;
+  const int grid = (int)std::min<int64_t>(items, sms);
+  k<<<grid, attn_tc::BWD_THREADS, smem, s>>>(m_qkv, m_dout, m_out, (const __nv_bfloat16*)qkv, qw, kw,
+                                             (const __nv_bfloat16*)out, (const __nv_bfloat16*)dout, lse,
+                                             (__nv_bfloat16*)dqkv, dqw_part, dkw_part, g, device_error_flag(),
+                                             stamps);
+  return cudaGetLastError();
 }
 
 cudaError_t window_attn_fwd_tc(const void* qkv, const float* qw, const float* kw, void* out, float* lse,

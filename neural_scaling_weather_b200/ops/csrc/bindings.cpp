@@ -343,7 +343,8 @@ std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vecto
 }
 
 std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out, Tensor dout, Tensor lse,
-                                    std::vector<int64_t> gi, double scale) {
+                                    std::vector<int64_t> gi, double scale, int64_t impl,
+                                    c10::optional<Tensor> stamps) {
   need_cuda(qkv, "qkv");
   need_cuda(dout, "dout");
   auto g = make_geom(gi, scale);
@@ -351,6 +352,17 @@ std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out
   const int64_t nwin = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww);
   auto qp = torch::empty({nwin * g.nh, (int64_t)g.hd}, qkv.options().dtype(at::kFloat));
   auto kp = torch::empty_like(qp);
+  // impl: 0 = default (tcgen05 where supported), 1 = mma.sync, 2 = tcgen05/TMEM
+  const bool tc_ok = nsw::window_attn_fwd_tc_supported(g, dt_code(qkv));
+  TORCH_CHECK(impl != 2 || tc_ok, "window_attn_bwd: tcgen05 path needs bf16, head_dim 64, window <= 176 tokens");
+  if (tc_ok && impl != 1) {
+    check(nsw::window_attn_bwd_tc(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                                  dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp.data_ptr<float>(),
+                                  kp.data_ptr<float>(), g, stream(),
+                                  stamps ? reinterpret_cast<long long*>(stamps->data_ptr<int64_t>()) : nullptr),
+          "window_attn_bwd_tc");
+    return {dqkv, qp.sum(0), kp.sum(0)};
+  }
   check(nsw::window_attn_bwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
                              dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp.data_ptr<float>(),
                              kp.data_ptr<float>(), g, dt_code(qkv), stream()),
@@ -383,5 +395,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("segment_sumsq", &segment_sumsq);
   m.def("window_attn_fwd", &window_attn_fwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("geom"),
         py::arg("scale"), py::arg("impl") = 0);
-  m.def("window_attn_bwd", &window_attn_bwd);
+  m.def("window_attn_bwd", &window_attn_bwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("out"),
+        py::arg("dout"), py::arg("lse"), py::arg("geom"), py::arg("scale"), py::arg("impl") = 0,
+        py::arg("stamps") = py::none());
 }

@@ -73,6 +73,9 @@ cudaError_t window_attn_fwd(const void* qkv, const float* qw, const float* kw, v
 bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype);
 cudaError_t window_attn_fwd_tc(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
                                const AttnGeom& g, cudaStream_t s);
+cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw, const void* out,
+                               const void* dout, const float* lse, void* dqkv, float* dqw_part, float* dkw_part,
+                               const AttnGeom& g, cudaStream_t s, long long* stamps = nullptr);
 cudaError_t window_attn_bwd(const void* qkv, const float* qw, const float* kw, const void* out,
                             const void* dout, const float* lse, void* dqkv, float* dqw_part,
                             float* dkw_part, const AttnGeom& g, int dtype, cudaStream_t s);

@@ -302,3 +302,31 @@ def test_window_attention_tcgen05_forward(case, _ext_loaded):
     assert rel(out_tc.view_as(ref), ref) < 2e-2
     assert rel(out_tc, out_mma) < 1e-2
     assert torch.allclose(lse_tc, lse_mma, atol=2e-2, rtol=1e-3)
+
+
+@pytest.mark.parametrize("case", TC_CASES)
+def test_window_attention_tcgen05_backward(case, _ext_loaded):
+    B, T, H, W, nh, win, shift, mask = case
+    hd = 64
+    torch.manual_seed(1)
+    C = nh * hd
+    geom = WindowGeometry(window=win, shift=shift, mask=mask, mask_shift=shift[0], row_offset=0, h_global=H)
+    qkv = torch.randn(B, T, H, W, 3 * C, device=DEV).bfloat16()
+    qw = 1 + 0.1 * torch.randn(hd, device=DEV)
+    kw = 1 + 0.1 * torch.randn(hd, device=DEV)
+    gi = [B, T, H, W, nh, hd, win[0], win[1], shift[0], shift[1], int(mask), shift[0], 0, H]
+    out, lse = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 1)
+    dout = torch.randn_like(out)
+    args = (qkv.view(-1, 3 * C), qw, kw, out, dout, lse, gi, hd ** -0.5)
+    dq_tc, dqw_tc, dkw_tc = _ext_loaded.window_attn_bwd(*args, 2)
+    dq_mma, dqw_mma, dkw_mma = _ext_loaded.window_attn_bwd(*args, 1)
+    assert _ext_loaded.read_error_flag(True) == 0
+    xr = qkv.float().requires_grad_()
+    qwr = qw.clone().requires_grad_()
+    kwr = kw.clone().requires_grad_()
+    ref = reference.window_attention(xr, qwr, kwr, nh, hd, geom, hd ** -0.5)
+    ref.backward(dout.float().view_as(ref))
+    assert rel(dq_tc.view_as(xr), xr.grad) < 3e-2
+    assert rel(dq_tc, dq_mma) < 2e-2
+    assert rel(dqw_tc, qwr.grad) < 3e-2
+    assert rel(dkw_tc, kwr.grad) < 3e-2
