@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include <algorithm>
+#include <cstring>
 
 #include "kernels.h"
 
@@ -400,22 +401,22 @@ constexpr int ROWBUF = MAXL * ROW_B;
 static_assert(BWD_THREADS >= 2 * MAXL, "D is computed by two threads per row");
 
 struct __align__(1024) SmemB {
-  unsigned char q[ROWBUF];   // normalized q (MMA operand)
-  unsigned char k[ROWBUF];   // normalized k
+  // q and k rows in two roles that swap every item: raw (gathered; read by the norm backward)
+  // and normalized (MMA operand).  Once an item's last MMA has read its normalized rows, the
+  // next item's raw rows are gathered into that buffer.
+  unsigned char qbuf[2][ROWBUF];
+  unsigned char kbuf[2][ROWBUF];
   unsigned char v[ROWBUF];
   unsigned char dO[ROWBUF];
   unsigned char ps[3 * PS_BLOCK];  // P, then dS, of the current query tile (keys < 192)
-  unsigned char xq[ROWBUF];  // raw q rows (norm backward)
-  unsigned char xk[ROWBUF];  // raw k rows
-  int tok[MAXL];
-  signed char lab[MAXL];
+  int tok[2][MAXL];                // token rows of the current and the next window
+  signed char lab[2][MAXL];
   float lse[MAXL];
-  float D[MAXL];
   float rq[MAXL];
   float rk[MAXL];
   float red[4][128];  // per-column-group partial dot products of the norm backward
-  float wq[HD];     // weight-gradient partials of the current item
-  float wk[HD];
+  float wq[16][HD];  // per-warp weight-gradient partials of the current item
+  float wk[16][HD];
   float qwv[HD];    // norm weights
   float kwv[HD];
   uint64_t bar;     // MMA completion
@@ -434,60 +435,76 @@ __device__ __forceinline__ uint32_t ps_off(int row, int key) {
   return (uint32_t)((key >> 6) * PS_BLOCK) + swz(row, (key & 63) >> 3);
 }
 
+// TMA tile load of a [1 x wh x ww x 64] box (one time step of a window that does not wrap at
+// the grid edge) from a 4-D view [B*T, H, W, cols]; lands in smem in window token order.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // Only warp 0 polls an mbarrier; the other warps wait in the block barrier that follows, so
 // 500 threads do not spin on shared memory while the tensor core reads its operands there.
 
-// Sum v[0..15] over the warp by recursive halving (16 shuffles instead of 80): afterwards
-// lanes 2m and 2m+1 hold the warp total of element e(lane) returned by this function.
-__device__ __forceinline__ int warp_reduce16(float* v, int lane) {
+// fp32 staging of a 128-row x 64-column tile in ps: 256-byte rows, 16-byte chunk q of row r at
+// chunk position q ^ (r & 15), so 32 lanes writing one chunk of 32 rows hit distinct banks.
+__device__ __forceinline__ uint32_t f32_off(int r, int q) { return (uint32_t)(r * 256 + ((q ^ (r & 15)) << 4)); }
+__device__ __forceinline__ void stage_f32(unsigned char* st, int rt, int cg, const float* v) {
 #pragma unroll
-  for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
-    const bool up = lane & bit;
-#pragma unroll
-    for (int i = 0; i < half; ++i) {
-      const float send = up ? v[i] : v[i + half];
-      const float keep = up ? v[i + half] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
-    }
-  }
-  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<float4*>(st + f32_off(rt, 4 * cg + q)) =
+        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
-// QK-RMSNorm backward of 16 columns [16*cg, 16*cg+16) of one row, split over four threads.
+// QK-RMSNorm backward of one staged row, eight threads per row (columns [8c, 8c + 8) each):
 // y = x * rs * w  =>  dx = rs*w*g - x * rs^3 * sum_j(w_j g_j x_j) / HD;  dw_j += g_j x_j rs.
-// Phase 1 (before a block barrier): partial dot.  Phase 2: output + dw partial.
-struct NormRow {
-  float x[16];
-  float dot;
-};
-__device__ __forceinline__ void norm_bwd_phase1(NormRow& nr, const float* g, const unsigned char* xrow_buf, int r,
-                                                int cg, const float* w, bool valid) {
-  nr.dot = 0.f;
+// The row dot product is combined over the eight lanes by shuffles; dw partials accumulate in
+// wacc.  Invalid rows still take part in the shuffles with zeros.
+__device__ __forceinline__ void norm_bwd_task(const unsigned char* st, const unsigned char* xbuf, const float* wv,
+                                              int row, int r, int c, bool valid, float rs, __nv_bfloat16* dst,
+                                              float* wacc) {
+  float gg[8], x[8], w[8];
+  const float4 g0 = *reinterpret_cast<const float4*>(st + f32_off(row, 2 * c));
+  const float4 g1 = *reinterpret_cast<const float4*>(st + f32_off(row, 2 * c + 1));
+  gg[0] = g0.x; gg[1] = g0.y; gg[2] = g0.z; gg[3] = g0.w;
+  gg[4] = g1.x; gg[5] = g1.y; gg[6] = g1.z; gg[7] = g1.w;
+  unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(xbuf + swz(valid ? r : 0, c)), x);
+  const float4 w0 = *reinterpret_cast<const float4*>(wv + 8 * c);
+  const float4 w1 = *reinterpret_cast<const float4*>(wv + 8 * c + 4);
+  w[0] = w0.x; w[1] = w0.y; w[2] = w0.z; w[3] = w0.w;
+  w[4] = w1.x; w[5] = w1.y; w[6] = w1.z; w[7] = w1.w;
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dot = fmaf(w[i] * gg[i], x[i], dot);
+  if (!valid) dot = 0.f;
+  dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+  dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+  dot += __shfl_xor_sync(0xffffffffu, dot, 4);
   if (!valid) return;
-  unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(xrow_buf + swz(r, 2 * cg)), nr.x);
-  unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(xrow_buf + swz(r, 2 * cg + 1)), nr.x + 8);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) nr.dot += w[i] * g[i] * nr.x[i];
-}
-__device__ __forceinline__ void norm_bwd_phase2(const NormRow& nr, const float* g, const float* w, float rs,
-                                                float dot, __nv_bfloat16* dst, float* wpart, bool valid) {
-  if (!valid) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) wpart[i] = 0.f;
-    return;
-  }
   const float k3 = rs * rs * rs * dot * (1.f / HD);
-  float o[16];
+  float o[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    o[i] = rs * w[i] * g[i] - nr.x[i] * k3;
-    wpart[i] = g[i] * nr.x[i] * rs;
+  for (int i = 0; i < 8; ++i) {
+    o[i] = rs * w[i] * gg[i] - x[i] * k3;
+    wacc[i] = fmaf(gg[i] * x[i], rs, wacc[i]);
   }
-  reinterpret_cast<uint4*>(dst)[0] = pack8<__nv_bfloat16>(o);
-  reinterpret_cast<uint4*>(dst)[1] = pack8<__nv_bfloat16>(o + 8);
+  *reinterpret_cast<uint4*>(dst) = pack8<__nv_bfloat16>(o);
 }
 
+// Add the per-thread dw partials of columns [8c, 8c+8) (c = lane & 7) over the warp's four
+// row groups, then into the warp's own slot (no atomics; slots are summed once per item).
+__device__ __forceinline__ void flush_wacc(float* wacc, float* slot, int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float v = wacc[i];
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    if (lane < 8) slot[8 * lane + i] += v;
+  }
+}
 
 // Load 16*NCH consecutive TMEM columns of this warp's lane quarter (one wait for all).
 template <int NCH>
@@ -529,8 +546,8 @@ __device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u 
 // path (one FMA + one ex2 per element); others add the -100 mask of mismatched labels and
 // give padding keys (label -1) P = 0.
 template <int NCH>
-__device__ __forceinline__ void p_chunks(uint32_t trow, SmemB& S, int rt, int c0, float lse_r, int lr, float sl2,
-                                         float ml2, int mixed, int L) {
+__device__ __forceinline__ void p_chunks(uint32_t trow, SmemB& S, const signed char* lab, int rt, int c0, float lse_r,
+                                         int lr, float sl2, float ml2, int mixed, int L) {
   float v[16 * NCH];
   ld_cols<NCH>(trow + 16 * c0, v);
 #pragma unroll
@@ -547,7 +564,7 @@ __device__ __forceinline__ void p_chunks(uint32_t trow, SmemB& S, int rt, int c0
         float pr[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int lk = S.lab[16 * j + 2 * i + e];
+          const int lk = lab[16 * j + 2 * i + e];
           const float s = fmaf(v[16 * c + 2 * i + e], sl2, (lk != lr ? ml2 : 0.f) - lse_r);
           pr[e] = lk >= 0 ? ex2(s) : 0.f;
         }
@@ -581,25 +598,124 @@ __device__ __forceinline__ void ds_chunks(uint32_t trow, SmemB& S, int rt, int c
   }
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+// Partial row sum of P * dP over keys [16 c0, 16 (c0 + NCH)) (D = rowsum(P dP) = rowsum(dO O)).
+template <int NCH>
+__device__ __forceinline__ float pdp_dot(uint32_t trow, const SmemB& S, int rt, int c0) {
+  float v[16 * NCH];
+  ld_cols<NCH>(trow + 16 * c0, v);
+  float d = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int j = c0 + c;
+    const uint4 a = *reinterpret_cast<const uint4*>(S.ps + ps_off(rt, 16 * j));
+    const uint4 b = *reinterpret_cast<const uint4*>(S.ps + ps_off(rt, 16 * j + 8));
+    const uint32_t pin[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      d = fmaf(bf16_lo(pin[i]), v[16 * c + 2 * i], fmaf(bf16_hi(pin[i]), v[16 * c + 2 * i + 1], d));
+  }
+  return d;
 }
 
-// TMA row gather: four 128-byte rows (one-row box of 64 bf16, SWIZZLE_128B) at row coordinates
-// r0..r3 and column `col` into 512 contiguous bytes of smem; out-of-range rows read as zeros.
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int col, int r0,
-                                            int r1, int r2, int r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-      : "memory");
+
+
+
+// How a window's rows are brought in: up to 2 x 2 TMA boxes per time step, split where the
+// shifted window wraps at the W (x) or H (y) edge of the token grid.  Boxes are issued y-part
+// major, x-part minor, and each lands as [height][width] rows, so smem row j holds the window
+// token win_row(j) (attention within a window does not depend on the row order; the token
+// table, labels and lse follow the same permutation).
+struct WinLoad {
+  int x0, y0, bt0;
+  int xw[2], yh[2];  // part widths / heights (second is 0 when that edge does not wrap)
+};
+__device__ __forceinline__ WinLoad win_load(const AttnGeom& g, int64_t w, int nww, int nwh) {
+  WinLoad wl;
+  const int wx = (int)(w % nww), wy = (int)((w / nww) % nwh), b = (int)(w / ((int64_t)nww * nwh));
+  wl.x0 = (wx * g.ww + g.sw) % g.W;
+  wl.y0 = (wy * g.wh + g.sh) % g.H;
+  if (wl.x0 < 0) wl.x0 += g.W;
+  if (wl.y0 < 0) wl.y0 += g.H;
+  wl.bt0 = b * g.T;
+  wl.xw[0] = min(g.ww, g.W - wl.x0);
+  wl.xw[1] = g.ww - wl.xw[0];
+  wl.yh[0] = min(g.wh, g.H - wl.y0);
+  wl.yh[1] = g.wh - wl.yh[0];
+  return wl;
+}
+// window-order index (t*wh + iy)*ww + ix of smem row j
+__device__ __forceinline__ int win_row(const AttnGeom& g, const WinLoad& wl, int j) {
+  const int wa = g.wh * g.ww;
+  const int t = j / wa;
+  int rem = j - t * wa;
+  int iy0 = 0;
+  for (int yp = 0; yp < 2; ++yp) {
+    int ix0 = 0;
+    for (int xp = 0; xp < 2; ++xp) {
+      const int n = wl.xw[xp] * wl.yh[yp];
+      if (rem < n) {
+        const int yy = rem / wl.xw[xp], xx = rem - yy * wl.xw[xp];
+        return (t * g.wh + iy0 + yy) * g.ww + ix0 + xx;
+      }
+      rem -= n;
+      ix0 += wl.xw[xp];
+    }
+    iy0 += wl.yh[yp];
+  }
+  return j;  // not reached
+}
+// map index of a box: 3 x 3 grid over (width, height) in {full, first part, second part}
+__device__ __forceinline__ int box_index(const WinLoad& wl, int xp, int yp) {
+  const int xi = wl.xw[1] == 0 ? 0 : 1 + xp;
+  const int yi = wl.yh[1] == 0 ? 0 : 1 + yp;
+  return yi * 3 + xi;
+}
+
+struct BoxMaps {
+  CUtensorMap m[9];
+};
+
+// One buffer of a window's rows (column `col`, 64 bf16 per token); L * 128 bytes.
+__device__ __forceinline__ void load_window(unsigned char* buf, const BoxMaps& maps, uint64_t* bar, int col,
+                                            const WinLoad& wl, const AttnGeom& g) {
+  const int wa = g.wh * g.ww;
+  for (int t = 0; t < g.T; ++t) {
+    int row = t * wa;
+    for (int yp = 0; yp < 2; ++yp) {
+      if (wl.yh[yp] == 0) continue;
+      for (int xp = 0; xp < 2; ++xp) {
+        if (wl.xw[xp] == 0) continue;
+        tma_load_4d(buf + row * ROW_B, &maps.m[box_index(wl, xp, yp)], bar, col, xp == 0 ? wl.x0 : 0,
+                    yp == 0 ? wl.y0 : 0, wl.bt0 + t);
+        row += wl.xw[xp] * wl.yh[yp];
+      }
+    }
+  }
+}
+
+// Token rows and mask labels of window `w`; returns whether the window mixes labels.
+__device__ __forceinline__ int build_table(const AttnGeom& g, int64_t w, int nww, int nwh, int L, int* tok,
+                                           signed char* lab, int tid) {
+  WinPos p;
+  p.wx = (int)(w % nww);
+  p.wy = (int)((w / nww) % nwh);
+  p.b = (int)(w / ((int64_t)nww * nwh));
+  const WinLoad wl = win_load(g, w, nww, nwh);
+  const int lab0 = label(g, p, 0);
+  int mx = 0;
+  for (int j = tid; j < MAXL; j += BWD_THREADS) {
+    const int i = j < L ? win_row(g, wl, j) : 0;
+    tok[j] = j < L ? (int)token(g, p, i) : 0;
+    const int lb = j < L ? label(g, p, i) : -1;
+    lab[j] = (signed char)lb;
+    mx |= (j < L && lb != lab0);
+  }
+  return __syncthreads_or(mx);
 }
 
 __global__ void __launch_bounds__(BWD_THREADS, 1)
-    bwd_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_dout,
-               const __grid_constant__ CUtensorMap map_out, const __nv_bfloat16* __restrict__ qkv,
-               const float* __restrict__ qw, const float* __restrict__ kw, const __nv_bfloat16* __restrict__ out,
+    bwd_kernel(const __grid_constant__ BoxMaps box_qkv, const __grid_constant__ BoxMaps box_dout,
+               const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
                const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
                __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqw_part, float* __restrict__ dkw_part,
                AttnGeom g, int* err, long long* __restrict__ stamps) {
@@ -635,16 +751,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar_ld)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  const int n_tok = g.B * g.T * g.H * g.W;
-  const int ng4 = (L + 3) / 4;  // gather4 groups per buffer
   const int pad_rows = max(NK, 128);
-  // rows [L, max(NK,128)) of the operands and all of ps start as zeros; the gathers write only
-  // rows < 4*ng4 (zeros beyond L), so the padding stays zero
+  // rows [L, max(NK,128)) of the operands and all of ps start as zeros; the window loads write
+  // only rows < L, so the padding stays zero
   for (int idx = tid; idx < (pad_rows - L) * 8; idx += BWD_THREADS) {
     const int r = L + (idx >> 3), c = idx & 7;
     const uint4 z = make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<uint4*>(S.q + swz(r, c)) = z;
-    *reinterpret_cast<uint4*>(S.k + swz(r, c)) = z;
+#pragma unroll
+    for (int b2 = 0; b2 < 2; ++b2) {
+      *reinterpret_cast<uint4*>(S.qbuf[b2] + swz(r, c)) = z;
+      *reinterpret_cast<uint4*>(S.kbuf[b2] + swz(r, c)) = z;
+    }
     *reinterpret_cast<uint4*>(S.v + swz(r, c)) = z;
     *reinterpret_cast<uint4*>(S.dO + swz(r, c)) = z;
   }
@@ -668,120 +785,92 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const float sl2 = g.scale * kLog2e;
   const float ml2 = -100.f * kLog2e;
   const int rt = lg * 32 + lane;  // row within a 128-row tile
-  const float* wcol_q = S.qwv + 16 * cg;
-  const float* wcol_k = S.kwv + 16 * cg;
   uint32_t parity = 0, ld_parity = 0;
   bool ok = true;
-  int64_t cur_win = -1;
+  int raw = 0;   // index of the raw q/k buffers of the current item
+  int tcur = 0;  // index of the current window's token table
+  int64_t win = i_begin / g.nh;
   int mixed = 0;
+  bool ld_pending = false;  // a gather phase was issued and not yet waited for
+  float lse_next = 0.f;     // lse of row tid of the next item, loaded a phase ahead
+  if (i_begin < i_end) {
+    ld_pending = true;
+    // first item: its table and all four gathers
+    mixed = build_table(g, win, nww, nwh, L, S.tok[0], S.lab[0], tid);
+    const WinLoad wl = win_load(g, win, nww, nwh);
+    if (tid == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.bar_ld)),
+                   "r"(4 * L * ROW_B)
+                   : "memory");
+    __syncthreads();
+    if (lane == 0 && warp < 4) {
+      const int h0 = (int)(i_begin - win * g.nh);
+      unsigned char* buf = warp == 0 ? S.qbuf[0] : warp == 1 ? S.kbuf[0] : warp == 2 ? S.v : S.dO;
+      load_window(buf, warp < 3 ? box_qkv : box_dout, &S.bar_ld, (warp < 3 ? warp * (int)C : 0) + h0 * HD, wl, g);
+    }
+  }
 
   for (int64_t item = i_begin; item < i_end && ok; ++item) {
     st = (st_base && item == i_begin + 2) ? st_base : nullptr;
     NSW_STAMP();
-    const int64_t win = item / g.nh;
     const int h = (int)(item - win * g.nh);
-    if (win != cur_win) {
-      cur_win = win;
-      WinPos p;
-      p.wx = (int)(win % nww);
-      p.wy = (int)((win / nww) % nwh);
-      p.b = (int)(win / ((int64_t)nww * nwh));
-      const int lab0 = label(g, p, 0);
-      int mx = 0;
-      for (int i = tid; i < MAXL; i += BWD_THREADS) {
-        S.tok[i] = i < L ? (int)token(g, p, i) : 0;
-        const int lb = i < L ? label(g, p, i) : -1;
-        S.lab[i] = (signed char)lb;
-        mx |= (i < L && lb != lab0);
-      }
-      mixed = __syncthreads_or(mx);
+    const bool has_next = item + 1 < i_end;
+    const int64_t nwin = (item + 1) / g.nh;
+    const int nh_ = (int)(item + 1 - nwin * g.nh);
+    const int ntab = nwin == win ? tcur : 1 - tcur;
+    int mixed_n = mixed;
+    const int* tok = S.tok[tcur];
+    const signed char* lab = S.lab[tcur];
+    unsigned char* qx = S.qbuf[raw];       // raw q
+    unsigned char* qn = S.qbuf[1 - raw];   // normalized q
+    unsigned char* kx = S.kbuf[raw];
+    unsigned char* kn = S.kbuf[1 - raw];
+    for (int i = lane; i < HD; i += 32) {
+      S.wq[warp][i] = 0.f;
+      S.wk[warp][i] = 0.f;
     }
-    if (tid < HD) {
-      S.wq[tid] = 0.f;
-      S.wk[tid] = 0.f;
-    }
-    // TMA gathers of raw q, raw k, v, dO and O (O into the P/dS area, free until the first tile)
-    if (tid == 0)
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.bar_ld)),
-                   "r"(5 * ng4 * 512)
-                   : "memory");
-    __syncthreads();  // token table, expect_tx
-    if (lane == 0 && warp < 5) {
-      const CUtensorMap* map = warp < 3 ? &map_qkv : warp == 3 ? &map_dout : &map_out;
-      unsigned char* buf = warp == 0 ? S.xq : warp == 1 ? S.xk : warp == 2 ? S.v : warp == 3 ? S.dO : S.ps;
-      const int col = (warp < 3 ? warp * (int)C : 0) + h * HD;
-      for (int g4 = 0; g4 < ng4; ++g4) {
-        int rr[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) rr[i] = 4 * g4 + i < L ? S.tok[4 * g4 + i] : n_tok;
-        tma_gather4(buf + g4 * 512, map, &S.bar_ld, col, rr[0], rr[1], rr[2], rr[3]);
-      }
-    }
-    // L2 prefetch of the next item's rows (q, k, v, dO, O of its head)
-    if (item + 1 < i_end) {
-      const int64_t nwin = (item + 1) / g.nh;
-      const int nh_ = (int)(item + 1 - nwin * g.nh);
-      WinPos pn;
-      pn.wx = (int)(nwin % nww);
-      pn.wy = (int)((nwin / nww) % nwh);
-      pn.b = (int)(nwin / ((int64_t)nww * nwh));
-      for (int idx = tid; idx < 5 * L; idx += BWD_THREADS) {
-        const int i = idx % L, which = idx / L;
-        const int64_t tk = nwin == win ? (int64_t)S.tok[i] : token(g, pn, i);
-        const __nv_bfloat16* ptr = which < 3 ? qkv + tk * g.qkv_stride + which * C + (int64_t)nh_ * HD
-                                   : which == 3 ? dout + tk * g.out_stride + (int64_t)nh_ * HD
-                                                : out + tk * g.out_stride + (int64_t)nh_ * HD;
-        prefetch_l2(ptr);
-      }
-    }
-    const int64_t lse_base = item * L;  // items are (window, head) in the forward's lse order
-    if (tid < L) S.lse[tid] = lse[lse_base + tid];
+    // lse rows of this item (items are (window, head) in the forward's lse order; smem row j
+    // holds window token win_row(j)); loaded during the previous item except for the first
+    if (item == i_begin && tid < L) lse_next = lse[item * L + win_row(g, win_load(g, win, nww, nwh), tid)];
+    if (tid < L) S.lse[tid] = lse_next;
+    NSW_STAMP();
     ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar_ld, ld_parity, err) : true);
     ld_parity ^= 1;
+    ld_pending = false;
     if (!ok) break;
     NSW_STAMP();
-    // D = rowsum(dO * O), two threads per row
-    {
-      const int r = tid >> 1, half = tid & 1;
-      float d = 0.f;
-      if (r < L) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float a8[8], o8[8];
-          unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(S.dO + swz(r, 4 * half + c)), a8);
-          unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(S.ps + swz(r, 4 * half + c)), o8);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) d += a8[i] * o8[i];
-        }
-      }
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      if (half == 0 && r < L) S.D[r] = d;
-    }
-    // QK-RMSNorm of the raw rows into the MMA operands (rstd kept for the backward)
-    for (int rr = tid; rr < 2 * L; rr += BWD_THREADS) {
+    // QK-RMSNorm of the raw rows into the MMA operands (rstd kept for the backward); two
+    // threads per row, each with four of its eight 16-byte chunks
+    for (int base = 0; base < 4 * L; base += BWD_THREADS) {
+      const int idx = base + tid;
+      const bool act = idx < 4 * L;
+      const int rr = act ? idx >> 1 : 0, half = idx & 1;
       const bool isq = rr < L;
       const int r = isq ? rr : rr - L;
-      const unsigned char* src = isq ? S.xq : S.xk;
-      unsigned char* dst = isq ? S.q : S.k;
+      const unsigned char* src = isq ? qx : kx;
+      unsigned char* dst = isq ? qn : kn;
       const float* w = isq ? S.qwv : S.kwv;
+      float f[4][8];
       float ss = 0.f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float f[8];
-        unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(src + swz(r, c)), f);
+      for (int c = 0; c < 4; ++c) {
+        unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(src + swz(r, 4 * half + c)), f[c]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+        for (int i = 0; i < 8; ++i) ss += f[c][i] * f[c][i];
       }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       const float rs = rsqrtf(ss / (float)HD + FLT_EPSILON);
-      if (isq) S.rq[r] = rs;
-      else S.rk[r] = rs;
+      if (act) {
+        if (half == 0) {
+          if (isq) S.rq[r] = rs;
+          else S.rk[r] = rs;
+        }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float f[8];
-        unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(src + swz(r, c)), f);
+        for (int c = 0; c < 4; ++c) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] *= rs * w[c * 8 + i];
-        *reinterpret_cast<uint4*>(dst + swz(r, c)) = pack8<__nv_bfloat16>(f);
+          for (int i = 0; i < 8; ++i) f[c][i] *= rs * w[(4 * half + c) * 8 + i];
+          *reinterpret_cast<uint4*>(dst + swz(r, 4 * half + c)) = pack8<__nv_bfloat16>(f[c]);
+        }
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -796,12 +885,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const int r = qb + rt;
       const bool rvalid = r >= lo && r < L;
       const bool warp_live = qb + lg * 32 + 31 >= lo && qb + lg * 32 < L;  // warp-uniform
-      // ---- S
-      if (tid == 0) {
+      // ---- S (tile 0 here; later tiles are issued before the previous tile's dQ epilogue)
+      if (t == 0 && tid == 0) {
         fence_after();
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
-          mma_ss(tmem, desc_kmajor(S.q + qb * ROW_B + ks * 32), desc_kmajor(S.k + ks * 32), id_s, ks > 0);
+          mma_ss(tmem, desc_kmajor(qn + ks * 32), desc_kmajor(kn + ks * 32), id_s, ks > 0);
         commit(&S.bar);
       }
       __syncwarp();
@@ -816,10 +905,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const int c0 = 3 * cg, nch = max(0, min(3, NK / 16 - c0));
         if (warp_live) {
           const float lse_r = rvalid ? S.lse[r] : INFINITY;
-          const int lr = rvalid ? S.lab[r] : 0;
-          if (nch == 3) p_chunks<3>(trow, S, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
-          else if (nch == 2) p_chunks<2>(trow, S, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
-          else if (nch == 1) p_chunks<1>(trow, S, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
+          const int lr = rvalid ? lab[r] : 0;
+          if (nch == 3) p_chunks<3>(trow, S, lab, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
+          else if (nch == 2) p_chunks<2>(trow, S, lab, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
+          else if (nch == 1) p_chunks<1>(trow, S, lab, rt, c0, lse_r, lr, sl2, ml2, mixed, L);
         } else {
           for (int j = c0; j < c0 + nch; ++j) {
             *reinterpret_cast<uint4*>(S.ps + ps_off(rt, 16 * j)) = make_uint4(0, 0, 0, 0);
@@ -851,13 +940,38 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (!ok) break;
       NSW_STAMP();
       fence_after();
-      // ---- dS = P (dP - D) scale, over P (rows of dead warps stay zero)
-      if (warp_live) {
+      // v and dO are free once the last tile's dP/dV MMAs are done: gather the next item's
+      if (t == ntiles - 1 && has_next) {
+        if (nwin != win) mixed_n = build_table(g, nwin, nww, nwh, L, S.tok[ntab], S.lab[ntab], tid);
+        if (tid == 0)
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.bar_ld)),
+                       "r"(4 * L * ROW_B)
+                       : "memory");
+        ld_pending = true;
+        __syncthreads();
+        if (lane == 0 && (warp == 2 || warp == 3))
+          load_window(warp == 2 ? S.v : S.dO, warp == 2 ? box_qkv : box_dout, &S.bar_ld,
+                      (warp == 2 ? 2 * (int)C : 0) + nh_ * HD, win_load(g, nwin, nww, nwh), g);
+        if (tid < L) lse_next = __ldg(lse + (item + 1) * L + win_row(g, win_load(g, nwin, nww, nwh), tid));
+      }
+      // ---- D = rowsum(P dP) (four column groups combined through smem), then
+      // dS = P (dP - D) scale over P (rows of dead warps stay zero)
+      {
         const int c0 = 3 * cg, nch = max(0, min(3, NK / 16 - c0));
-        const float Ds = rvalid ? S.D[r] * g.scale : 0.f;
-        if (nch == 3) ds_chunks<3>(trow, S, rt, c0, g.scale, Ds);
-        else if (nch == 2) ds_chunks<2>(trow, S, rt, c0, g.scale, Ds);
-        else if (nch == 1) ds_chunks<1>(trow, S, rt, c0, g.scale, Ds);
+        float part = 0.f;
+        if (warp_live) {
+          if (nch == 3) part = pdp_dot<3>(trow, S, rt, c0);
+          else if (nch == 2) part = pdp_dot<2>(trow, S, rt, c0);
+          else if (nch == 1) part = pdp_dot<1>(trow, S, rt, c0);
+        }
+        S.red[cg][rt] = part;
+        __syncthreads();
+        if (warp_live) {
+          const float Ds = (S.red[0][rt] + S.red[1][rt] + S.red[2][rt] + S.red[3][rt]) * g.scale;
+          if (nch == 3) ds_chunks<3>(trow, S, rt, c0, g.scale, Ds);
+          else if (nch == 2) ds_chunks<2>(trow, S, rt, c0, g.scale, Ds);
+          else if (nch == 1) ds_chunks<1>(trow, S, rt, c0, g.scale, Ds);
+        }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
@@ -869,10 +983,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int kt = 0; kt < ntiles; ++kt)
           for (int ks = 0; ks < 8; ++ks)
             mma_ss(tmem + DK_COL + 64 * kt, desc_mn(S.ps + kt * PS_BLOCK + ks * 2048, PS_BLOCK),
-                   desc_mn(S.q + qb * ROW_B + ks * 2048, 16), id_mn, (t > 0 || ks > 0));
+                   desc_mn(qn + qb * ROW_B + ks * 2048, 16), id_mn, (t > 0 || ks > 0));
         for (int ks = 0; ks < NK / 16; ++ks)
           mma_ss(tmem + DQ_COL, desc_kmajor(S.ps + (ks >> 2) * PS_BLOCK + (ks & 3) * 32),
-                 desc_mn(S.k + ks * 2048, 16), id_q, ks > 0);
+                 desc_mn(kn + ks * 2048, 16), id_q, ks > 0);
         commit(&S.bar);
       }
       __syncwarp();
@@ -881,68 +995,108 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (!ok) break;
       NSW_STAMP();
       fence_after();
-      // ---- dQ epilogue (QK-norm backward of q)
+      // S of the next tile overlaps this tile's dQ epilogue (R is free: dP was consumed by dS)
+      if (t + 1 < ntiles && tid == 0) {
+        fence_after();
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_ss(tmem, desc_kmajor(qn + (NK - 128) * ROW_B + ks * 32), desc_kmajor(kn + ks * 32), id_s, ks > 0);
+        commit(&S.bar);
+      }
+      // the normalized q/k rows are free once the last tile's dK/dQ MMAs are done: gather the
+      // next item's raw rows into them
+      if (t == ntiles - 1 && has_next && lane == 0 && warp < 2)
+        load_window(warp == 0 ? qn : kn, box_qkv, &S.bar_ld, (warp == 0 ? 0 : (int)C) + nh_ * HD,
+                    win_load(g, nwin, nww, nwh), g);
+      // ---- dQ epilogue: TMEM -> fp32 staging in ps, then the QK-norm backward of q with eight
+      // threads per row and coalesced row stores
       {
-        float gq[16];
-        NormRow nr;
-        if (warp_live) ld16(trow + DQ_COL + 16 * cg, gq);
-        norm_bwd_phase1(nr, gq, S.xq, r, cg, wcol_q, rvalid);
-        S.red[cg][rt] = nr.dot;
-        __syncthreads();
-        const float dot = S.red[0][rt] + S.red[1][rt] + S.red[2][rt] + S.red[3][rt];
-        float wpart[16];
-        const int64_t off = rvalid ? (int64_t)S.tok[r] * g.qkv_stride + (int64_t)h * HD + 16 * cg : 0;
-        norm_bwd_phase2(nr, gq, wcol_q, rvalid ? S.rq[r] : 0.f, dot, dqkv + off, wpart, rvalid);
         if (warp_live) {
-          const int e = warp_reduce16(wpart, lane);
-          if ((lane & 1) == 0) atomicAdd(&S.wq[16 * cg + e], wpart[0]);
+          float gq[16];
+          ld16(trow + DQ_COL + 16 * cg, gq);
+          stage_f32(S.ps, rt, cg, gq);
         }
+        __syncthreads();
+        NSW_STAMP();
+        float wacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const int c = tid & 7;
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const int row = (tid >> 3) + 64 * k2;
+          const int rr = qb + row;
+          const bool valid = rr >= lo && rr < L;
+          __nv_bfloat16* dst = dqkv + (valid ? (int64_t)tok[rr] * g.qkv_stride : 0) + (int64_t)h * HD + 8 * c;
+          norm_bwd_task(S.ps, qx, S.qwv, row, rr, c, valid, valid ? S.rq[rr] : 0.f, dst, wacc);
+        }
+        NSW_STAMP();
+        flush_wacc(wacc, S.wq[warp], lane);
       }
       fence_before();
       __syncthreads();  // R, dQ, red and ps are reused by the next tile
       NSW_STAMP();
     }
     if (!ok) break;
-    // ---- dV, dK epilogues (key rows)
+    if (!ok) break;
+    // ---- dV, dK epilogues (key rows): dV through bf16 staging, dK through fp32 staging and the
+    // QK-norm backward of k, eight threads per row, coalesced row stores
     for (int kt = 0; kt < ntiles; ++kt) {
       const int kb = kt == 0 ? 0 : KT1;
       const int lo = kt * 128;
-      const int kr = kb + rt;
       const bool live = kb + lg * 32 + 31 >= lo && kb + lg * 32 < L;  // warp-uniform
-      const bool kvalid = kr >= lo && kr < L;
-      const int64_t row_off = kvalid ? (int64_t)S.tok[kr] * g.qkv_stride + (int64_t)h * HD + 16 * cg : 0;
-      {
-        float gv[16];
-        if (live) ld16(trow + DV_COL + 64 * kt + 16 * cg, gv);
-        if (kvalid) {
-          uint4* dv = reinterpret_cast<uint4*>(dqkv + row_off + 2 * C);
-          dv[0] = pack8<__nv_bfloat16>(gv);
-          dv[1] = pack8<__nv_bfloat16>(gv + 8);
-        }
-      }
-      float gk[16];
-      if (live) ld16(trow + DK_COL + 64 * kt + 16 * cg, gk);
-      NormRow nr;
-      norm_bwd_phase1(nr, gk, S.xk, kr, cg, wcol_k, kvalid);
-      S.red[cg][rt] = nr.dot;
-      __syncthreads();
-      const float dot = S.red[0][rt] + S.red[1][rt] + S.red[2][rt] + S.red[3][rt];
-      float wpart[16];
-      norm_bwd_phase2(nr, gk, wcol_k, kvalid ? S.rk[kr] : 0.f, dot, dqkv + row_off + C, wpart, kvalid);
+      unsigned char* st_v = S.ps + 2 * PS_BLOCK;
       if (live) {
-        const int e = warp_reduce16(wpart, lane);
-        if ((lane & 1) == 0) atomicAdd(&S.wk[16 * cg + e], wpart[0]);
+        float gv[16];
+        ld16(trow + DV_COL + 64 * kt + 16 * cg, gv);
+        *reinterpret_cast<uint4*>(st_v + swz(rt, 2 * cg)) = pack8<__nv_bfloat16>(gv);
+        *reinterpret_cast<uint4*>(st_v + swz(rt, 2 * cg + 1)) = pack8<__nv_bfloat16>(gv + 8);
+        float gk[16];
+        ld16(trow + DK_COL + 64 * kt + 16 * cg, gk);
+        stage_f32(S.ps, rt, cg, gk);
       }
-      __syncthreads();  // red is rewritten by the next key tile; wq/wk complete
+      __syncthreads();
+      NSW_STAMP();
+      float wacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const int c = tid & 7;
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int row = (tid >> 3) + 64 * k2;
+        const int kr = kb + row;
+        const bool valid = kr >= lo && kr < L;
+        const int64_t base_off = (valid ? (int64_t)tok[kr] * g.qkv_stride : 0) + (int64_t)h * HD + 8 * c;
+        if (valid)
+          *reinterpret_cast<uint4*>(dqkv + base_off + 2 * C) = *reinterpret_cast<const uint4*>(st_v + swz(row, c));
+        norm_bwd_task(S.ps, kx, S.kwv, row, kr, c, valid, valid ? S.rk[kr] : 0.f, dqkv + base_off + C, wacc);
+      }
+      NSW_STAMP();
+      flush_wacc(wacc, S.wk[warp], lane);
+      __syncthreads();  // the staging area is rewritten by the next key tile
+      NSW_STAMP();
     }
     fence_before();
-    NSW_STAMP();
-    if (tid < HD) {
-      dqw_part[item * HD + tid] = S.wq[tid];
-      dkw_part[item * HD + tid] = S.wk[tid];
+    __syncthreads();  // all warps' slots are complete
+    if (tid < 2 * HD) {
+      const int col = tid & (HD - 1);
+      float acc = 0.f;
+      if (tid < HD) {
+#pragma unroll
+        for (int w = 0; w < 16; ++w) acc += S.wq[w][col];
+        dqw_part[item * HD + col] = acc;
+      } else {
+#pragma unroll
+        for (int w = 0; w < 16; ++w) acc += S.wk[w][col];
+        dkw_part[item * HD + col] = acc;
+      }
     }
+    __syncthreads();  // slots are cleared by their warps at the next item's start
+    raw = 1 - raw;
+    tcur = ntab;
+    win = nwin;
+    mixed = mixed_n;
   }
 #undef NSW_STAMP
+  // after an error, let gathers still in flight land before the shared memory is released
+  // (bounded; a second timeout is not recorded again)
+  if (!ok && ld_pending && tid == 0) wait_bar(&S.bar_ld, ld_parity, nullptr);
   fence_before();
   __syncthreads();
   fence_after();
@@ -974,17 +1128,43 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [rows, cols] bf16 row-major with leading dimension ld; box = one row of 64 elements (gather4)
-bool row_gather_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+// 4-D view [B*T, H, W, ld] of a token-major bf16 tensor, box = [1, h, w, 64] (SWIZZLE_128B)
+bool box_map(CUtensorMap* map, const void* ptr, const AttnGeom& g, int64_t ld, int w, int h) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {64, 1};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  cuuint64_t dims[4] = {(cuuint64_t)ld, (cuuint64_t)g.W, (cuuint64_t)g.H, (cuuint64_t)g.B * g.T};
+  cuuint64_t strides[3] = {(cuuint64_t)(ld * 2), (cuuint64_t)(ld * 2 * g.W), (cuuint64_t)(ld * 2 * g.W * g.H)};
+  cuuint32_t box[4] = {64, (cuuint32_t)w, (cuuint32_t)h, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Split of a window dimension at the grid edge: first-part size of the one window column (row)
+// that wraps, 0 if none wraps (the grid is a whole number of windows, so all wrapping windows
+// split the same way).
+int wrap_split(int n, int wsize, int shift) {
+  for (int w0 = 0; w0 < n; w0 += wsize) {
+    int x0 = (w0 + shift) % n;
+    if (x0 < 0) x0 += n;
+    if (x0 + wsize > n) return n - x0;
+  }
+  return 0;
+}
+
+// The 3 x 3 box shapes {full, first part, second part} of width x height (see box_index).
+bool window_box_maps(attn_tc::BoxMaps* maps, const void* ptr, const AttnGeom& g, int64_t ld) {
+  const int ax = wrap_split(g.W, g.ww, g.sw), ay = wrap_split(g.H, g.wh, g.sh);
+  const int ws[3] = {g.ww, ax, g.ww - ax}, hs[3] = {g.wh, ay, g.wh - ay};
+  for (int yi = 0; yi < 3; ++yi)
+    for (int xi = 0; xi < 3; ++xi) {
+      CUtensorMap* m = &maps->m[yi * 3 + xi];
+      memset(m, 0, sizeof(*m));
+      if (ws[xi] <= 0 || hs[yi] <= 0 || ws[xi] > 256 || hs[yi] > 256) continue;
+      if (!box_map(m, ptr, g, ld, ws[xi], hs[yi])) return false;
+    }
+  return true;
 }
 }  // namespace
 
@@ -999,15 +1179,14 @@ cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw
   NSW_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t n_tok = (int64_t)g.B * g.T * g.H * g.W;
   if (n_tok >= (1LL << 31) - 1) return cudaErrorInvalidValue;
-  CUtensorMap m_qkv, m_dout, m_out;
-  if (!row_gather_map(&m_qkv, qkv, n_tok, g.qkv_stride, g.qkv_stride) ||
-      !row_gather_map(&m_dout, dout, n_tok, g.out_stride, g.out_stride) ||
-      !row_gather_map(&m_out, out, n_tok, g.out_stride, g.out_stride))
+  (void)out;  // D = rowsum(P dP) is formed in the kernel; O itself is not read
+  attn_tc::BoxMaps b_qkv, b_dout;
+  if (!window_box_maps(&b_qkv, qkv, g, g.qkv_stride) || !window_box_maps(&b_dout, dout, g, g.out_stride))
     return cudaErrorInvalidValue;
   const int64_t items = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww) * g.nh;
   const int grid = (int)std::min<int64_t>(items, sms);
-  k<<<grid, attn_tc::BWD_THREADS, smem, s>>>(m_qkv, m_dout, m_out, (const __nv_bfloat16*)qkv, qw, kw,
-                                             (const __nv_bfloat16*)out, (const __nv_bfloat16*)dout, lse,
+  k<<<grid, attn_tc::BWD_THREADS, smem, s>>>(b_qkv, b_dout, (const __nv_bfloat16*)qkv, qw, kw,
+                                             (const __nv_bfloat16*)dout, lse,
                                              (__nv_bfloat16*)dqkv, dqw_part, dkw_part, g, device_error_flag(),
                                              stamps);
   return cudaGetLastError();
