@@ -149,7 +149,7 @@ def bench_rmsnorm(a):
     ms = timeit(lambda: ext.rmsnorm_fwd(x, w, 1e-7), a.iters)
     report(f"rmsnorm_fwd {a.M}x{a.N}", ms, None, 4 * a.M * a.N)
     y, r = ext.rmsnorm_fwd(x, w, 1e-7)
-    ms = timeit(lambda: ext.rmsnorm_bwd(y, x, w, r), a.iters)
+    ms = timeit(lambda: ext.rmsnorm_bwd(y, x, w, r, 1e-7), a.iters)
     report(f"rmsnorm_bwd {a.M}x{a.N}", ms, None, 6 * a.M * a.N)
 
 

@@ -64,17 +64,20 @@ std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
   return {y, rstd};
 }
 
-std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
+// eps >= 0: the kernel recomputes rstd from x with this eps (the forward's value); else it reads rstd
+std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, double eps) {
   need_cuda(dy, "dy");
   need_cuda(x, "x");
   const int n = (int)x.size(-1);
   const int64_t rows = x.numel() / n;
   auto dx = torch::empty_like(x);
-  int parts = 3 * 148;
+  // one partial weight-gradient row per CTA: one persistent CTA per SM for the TMA kernel
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  int parts = nsw::rmsnorm_tma_supported(rows, n, dt_code(x)) ? sms : 3 * sms;
   if (rows < parts * 8) parts = (int)std::max<int64_t>(1, (rows + 7) / 8);
   auto part = torch::empty({parts, n}, x.options().dtype(at::kFloat));
   check(nsw::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(),
-                         dx.data_ptr(), part.data_ptr<float>(), parts, rows, n, dt_code(x), stream()),
+                         dx.data_ptr(), part.data_ptr<float>(), parts, rows, n, dt_code(x), stream(), (float)eps),
         "rmsnorm_bwd");
   return {dx, part.sum(0)};
 }
@@ -376,7 +379,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of neural_scaling_weather_b200";
   m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("eps") = -1.0);
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("res_period") = 0, py::arg("act") = 0, py::arg("preact") = py::none(), py::arg("out_f32") = false,
         py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false);

@@ -38,12 +38,26 @@ __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_
 template <>
 __device__ __forceinline__ float from_f<float>(float v) { return v; }
 
-// unpack/pack 8 16-bit floats from/to a uint4
+// unpack/pack 8 16-bit floats from/to a uint4.  The vector is taken by value: a reference to
+// a shared- or global-memory uint4 read through a 16-bit pointer can compile to eight 2-byte
+// loads (eight times the wavefronts, bank-conflicted) instead of one 16-byte load.
+__device__ __forceinline__ void unpack2(uint32_t w, float* f, __nv_bfloat16) {
+  f[0] = __uint_as_float(w << 16);
+  f[1] = __uint_as_float(w & 0xFFFF0000u);
+}
+__device__ __forceinline__ void unpack2(uint32_t w, float* f, __half) {
+  __half2 h;
+  memcpy(&h, &w, 4);
+  const float2 v = __half22float2(h);
+  f[0] = v.x;
+  f[1] = v.y;
+}
 template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  const T* h = reinterpret_cast<const T*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = to_f(h[i]);
+__device__ __forceinline__ void unpack8(const uint4 u, float* f) {
+  unpack2(u.x, f, T());
+  unpack2(u.y, f + 2, T());
+  unpack2(u.z, f + 4, T());
+  unpack2(u.w, f + 6, T());
 }
 template <typename T>
 __device__ __forceinline__ uint4 pack8(const float* f) {

@@ -152,6 +152,14 @@ __global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict
 
 cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n,
                         float eps, int dtype, cudaStream_t s) {
+  if (rmsnorm_tma_supported(rows, n, dtype))
+    return rmsnorm_fwd_tma(x, w, y, rstd, rows, n, eps, dtype, 2 * num_sms(), s);
+  return rmsnorm_fwd_rows(x, w, y, rstd, rows, n, eps, dtype, s);
+}
+
+// one warp per row, rows held in registers (fallback of the TMA version)
+cudaError_t rmsnorm_fwd_rows(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n,
+                             float eps, int dtype, cudaStream_t s) {
   if (n % 8 || n > 2048) return cudaErrorInvalidValue;
   const int threads = 256;
   int64_t blocks = (rows + 7) / 8;
@@ -175,7 +183,15 @@ cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int
 
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                         float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
-                        cudaStream_t s) {
+                        cudaStream_t s, float eps) {
+  if (rmsnorm_tma_supported(rows, n, dtype))
+    return rmsnorm_bwd_tma(dy, x, w, rstd, dx, dw_partial, partial_rows, rows, n, dtype, eps, s);
+  return rmsnorm_bwd_rows(dy, x, w, rstd, dx, dw_partial, partial_rows, rows, n, dtype, s);
+}
+
+cudaError_t rmsnorm_bwd_rows(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                             float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
+                             cudaStream_t s) {
   if (n % 8 || n > 2048) return cudaErrorInvalidValue;
   const int threads = 256;
   const size_t smem = (size_t)n * sizeof(float) * (threads / 32);

@@ -15,7 +15,7 @@ cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int
                         float eps, int dtype, cudaStream_t s);
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                         float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
-                        cudaStream_t s);
+                        cudaStream_t s, float eps = -1.f);
 
 // ---- elementwise epilogues -----------------------------------------------------
 // y = act(acc + bias) + residual (residual row index = row % res_period)
@@ -73,6 +73,21 @@ cudaError_t window_attn_fwd(const void* qkv, const float* qw, const float* kw, v
 bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype);
 cudaError_t window_attn_fwd_tc(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
                                const AttnGeom& g, cudaStream_t s);
+// RMSNorm, one warp per row with the row in registers (n <= 2048); rmsnorm_fwd/bwd use the TMA
+// version below where it applies and these otherwise
+cudaError_t rmsnorm_fwd_rows(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n,
+                             float eps, int dtype, cudaStream_t s);
+cudaError_t rmsnorm_bwd_rows(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                             float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
+                             cudaStream_t s);
+// RMSNorm with TMA bulk-copy row tiles (16-bit types, n % 8 == 0, n <= 4096)
+bool rmsnorm_tma_supported(int64_t rows, int n, int dtype);
+cudaError_t rmsnorm_fwd_tma(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n, float eps,
+                            int dtype, int grid, cudaStream_t s);
+// eps >= 0: rstd is recomputed from x (as the forward computed it); eps < 0: read from rstd
+cudaError_t rmsnorm_bwd_tma(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                            float* dw_partial, int partial_rows, int64_t rows, int n, int dtype, float eps,
+                            cudaStream_t s);
 cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw, const void* out,
                                const void* dout, const float* lse, void* dqkv, float* dqw_part, float* dkw_part,
                                const AttnGeom& g, cudaStream_t s, long long* stamps = nullptr);

@@ -76,6 +76,7 @@ class _RMSNorm(torch.autograd.Function):
         ctx.save_for_backward(x2, w, rstd)
         ctx.shape = x.shape
         ctx.in_dtype = x.dtype
+        ctx.eps = eps
         return y.view(x.shape)
 
     @staticmethod
@@ -83,7 +84,7 @@ class _RMSNorm(torch.autograd.Function):
         ext = require()
         x2, w, rstd = ctx.saved_tensors
         dy2 = dy.reshape(x2.shape).to(x2.dtype).contiguous()
-        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd)
+        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd, ctx.eps)
         return dx.view(ctx.shape).to(ctx.in_dtype), dw.to(w.dtype), None
 
 

@@ -19,6 +19,7 @@ SOURCES = [
     os.path.join(CSRC, "attention_tc.cu"),
     os.path.join(CSRC, "gemm_tcgen05.cu"),
     os.path.join(CSRC, "noalloc_rmsnorm.cu"),
+    os.path.join(CSRC, "rmsnorm_tma.cu"),
 ]
 
 NVCC_FLAGS = [

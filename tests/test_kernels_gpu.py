@@ -71,10 +71,12 @@ def test_gemm_epilogues(_ext_loaded):
 
 
 # --------------------------------------------------------------------------- RMSNorm
-@pytest.mark.parametrize("n", [64, 1024, 2048])
-def test_rmsnorm(n):
+@pytest.mark.parametrize("rows,n", [(333, 64), (333, 1024), (333, 2048), (777, 4096), (20011, 1024),
+                                    (70000, 1024)])
+def test_rmsnorm(rows, n):
+    """TMA row-tile kernels (ring of three tiles per CTA, partial last tile) against fp32."""
     torch.manual_seed(0)
-    x = torch.randn(333, n, device=DEV).bfloat16().requires_grad_()
+    x = torch.randn(rows, n, device=DEV).bfloat16().requires_grad_()
     w = (1 + 0.1 * torch.randn(n, device=DEV)).requires_grad_()
     y = ops.rms_norm(x, w)
     xr = x.detach().float().requires_grad_()
