@@ -96,15 +96,15 @@ def bench_block_gemms(a):
     g3 = torch.randn(M, 3 * E, **bf)
     pre = torch.empty(M, 4 * E, **bf)
     cases = [
-        ("fwd qkv +bias", lambda: ext.gemm(x, W["qkv"], b["qkv"]), M, 3 * E, E),
-        ("fwd proj +bias+res", lambda: ext.gemm(x, W["proj"], b["proj"], res), M, E, E),
-        ("fwd fc1 +bias+gelu(+preact)", lambda: ext.gemm(x, W["fc1"], b["fc1"], None, 0, 1, pre), M, 4 * E, E),
-        ("fwd fc2 +bias+res", lambda: ext.gemm(h4, W["fc2"], b["fc2"], res), M, E, 4 * E),
-        ("dgrad qkv", lambda: ext.gemm(g3, Wt["qkv"]), M, E, 3 * E),
-        ("dgrad proj", lambda: ext.gemm(x, Wt["proj"]), M, E, E),
-        ("dgrad fc2 *gelu'(u)", lambda: ext.gemm(x, Wt["fc2"], None, u, 0, 2), M, 4 * E, E),
-        ("dgrad fc2 plain", lambda: ext.gemm(x, Wt["fc2"]), M, 4 * E, E),
-        ("dgrad fc1", lambda: ext.gemm(h4, Wt["fc1"]), M, E, 4 * E),
+        ("fwd qkv +bias", lambda: ext.gemm(x, W["qkv"], b["qkv"], impl=a.impl), M, 3 * E, E),
+        ("fwd proj +bias+res", lambda: ext.gemm(x, W["proj"], b["proj"], res, impl=a.impl), M, E, E),
+        ("fwd fc1 +bias+gelu(+preact)", lambda: ext.gemm(x, W["fc1"], b["fc1"], None, 0, 1, pre, impl=a.impl), M, 4 * E, E),
+        ("fwd fc2 +bias+res", lambda: ext.gemm(h4, W["fc2"], b["fc2"], res, impl=a.impl), M, E, 4 * E),
+        ("dgrad qkv", lambda: ext.gemm(g3, Wt["qkv"], impl=a.impl), M, E, 3 * E),
+        ("dgrad proj", lambda: ext.gemm(x, Wt["proj"], impl=a.impl), M, E, E),
+        ("dgrad fc2 *gelu'(u)", lambda: ext.gemm(x, Wt["fc2"], None, u, 0, 2, impl=a.impl), M, 4 * E, E),
+        ("dgrad fc2 plain", lambda: ext.gemm(x, Wt["fc2"], impl=a.impl), M, 4 * E, E),
+        ("dgrad fc1", lambda: ext.gemm(h4, Wt["fc1"], impl=a.impl), M, E, 4 * E),
         ("wgrad fc1 cublas", lambda: torch.mm(h4.t(), x, out_dtype=torch.float32), 4 * E, E, M),
     ]
     tot = 0.0
@@ -190,7 +190,9 @@ def main():
     ap.add_argument("--epilogue", default="bias", choices=["none", "bias", "gelu", "residual"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true")
-    ap.add_argument("--impl", type=int, default=0, help="attention: 1 = mma.sync only, 2 = tcgen05 only")
+    ap.add_argument("--impl", type=int, default=0,
+                    help="attention: 1 = mma.sync only, 2 = tcgen05 only; block GEMMs: 1 = one CTA per tile, "
+                         "2 = CTA pair, 0 = default dispatch")
     a = ap.parse_args()
     if a.kernel in ("gemm", "all"):
         bench_gemm(a)

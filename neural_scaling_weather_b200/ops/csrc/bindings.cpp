@@ -85,7 +85,7 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, doub
 // ------------------------------------------------------------------------------ GEMM
 Tensor gemm(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor> residual,
             int64_t res_period, int64_t act, c10::optional<Tensor> preact, bool out_f32, double alpha,
-            c10::optional<Tensor> out, bool accumulate) {
+            c10::optional<Tensor> out, bool accumulate, int64_t impl) {
   need_cuda(A, "A");
   need_cuda(B, "B");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm: A [M,K], B [N,K]");
@@ -126,7 +126,7 @@ Tensor gemm(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor
   g.alpha = (float)alpha;
   g.accumulate = accumulate ? 1 : 0;
   TORCH_CHECK(nsw::gemm_tcgen05_supported(g), "gemm: shape/alignment not supported by the tcgen05 kernel");
-  check(nsw::gemm_tcgen05(g, stream()), "gemm_tcgen05");
+  check(nsw::gemm_tcgen05(g, stream(), (int)impl), "gemm_tcgen05");
   return D;
 }
 
@@ -383,7 +383,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("eps") = -1.0);
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("res_period") = 0, py::arg("act") = 0, py::arg("preact") = py::none(), py::arg("out_f32") = false,
-        py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false);
+        py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("impl") = 0);
   m.def("gemm_supported", &gemm_supported);
   m.def("bias_act_residual", &bias_act_residual);
   m.def("gelu_bwd", &gelu_bwd);

@@ -23,6 +23,8 @@
 // word, stops issuing work, and still frees its TMEM before returning.
 #include <cuda.h>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -33,7 +35,12 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // bf16: 128 bytes = one swizzle row
 constexpr int kEpiWarps = 8;                   // 2 warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
-constexpr int kStageRow = 40;                   // staging row stride (elements): 32 + 8 pad
+constexpr int kStageRow = 32;                   // staging row: 32 elements (64 bytes)
+
+// element offset of 16-byte chunk c (0..3) of staging row r: chunk c ^ ((r >> 1) & 3), the TMA
+// SWIZZLE_64B pattern for 64-byte rows (buffers are 512-byte aligned); a warp writing one row per
+// lane, or reading 4 chunks of 8 rows, hits distinct banks
+__device__ __forceinline__ int stg_off(int r, int c) { return r * kStageRow + ((c ^ ((r >> 1) & 3)) << 3); }
 constexpr unsigned long long kWaitBudgetNs = 4000000000ull;  // 4 s
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -129,6 +136,41 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.ld without the wait, and the wait with the loaded registers as in-out operands so no
+// use of them can be scheduled before it (double-buffered TMEM reads in the epilogue)
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// TMA store of a 32 x 32 tile (SWIZZLE_64B staging in smem) and its bulk-group bookkeeping
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -137,6 +179,9 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 struct EpiParams {
+  CUtensorMap map_d;    // TMA store maps (32 x 32 box, SWIZZLE_64B) of D and the pre-activation;
+  CUtensorMap map_pre;  // used when tma_out is set (16-bit D, N % 8 == 0)
+  int tma_out;
   void* D;
   int64_t M, N, ldd;
   const float* bias;
@@ -149,6 +194,183 @@ struct EpiParams {
   float alpha;
 };
 
+// Epilogue of one warp for one accumulator tile: rows [row_base, row_base + 32) (the warp's
+// TMEM lane quadrant) and columns [n0 + half * BN/2, n0 + (half + 1) * BN/2).
+template <typename T, int BN>
+struct EpiWarp {
+  static constexpr int kChunks = BN / 64;
+  uint4 pre_res[kChunks][4];
+
+  // Residual / aux prefetch into registers, issued before the accumulator wait.
+  __device__ __forceinline__ void prefetch(const EpiParams& ep, int64_t row_base, int64_t n0, int half, int lane) {
+    // Prefetch this warp's residual/aux strip (32 rows x BN/2 columns) into registers in
+    // the coalesced layout (lane -> row sub_r + 8 i, 8-column group sub_c) BEFORE waiting
+    // for the accumulator, so the global latency hides behind this tile's MMAs.
+    const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
+    const bool res_vec = ep.residual != nullptr && !ep.out_f32;
+    if (res_vec) {
+#pragma unroll
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int64_t nbp = n0 + (half * kChunks + cc) * 32;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int64_t rr = row_base + sub_r + 8 * i;
+          pre_res[cc][i] = make_uint4(0, 0, 0, 0);
+          if (rr < ep.M && nbp + 32 <= ep.N)
+            pre_res[cc][i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                            (rr % ep.res_period) * ep.ldr + nbp + sub_c);
+        }
+      }
+    }
+  }
+
+  // TMEM -> registers -> fused bias / GELU / residual -> stores.  Full 32-column chunks of a
+  // 16-bit D leave through TMA stores: the warp writes the chunk into one of its two 2 KB staging
+  // buffers (32 rows x 64 bytes, SWIZZLE_64B) and lane 0 issues one bulk tensor store, so no
+  // lane loads the tile back or issues global stores; the TMEM read of the next chunk is in
+  // flight meanwhile.  `ring` counts this warp's staging uses across tiles.
+  __device__ __forceinline__ void drain(const EpiParams& ep, T* stg, uint32_t t_row, int64_t row_base, int64_t n0,
+                                        int half, int lane, uint32_t& ring) {
+    const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
+    const int64_t row = row_base + lane;
+    const bool row_ok = row < ep.M;
+    uint32_t r[2][32];
+    tmem_ld32_async(t_row + (uint32_t)(half * kChunks * 32), r[0]);
+    tmem_wait_ld(r[0]);
+#pragma unroll
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = half * kChunks + cc;
+      uint32_t* rc = r[cc & 1];
+      if (cc + 1 < kChunks) tmem_ld32_async(t_row + (uint32_t)((c + 1) * 32), r[(cc + 1) & 1]);
+      const int64_t nb = n0 + c * 32;
+      if (nb < ep.N) {  // warp-uniform
+        const bool full = nb + 32 <= ep.N;
+        float f[32];
+        if (ep.alpha != 1.f) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(rc[j]) * ep.alpha;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(rc[j]);
+        }
+        if (ep.bias) {
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const float4 b4 = __ldg(reinterpret_cast<const float4*>(ep.bias + nb) + v);
+              f[4 * v] += b4.x;
+              f[4 * v + 1] += b4.y;
+              f[4 * v + 2] += b4.z;
+              f[4 * v + 3] += b4.w;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < ep.N) f[j] += ep.bias[nb + j];
+          }
+        }
+        if (!full || ep.out_f32 || !ep.tma_out) {
+          direct_stores(ep, f, row, row_ok, nb, full);
+        } else {
+          const int m_tile = (int)row_base, n_tile = (int)nb;
+          if (ep.preact) stage_store(&ep.map_pre, f, stg, lane, n_tile, m_tile, ring);
+          if (ep.act == 1) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
+          }
+          if (ep.residual) {
+            // coalesced prefetch layout -> this lane's row, through a staging buffer
+            T* buf = stg + (ring & 1) * (32 * kStageRow);
+            if (lane == 0) bulk_wait_read_1();
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              *reinterpret_cast<uint4*>(buf + stg_off(sub_r + 8 * i, sub_c >> 3)) = pre_res[cc][i];
+            __syncwarp();
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float rr8[8];
+              unpack8<T>(*reinterpret_cast<const uint4*>(buf + stg_off(lane, v)), rr8);
+              if (ep.act == 2) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[8 * v + j] *= gelu_grad_fast(rr8[j]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
+              }
+            }
+            __syncwarp();
+          }
+          stage_store(&ep.map_d, f, stg, lane, n_tile, m_tile, ring);
+        }
+      }
+      if (cc + 1 < kChunks) tmem_wait_ld(r[(cc + 1) & 1]);
+    }
+  }
+
+  // This lane's row of a 32-column chunk into the next staging buffer, then one TMA store.
+  __device__ __forceinline__ static void stage_store(const CUtensorMap* map, const float* f, T* stg, int lane,
+                                                     int n_tile, int m_tile, uint32_t& ring) {
+    T* buf = stg + (ring & 1) * (32 * kStageRow);
+    if (lane == 0) bulk_wait_read_1();  // the store that last used this buffer has read it
+    __syncwarp();
+#pragma unroll
+    for (int v = 0; v < 4; ++v) *reinterpret_cast<uint4*>(buf + stg_off(lane, v)) = pack8<T>(&f[8 * v]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) tma_store_2d(map, buf, n_tile, m_tile);
+    ++ring;
+  }
+
+  // Ragged column edge, fp32 output, or no TMA maps: per-row stores of this lane's row.
+  __device__ __forceinline__ void direct_stores(const EpiParams& ep, float* f, int64_t row, bool row_ok, int64_t nb,
+                                                bool full) {
+    if (!row_ok) return;
+    if (ep.preact) {
+      T* pp = reinterpret_cast<T*>(ep.preact) + row * ep.ldd + nb;
+      for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(f[j]);
+    }
+    if (ep.act == 1) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
+    }
+    if (ep.residual) {
+      const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
+      if (ep.act == 2) {
+        for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] *= gelu_grad_fast(to_f(rp[j]));
+      } else {
+        for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
+      }
+    }
+    if (ep.out_f32) {
+      float* dp = reinterpret_cast<float*>(ep.D) + row * ep.ldd + nb;
+      if (full) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          float4 o = make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
+          if (ep.accumulate) {
+            const float4 old = reinterpret_cast<float4*>(dp)[v];
+            o.x += old.x;
+            o.y += old.y;
+            o.z += old.z;
+            o.w += old.w;
+          }
+          reinterpret_cast<float4*>(dp)[v] = o;
+        }
+      } else {
+        for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = ep.accumulate ? dp[j] + f[j] : f[j];
+      }
+    } else {
+      T* dp = reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb;
+      if (full) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dp)[v] = pack8<T>(&f[8 * v]);
+      } else {
+        for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = from_f<T>(f[j]);
+      }
+    }
+  }
+};
+
 template <typename T, int BN, int STAGES>
 struct Smem {
   alignas(1024) T a[STAGES][BM * BK];
@@ -157,7 +379,7 @@ struct Smem {
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
-  alignas(16) T stage[kEpiWarps][32 * kStageRow];
+  alignas(1024) T stage[kEpiWarps][2 * 32 * kStageRow];  // two 2 KB staging buffers per epilogue warp
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -165,7 +387,8 @@ struct Smem {
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                int64_t M, int64_t N, int64_t K, EpiParams ep, uint32_t idesc, int* err) {
+                int64_t M, int64_t N, int64_t K, const __grid_constant__ EpiParams ep, uint32_t idesc,
+                int* err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // align the working area to 1024 B (the swizzle atom)
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -267,160 +490,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;         // TMEM lane quadrant this warp may access
     const int half = ew >> 2;       // which half of the BN columns
     T* stg = S.stage[ew];
+    uint32_t ring = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int64_t m0 = (tile / n_tiles) * BM;
       const int64_t n0 = (tile % n_tiles) * BN;
       const int64_t row_base = m0 + q * 32;
-      const int64_t row = row_base + lane;
-      const bool row_ok = row < ep.M;
-      // Prefetch this warp's residual/aux strip (32 rows x BN/2 columns) into registers in
-      // the coalesced layout (lane -> row sub_r + 8 i, 8-column group sub_c) BEFORE waiting
-      // for the accumulator, so the global latency hides behind this tile's MMAs.
-      constexpr int kChunks = BN / 64;
-      const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
-      uint4 pre_res[kChunks][4];
-      const bool res_vec = ep.residual != nullptr && !ep.out_f32;
-      if (res_vec) {
-#pragma unroll
-        for (int cc = 0; cc < kChunks; ++cc) {
-          const int64_t nbp = n0 + (half * kChunks + cc) * 32;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int64_t rr = row_base + sub_r + 8 * i;
-            pre_res[cc][i] = make_uint4(0, 0, 0, 0);
-            if (rr < ep.M && nbp + 32 <= ep.N)
-              pre_res[cc][i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
-                                                              (rr % ep.res_period) * ep.ldr + nbp + sub_c);
-          }
-        }
-      }
+      EpiWarp<T, BN> epi;
+      epi.prefetch(ep, row_base, n0, half, lane);
       if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int c = half * kChunks + cc;
-        uint32_t r[32];
-        tmem_ld32(t_row + (uint32_t)(c * 32), r);
-        const int64_t nb = n0 + c * 32;
-        if (nb >= ep.N) continue;  // warp-uniform
-        const bool full = nb + 32 <= ep.N;
-        float f[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) * ep.alpha;
-        if (ep.bias) {
-          if (full) {
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              const float4 b4 = __ldg(reinterpret_cast<const float4*>(ep.bias + nb) + v);
-              f[4 * v] += b4.x;
-              f[4 * v + 1] += b4.y;
-              f[4 * v + 2] += b4.z;
-              f[4 * v + 3] += b4.w;
-            }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < ep.N) f[j] += ep.bias[nb + j];
-          }
-        }
-        if (!full || ep.out_f32) {
-          // ragged column edge or fp32 output: direct per-row stores
-          if (row_ok) {
-            if (ep.preact) {
-              T* pp = reinterpret_cast<T*>(ep.preact) + row * ep.ldd + nb;
-              for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(f[j]);
-            }
-            if (ep.act == 1) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
-            }
-            if (ep.residual) {
-              const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
-              if (ep.act == 2) {
-                for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] *= gelu_grad_fast(to_f(rp[j]));
-              } else {
-                for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
-              }
-            }
-            if (ep.out_f32) {
-              float* dp = reinterpret_cast<float*>(ep.D) + row * ep.ldd + nb;
-              if (full) {
-#pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                  float4 o = make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
-                  if (ep.accumulate) {
-                    const float4 old = reinterpret_cast<float4*>(dp)[v];
-                    o.x += old.x;
-                    o.y += old.y;
-                    o.z += old.z;
-                    o.w += old.w;
-                  }
-                  reinterpret_cast<float4*>(dp)[v] = o;
-                }
-              } else {
-                for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = ep.accumulate ? dp[j] + f[j] : f[j];
-              }
-            } else {
-              T* dp = reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb;
-              for (int j = 0; j < 32 && nb + j < ep.N; ++j) dp[j] = from_f<T>(f[j]);
-            }
-          }
-          continue;
-        }
-        // ---- full 32-column chunk, 16-bit output: staged, coalesced
-        // lane l moves 16 bytes of row (l / 4 + 8 i), 8-column group (l % 4)
-        if (ep.preact) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            *reinterpret_cast<uint4*>(stg + lane * kStageRow + 8 * v) = pack8<T>(&f[8 * v]);
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int rr = sub_r + 8 * i;
-            if (row_base + rr < ep.M)
-              *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.preact) + (row_base + rr) * ep.ldd + nb + sub_c) =
-                  *reinterpret_cast<const uint4*>(stg + rr * kStageRow + sub_c);
-          }
-          __syncwarp();
-        }
-        if (ep.act == 1) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
-        }
-        if (ep.residual) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            *reinterpret_cast<uint4*>(stg + (sub_r + 8 * i) * kStageRow + sub_c) = pre_res[cc][i];
-          __syncwarp();
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            float rr8[8];
-            unpack8<T>(*reinterpret_cast<const uint4*>(stg + lane * kStageRow + 8 * v), rr8);
-            if (ep.act == 2) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) f[8 * v + j] *= gelu_grad_fast(rr8[j]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
-            }
-          }
-          __syncwarp();
-        }
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          *reinterpret_cast<uint4*>(stg + lane * kStageRow + 8 * v) = pack8<T>(&f[8 * v]);
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int rr = sub_r + 8 * i;
-          if (row_base + rr < ep.M)
-            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + (row_base + rr) * ep.ldd + nb + sub_c) =
-                *reinterpret_cast<const uint4*>(stg + rr * kStageRow + sub_c);
-        }
-        __syncwarp();
-      }
+      epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half, lane,
+                ring);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);
@@ -429,6 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) bulk_wait_all();  // the warp's TMA stores have completed
   }
 
   tc_fence_before();
@@ -437,6 +520,222 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
   }
+}
+
+
+// ============================================================================ 2-SM GEMM
+// A CTA pair (cluster of 2 on neighbouring SMs) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2: each CTA loads its own 128 rows of A and its 128-row half of B (plain
+// TMA loads into its own shared memory, no multicast) and receives 128 x 256 accumulator rows in
+// its own TMEM.  Per SM, an MMA of the pair reads 8 KB of operands per K=16 step instead of 12 KB
+// for a 128 x 256 single-CTA tile, which keeps the tensor core's operand reads plus the TMA writes
+// within the SM's shared-memory bandwidth.
+//   leader (rank 0): warp 1 issues every MMA of the pair and commits, multicast to both CTAs,
+//     the stage-free barriers and the accumulator-ready barrier;
+//   both CTAs: warp 0 is the TMA producer (its bytes complete the LEADER's stage barrier, which
+//     the leader arms with both CTAs' byte count); warps 2-9 drain their CTA's accumulator
+//     exactly as the single-CTA kernel does and release it on the leader's barrier.
+constexpr int BM2 = 256;  // rows of a pair tile (128 per CTA)
+constexpr int BN2 = 256;  // columns of a pair tile (B rows: 128 per CTA)
+
+template <typename T, int STAGES>
+struct Smem2 {
+  alignas(1024) T a[STAGES][BM * BK];
+  alignas(1024) T b[STAGES][(BN2 / 2) * BK];
+  uint64_t full[STAGES];    // leader: both CTAs' TMA bytes of a stage have landed
+  uint64_t empty[STAGES];   // each CTA: the pair's MMAs are done with this stage
+  uint64_t tmem_full[2];    // each CTA: accumulator ready
+  uint64_t tmem_empty[2];   // leader: all 2 x kEpiWarps epilogue warps released the accumulator
+  uint64_t done;            // each CTA: the peer has finished its last tile
+  alignas(1024) T stage[kEpiWarps][2 * 32 * kStageRow];  // two 2 KB staging buffers per epilogue warp
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// TMA load into this CTA's smem whose completion is counted on an mbarrier of either CTA of the pair
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void umma2_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+// arrive on the barrier at this offset in both CTAs of the pair once the pair's MMAs are done
+__device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((unsigned short)0x3)
+      : "memory");
+}
+
+template <typename T, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 int64_t M, int64_t N, int64_t K, const __grid_constant__ EpiParams ep, uint32_t idesc,
+                int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto& S = *reinterpret_cast<Smem2<T, STAGES>*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int64_t m_tiles = (M + BM2 - 1) / BM2;
+  const int64_t n_tiles = (N + BN2 - 1) / BN2;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (int)((K + BK - 1) / BK);
+  volatile int* abort_flag = &S.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&S.tmem_full[a], 1);
+      mbar_init(&S.tmem_empty[a], 2 * kEpiWarps);
+    }
+    mbar_init(&S.done, 1);
+    S.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  if (warp == 1) {  // both CTAs take part in the pair's allocation
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+                 "r"(2 * BN2));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barrier initialisation and the TMEM address are visible to both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = map_rank(&S.full[0], 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
+        const int m0 = (int)((tile / n_tiles) * BM2) + (int)rank * BM;
+        const int nb0 = (int)((tile % n_tiles) * BN2) + (int)rank * (BN2 / 2);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&S.empty[stage], phase ^ 1, abort_flag, err)) break;
+          if (rank == 0) mbar_expect_tx(&S.full[stage], (uint32_t)(2 * (BM + BN2 / 2) * BK * sizeof(T)));
+          tma_load_2d_pair(S.a[stage], &map_a, full_leader + 8u * stage, kb * BK, m0);
+          tma_load_2d_pair(S.b[stage], &map_b, full_leader + 8u * stage, kb * BK, nb0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int64_t tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
+        if (!mbar_wait(&S.tmem_empty[acc], acc_phase ^ 1, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN2);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&S.full[stage], phase, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma2_f16(d_tmem, smem_desc_sw128(&S.a[stage][k * 16]), smem_desc_sw128(&S.b[stage][k * 16]), idesc,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          umma2_commit_both(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma2_commit_both(&S.tmem_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;
+    T* stg = S.stage[ew];
+    uint32_t ring = 0;
+    const uint32_t empty_leader = map_rank(&S.tmem_empty[0], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
+      const int64_t m0 = (tile / n_tiles) * BM2 + (int64_t)rank * BM;
+      const int64_t n0 = (tile % n_tiles) * BN2;
+      const int64_t row_base = m0 + q * 32;
+      EpiWarp<T, BN2> epi;
+      epi.prefetch(ep, row_base, n0, half, lane);
+      if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
+      tc_fence_after();
+      epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN2), row_base, n0, half, lane,
+                ring);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(empty_leader + 8u * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_all();  // the warp's TMA stores have completed
+  }
+
+  // teardown: both CTAs are past their last tile before the pair's TMEM is released
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(map_rank(&S.done, rank ^ 1u));
+    int never = 0;
+    mbar_wait(&S.done, 0, &never, err);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN2));
 }
 
 // ---------------------------------------------------------------------------- host side
@@ -483,12 +782,25 @@ static int sm_count() {
   return n;
 }
 
-template <typename T, int BN, int STAGES>
-static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
-  if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN, a.dtype)) return cudaErrorInvalidValue;
+// [M, N] 16-bit output with leading dimension ld: box of 32 x 32 elements, 64-byte swizzle
+static bool make_store_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int64_t ld, int dtype) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static EpiParams epi_params(const GemmArgs& a) {
   EpiParams ep;
+  memset(&ep, 0, sizeof(ep));
+  ep.tma_out = !a.out_f32 && make_store_map(&ep.map_d, a.D, a.M, a.N, a.ldd, a.dtype) &&
+               (!a.preact || make_store_map(&ep.map_pre, a.preact, a.M, a.N, a.ldd, a.dtype));
   ep.D = a.D;
   ep.M = a.M;
   ep.N = a.N;
@@ -502,6 +814,54 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   ep.out_f32 = a.out_f32;
   ep.accumulate = a.accumulate;
   ep.alpha = a.alpha;
+  return ep;
+}
+
+// CTA-pair GEMM: cluster launch of 2 x (co-resident pairs, capped at the tile count)
+template <typename T, int STAGES>
+static cudaError_t launch2(const GemmArgs& a, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
+  if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN2 / 2, a.dtype)) return cudaErrorInvalidValue;
+  const EpiParams ep = epi_params(a);
+  const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
+  const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN2 >> 3) << 17) |
+                         ((uint32_t)(BM2 >> 4) << 24);
+  const size_t smem = sizeof(Smem2<T, STAGES>) + 1024;
+  auto k = gemm2_kernel<T, STAGES>;
+  NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t tiles = ((a.M + BM2 - 1) / BM2) * ((a.N + BN2 - 1) / BN2);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(sm_count() & ~1, 1, 1);
+  static int max_pairs = 0;  // co-resident clusters of this kernel (same for every shape)
+  if (!max_pairs) {
+    int n = 0;
+    NSW_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, k, &cfg));
+    max_pairs = n > 0 ? n : 1;
+  }
+  int pairs = max_pairs;
+  if (tiles < pairs) pairs = (int)tiles;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  NSW_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag()));
+  return cudaGetLastError();
+}
+
+template <typename T, int BN, int STAGES>
+static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
+  if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN, a.dtype)) return cudaErrorInvalidValue;
+  const EpiParams ep = epi_params(a);
   const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
   const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                          ((uint32_t)(BM >> 4) << 24);
@@ -529,12 +889,21 @@ int gemm_tcgen05_supported(const GemmArgs& a) {
   return tc::get_encode() != nullptr;
 }
 
-cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s) {
+// impl: 0 = default, 1 = single CTA, 2 = CTA pair.  The default takes the CTA pair for wide
+// GEMMs whose epilogue is light (bias only): there the pair's lower shared-memory traffic per
+// MMA wins; with GELU / pre-activation / residual epilogues the single-CTA kernel is faster
+// (measured at 64800 x 4096 x 1024), since a pair reuses an accumulator only when both CTAs'
+// epilogues have drained it.
+cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl) {
   if (!gemm_tcgen05_supported(a)) return cudaErrorInvalidValue;
   const bool wide = a.N > 128;
+  const bool light = a.act == 0 && !a.residual && !a.preact;
+  const bool pair = impl == 2 || (impl == 0 && wide && a.M > tc::BM && light);
   if (a.dtype == kBF16) {
+    if (pair) return tc::launch2<__nv_bfloat16, 6>(a, s);
     return wide ? tc::launch<__nv_bfloat16, 256, 4>(a, s) : tc::launch<__nv_bfloat16, 128, 6>(a, s);
   }
+  if (pair) return tc::launch2<__half, 6>(a, s);
   return wide ? tc::launch<__half, 256, 4>(a, s) : tc::launch<__half, 128, 6>(a, s);
 }
 

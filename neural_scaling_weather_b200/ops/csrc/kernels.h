@@ -112,7 +112,7 @@ struct GemmArgs {
   float alpha;
   int accumulate;       // D += result (fp32 output only)
 };
-cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s);
+cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl = 0);
 int gemm_tcgen05_supported(const GemmArgs& a);
 
 }  // namespace nsw

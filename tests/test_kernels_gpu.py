@@ -34,16 +34,19 @@ def rel(a, b):
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (300, 1120, 1168), (1000, 3072, 1024),
                                    (777, 128, 64), (129, 40, 96), (4096, 4096, 1024)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_gemm_plain(M, N, K, dtype, _ext_loaded):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_gemm_plain(M, N, K, dtype, impl, _ext_loaded):
+    """impl 1: one CTA per 128 x BN tile; impl 2: CTA pair (cta_group::2) per 256 x 256 tile."""
     torch.manual_seed(0)
     a = torch.randn(M, K, device=DEV, dtype=dtype)
     b = torch.randn(N, K, device=DEV, dtype=dtype)
-    d = _ext_loaded.gemm(a, b)
+    d = _ext_loaded.gemm(a, b, impl=impl)
     ref = a.float() @ b.float().t()
     assert rel(d, ref) < 1e-2
 
 
-def test_gemm_epilogues(_ext_loaded):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_gemm_epilogues(impl, _ext_loaded):
     torch.manual_seed(1)
     M, N, K = 515, 512, 256
     a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
@@ -51,22 +54,22 @@ def test_gemm_epilogues(_ext_loaded):
     bias = torch.randn(N, device=DEV)
     res = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
     pre = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    y = _ext_loaded.gemm(a, b, bias, None, 0, 1, pre)
+    y = _ext_loaded.gemm(a, b, bias, None, 0, 1, pre, impl=impl)
     u = a.float() @ b.float().t() + bias
     assert rel(pre, u) < 1e-2
     assert rel(y, torch.nn.functional.gelu(u)) < 1e-2
-    y2 = _ext_loaded.gemm(a, b, bias, res)
+    y2 = _ext_loaded.gemm(a, b, bias, res, impl=impl)
     assert rel(y2, u + res.float()) < 1e-2
     # broadcast residual (period)
     pos = torch.randn(128, N, device=DEV, dtype=torch.bfloat16)
     a3 = a[:512].contiguous()
-    y3 = _ext_loaded.gemm(a3, b, None, pos, 128)
+    y3 = _ext_loaded.gemm(a3, b, None, pos, 128, impl=impl)
     ref3 = (a3.float() @ b.float().t()).view(4, 128, N) + pos.float()
     assert rel(y3, ref3.view(512, N)) < 1e-2
     # fp32 output with accumulation
     out = torch.randn(M, N, device=DEV)
     base = out.clone()
-    _ext_loaded.gemm(a, b, None, None, 0, 0, None, True, 0.5, out, True)
+    _ext_loaded.gemm(a, b, None, None, 0, 0, None, True, 0.5, out, True, impl=impl)
     assert rel(out, base + 0.5 * (a.float() @ b.float().t())) < 1e-3
 
 
