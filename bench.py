@@ -295,11 +295,13 @@ def kernel_breakdown(fn, path):
     for ev in prof.events():
         if ev.device_type is not None and "CUDA" in str(ev.device_type):
             name = ev.name
-            for key in ("gemm_kernel", "fwd_kernel", "bwd_kernel", "rmsnorm", "adamw", "col_sum", "gelu",
-                        "sse", "im2col", "col2im", "unpatchify", "patchify", "sumsq", "nvjet", "gemm",
-                        "elementwise", "reduce", "copy", "fill", "cat"):
+            own = "nsw::" in ev.name
+            keys = ("rms_tma", "rmsnorm", "attn_tc::fwd", "attn_tc::bwd", "attn::fwd", "attn::bwd", "gemm2_kernel",
+                    "gemm_kernel", "adamw", "col_sum", "gelu", "sse", "im2col", "col2im", "unpatchify", "patchify",
+                    "sumsq", "nvjet") if own else ("nvjet",)
+            for key in keys:
                 if key in name:
-                    name = key + ("(own)" if "nsw::" in ev.name else "")
+                    name = key + ("(own)" if own else "")
                     break
             t = ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
             c, tt = agg.get(name, (0, 0.0))

@@ -26,6 +26,28 @@ def trunc_normal_(t: torch.Tensor, std: float = 0.02, mean: float = 0.0,
     return nn.init.trunc_normal_(t, mean=mean, std=std, a=a, b=b)
 
 
+def drop_path(x: torch.Tensor, drop_prob: float = 0.0, training: bool = False) -> torch.Tensor:
+    """Stochastic depth per sample (timm's ``drop_path``; reference ``models/timm_helpers.py``,
+    unused by the Swin blocks there as here): zero whole samples with probability ``drop_prob``
+    and rescale the rest by ``1 / (1 - drop_prob)``."""
+    if drop_prob == 0.0 or not training:
+        return x
+    keep = 1.0 - drop_prob
+    mask = x.new_empty((x.shape[0],) + (1,) * (x.ndim - 1)).bernoulli_(keep)
+    return x * mask / keep
+
+
+class DropPath(nn.Module):
+    """Module form of :func:`drop_path`."""
+
+    def __init__(self, drop_prob: float = 0.0):
+        super().__init__()
+        self.drop_prob = drop_prob
+
+    def forward(self, x):
+        return drop_path(x, self.drop_prob, self.training)
+
+
 def _meta(sharded, shared, reduce):
     return {"sharded": list(sharded), "shared": list(shared), "reduce": list(reduce)}
 
