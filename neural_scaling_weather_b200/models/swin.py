@@ -196,10 +196,18 @@ class Block(nn.Module):
 
     def forward(self, x: torch.Tensor, condition: Optional[torch.Tensor] = None) -> torch.Tensor:
         """x: (B, T, H, W, C) -> same shape."""
-        h = self.norm1(x)
-        x = self._shifted_window_attn(h, x)
-        h = self.norm2(x)
-        return self.mlp(h, residual=x)
+        # each pre-norm and its skip connection come from one node, so the two gradients of
+        # the residual stream are summed inside the RMSNorm backward
+        h, skip = self._norm_skip(self.norm1, x)
+        x = self._shifted_window_attn(h, skip)
+        h, skip = self._norm_skip(self.norm2, x)
+        return self.mlp(h, residual=skip)
+
+    @staticmethod
+    def _norm_skip(norm, x):
+        if norm.norm_type == "rms_norm":
+            return ops.rms_norm_with_skip(x, norm.weight)
+        return norm(x), x
 
 
 class SwinTransformer(nn.Module):

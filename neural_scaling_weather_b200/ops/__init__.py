@@ -54,6 +54,16 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: Optional[float] = None) -> t
     return rms_norm_cuda(x, w, eps)
 
 
+def rms_norm_with_skip(x: torch.Tensor, w: torch.Tensor, eps: Optional[float] = None):
+    """``(rms_norm(x, w), x)``: the pre-norm block input and its skip connection from one
+    autograd node, so their gradients are summed inside the RMSNorm backward on CUDA."""
+    if not _use_cuda(x):
+        return reference.rms_norm(x, w, eps), x
+    from .fused import rms_norm_skip_cuda
+
+    return rms_norm_skip_cuda(x, w, eps)
+
+
 def linear(x: torch.Tensor, weight: TensorOrParts, bias: Optional[TensorOrParts] = None,
            residual: Optional[torch.Tensor] = None, activation: Optional[str] = None):
     """``act(x W^T + b) + residual``; ``weight``/``bias`` may be lists concatenated on N."""

@@ -65,20 +65,26 @@ std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
 }
 
 // eps >= 0: the kernel recomputes rstd from x with this eps (the forward's value); else it reads rstd
-std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, double eps) {
+// add (optional, [rows, n] like x): added to dx in the same pass (skip-connection gradient)
+std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, double eps, c10::optional<Tensor> add) {
   need_cuda(dy, "dy");
   need_cuda(x, "x");
   const int n = (int)x.size(-1);
   const int64_t rows = x.numel() / n;
   auto dx = torch::empty_like(x);
+  const bool fused_add = add.has_value() && nsw::rmsnorm_tma_supported(rows, n, dt_code(x));
+  if (add) TORCH_CHECK(add->is_contiguous() && add->scalar_type() == x.scalar_type() && add->numel() == x.numel(),
+                       "rmsnorm_bwd: add must be a contiguous tensor like x");
   // one partial weight-gradient row per CTA: one persistent CTA per SM for the TMA kernel
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   int parts = nsw::rmsnorm_tma_supported(rows, n, dt_code(x)) ? sms : 3 * sms;
   if (rows < parts * 8) parts = (int)std::max<int64_t>(1, (rows + 7) / 8);
   auto part = torch::empty({parts, n}, x.options().dtype(at::kFloat));
   check(nsw::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(),
-                         dx.data_ptr(), part.data_ptr<float>(), parts, rows, n, dt_code(x), stream(), (float)eps),
+                         dx.data_ptr(), part.data_ptr<float>(), parts, rows, n, dt_code(x), stream(), (float)eps,
+                         fused_add ? add->data_ptr() : nullptr),
         "rmsnorm_bwd");
+  if (add && !fused_add) dx.add_(*add);
   return {dx, part.sum(0)};
 }
 
@@ -380,7 +386,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
-        py::arg("eps") = -1.0);
+        py::arg("eps") = -1.0, py::arg("add") = py::none());
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("res_period") = 0, py::arg("act") = 0, py::arg("preact") = py::none(), py::arg("out_f32") = false,
         py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("impl") = 0);

@@ -183,9 +183,10 @@ cudaError_t rmsnorm_fwd_rows(const void* x, const float* w, void* y, float* rstd
 
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                         float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
-                        cudaStream_t s, float eps) {
+                        cudaStream_t s, float eps, const void* add) {
   if (rmsnorm_tma_supported(rows, n, dtype))
-    return rmsnorm_bwd_tma(dy, x, w, rstd, dx, dw_partial, partial_rows, rows, n, dtype, eps, s);
+    return rmsnorm_bwd_tma(dy, x, w, rstd, dx, dw_partial, partial_rows, rows, n, dtype, eps, s, add);
+  if (add) return cudaErrorInvalidValue;  // callers add the skip gradient themselves on this path
   return rmsnorm_bwd_rows(dy, x, w, rstd, dx, dw_partial, partial_rows, rows, n, dtype, s);
 }
 

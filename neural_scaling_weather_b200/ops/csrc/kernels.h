@@ -15,7 +15,7 @@ cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int
                         float eps, int dtype, cudaStream_t s);
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                         float* dw_partial, int partial_rows, int64_t rows, int n, int dtype,
-                        cudaStream_t s, float eps = -1.f);
+                        cudaStream_t s, float eps = -1.f, const void* add = nullptr);
 
 // ---- elementwise epilogues -----------------------------------------------------
 // y = act(acc + bias) + residual (residual row index = row % res_period)
@@ -87,7 +87,7 @@ cudaError_t rmsnorm_fwd_tma(const void* x, const float* w, void* y, float* rstd,
 // eps >= 0: rstd is recomputed from x (as the forward computed it); eps < 0: read from rstd
 cudaError_t rmsnorm_bwd_tma(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                             float* dw_partial, int partial_rows, int64_t rows, int n, int dtype, float eps,
-                            cudaStream_t s);
+                            cudaStream_t s, const void* add = nullptr);  // add: optional [rows, n] added to dx
 cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw, const void* out,
                                const void* dout, const float* lse, void* dqkv, float* dqw_part, float* dkw_part,
                                const AttnGeom& g, cudaStream_t s, long long* stamps = nullptr);

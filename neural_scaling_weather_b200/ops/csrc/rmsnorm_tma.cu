@@ -176,7 +176,7 @@ template <typename T, int NCH>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
                const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dw_part, Geometry gm, float eps,
-               int* err) {
+               const T* __restrict__ add, int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* sx = smem;                          // [kStages][kTileBytes]
   unsigned char* sg = smem + kStages * kTileBytes;   // [kStages][kTileBytes]
@@ -217,6 +217,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint4* xr = reinterpret_cast<const uint4*>(tx + (size_t)rr * gm.n * sizeof(T));
       const uint4* gr = reinterpret_cast<const uint4*>(tg + (size_t)rr * gm.n * sizeof(T));
       const int64_t r = r0 + rr;
+      // the skip-connection gradient added to dx (when given) is fetched first, so its global
+      // latency overlaps the reduction pass
+      uint4 addv[NCH];
+      if (add) {
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+          if (lane + 32 * j < nvec) addv[j] = __ldg(reinterpret_cast<const uint4*>(add + r * gm.n) + lane + 32 * j);
+      }
       // dx = rs * (g*w - xhat * mean(g*w*xhat)),  xhat = x * rs;  dw += g * xhat.  With eps >= 0,
       // rs is recomputed from the x row in smem (the forward's arithmetic, so the same value) in
       // the pass that forms the dot product, instead of a dependent global load per row.
@@ -252,6 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float xh = fx[i] * rs;
             o[i] = rs * (fg[i] * ww[i] - xh * dot);
             acc[j][i] = fmaf(fg[i], xh, acc[j][i]);
+          }
+          if (add) {
+            float fa[8];
+            unpack8<T>(addv[j], fa);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] += fa[i];
           }
           dxr[c] = pack8<T>(o);
         }
@@ -328,7 +342,7 @@ cudaError_t rmsnorm_fwd_tma(const void* x, const float* w, void* y, float* rstd,
 
 cudaError_t rmsnorm_bwd_tma(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                             float* dw_partial, int partial_rows, int64_t rows, int n, int dtype, float eps,
-                            cudaStream_t s) {
+                            cudaStream_t s, const void* add) {
   using namespace rms_tma;
   if (!rmsnorm_tma_supported(rows, n, dtype)) return cudaErrorInvalidValue;
   const Geometry gm = make_geometry(rows, n, 2);
@@ -339,7 +353,8 @@ cudaError_t rmsnorm_bwd_tma(const void* dy, const void* x, const float* w, const
   do {                                                                                                       \
     NSW_CUDA_CHECK(cudaFuncSetAttribute(bwd_kernel<T, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
     bwd_kernel<T, NC><<<partial_rows, kThreads, smem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx,       \
-                                                           dw_partial, gm, eps, device_error_flag());       \
+                                                           dw_partial, gm, eps, (const T*)add,              \
+                                                           device_error_flag());                            \
   } while (0)
 #define NSW_RB_N(T)                    \
   if (nch <= 1) NSW_RB(T, 1);          \

@@ -88,6 +88,40 @@ class _RMSNorm(torch.autograd.Function):
         return dx.view(ctx.shape).to(ctx.in_dtype), dw.to(w.dtype), None
 
 
+class _RMSNormSkip(torch.autograd.Function):
+    """(rms_norm(x), x) from one node: the skip connection's gradient arrives here together with
+    the normalised branch's and is added inside the RMSNorm backward kernel (no separate add
+    of two activation-sized gradients)."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        ext = require()
+        dt = _cdtype(x)
+        x2 = x.reshape(-1, x.shape[-1]).to(dt).contiguous()
+        y, rstd = ext.rmsnorm_fwd(x2, w.detach().float().contiguous(), eps)
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shape = x.shape
+        ctx.in_dtype = x.dtype
+        ctx.eps = eps
+        return y.view(x.shape), x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, dy, dskip):
+        ext = require()
+        x2, w, rstd = ctx.saved_tensors
+        if dy is None:
+            return dskip, None, None
+        dy2 = dy.reshape(x2.shape).to(x2.dtype).contiguous()
+        add = None if dskip is None else dskip.reshape(x2.shape).to(x2.dtype).contiguous()
+        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd, ctx.eps, add)
+        return dx.view(ctx.shape).to(ctx.in_dtype), dw.to(w.dtype), None
+
+
+def rms_norm_skip_cuda(x, w, eps=None):
+    eps = float(torch.finfo(torch.float32).eps) if eps is None else float(eps)
+    return _RMSNormSkip.apply(x, w, eps)
+
+
 def rms_norm_cuda(x, w, eps=None):
     eps = float(torch.finfo(torch.float32).eps) if eps is None else float(eps)
     return _RMSNorm.apply(x, w, eps)

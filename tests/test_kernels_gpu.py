@@ -335,3 +335,20 @@ def test_window_attention_tcgen05_backward(case, _ext_loaded):
     assert rel(dq_tc, dq_mma) < 2e-2
     assert rel(dqw_tc, qwr.grad) < 3e-2
     assert rel(dkw_tc, kwr.grad) < 3e-2
+
+
+def test_rms_norm_with_skip_gradients():
+    """(norm(x), x) from one node: dx sums both paths inside the RMSNorm backward kernel."""
+    torch.manual_seed(3)
+    x = torch.randn(4097, 1024, device=DEV).bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(1024, device=DEV)).requires_grad_()
+    y, skip = ops.rms_norm_with_skip(x, w)
+    g1, g2 = torch.randn_like(y), torch.randn_like(skip)
+    (y * g1 + skip * g2).float().sum().backward()
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().clone().requires_grad_()
+    yr = reference.rms_norm(xr, wr)
+    (yr * g1.float() + xr * g2.float()).sum().backward()
+    assert rel(y, yr) < 1e-2
+    assert rel(x.grad, xr.grad) < 2e-2
+    assert rel(w.grad, wr.grad) < 2e-2
