@@ -166,7 +166,7 @@ def native(args, rank, world, local):
         f"model.embed_dim={MODEL['embed_dim']}", f"model.depth={args.depth}",
         f"model.num_heads={MODEL['num_heads']}", f"model.patch_size={MODEL['patch_size']}",
         "model.window_size=[9,18]", f"data.batch_size={args.global_batch}",
-        "data.synthetic.n_samples=200", "train.seed=0",
+        "data.synthetic.n_samples=200", "train.seed=0", "train.cuda_graphs=true",
     ]
     cfg = C.compose("default", overrides)
     tr = Trainer(cfg)

@@ -23,6 +23,7 @@ from typing import List, Optional
 
 import numpy as np
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 
 from . import ops
@@ -94,10 +95,30 @@ class WeightedLoss(nn.Module):
         H, W = x.shape[-2], x.shape[-1]
         sse = ops.weighted_sse(x, y, self.weights if self.area_weighting else None,
                                self.channel_weights if self.ch_weighting else None)
-        npix = torch.tensor(float(H * W), dtype=torch.float32, device=x.device)
-        npix = allreduce_forward_identity_backward(npix, "sp1-sp2")
+        npix = global_pixel_count(H, W, x.device)
         sse = allreduce_forward_identity_backward(sse, "sp1-sp2")
         return sse / (npix * math.prod(x.shape[:-2]))
+
+
+_PIXELS = {}
+
+
+def global_pixel_count(h: int, w: int, device) -> float:
+    """Grid points summed over the sp1 x sp2 shards (shards may be uneven).  A constant per
+    local shape: computed once (one all-reduce when the spatial group is distributed) and kept
+    as a Python number, so the loss adds no host-to-device copy to a step (a captured CUDA
+    graph may not contain one)."""
+    distributed = comm.get_size("sp1") * comm.get_size("sp2") > 1
+    key = (h, w, comm.get_size("sp1"), comm.get_size("sp2"), comm.get_rank("sp1"), comm.get_rank("sp2"),
+           id(comm.get_group("sp1-sp2")) if distributed else None)
+    if key not in _PIXELS:
+        if not distributed:
+            _PIXELS[key] = float(h * w)
+        else:
+            t = torch.tensor(float(h * w), dtype=torch.float64, device=device)
+            dist.all_reduce(t, group=comm.get_group("sp1-sp2"))
+            _PIXELS[key] = float(t.item())
+    return _PIXELS[key]
 
 
 class AMSELoss(nn.Module):
@@ -146,10 +167,8 @@ class WeightedRMSE(nn.Module):
     def forward(self, pred, target):
         with profile_range("weighted_rmse"):
             se_sum = ops.weighted_se_per_channel(pred, target, self.weights)
-            count = torch.tensor(float(pred.shape[-2] * pred.shape[-1]), dtype=torch.float32,
-                                 device=pred.device)
+            count = global_pixel_count(pred.shape[-2], pred.shape[-1], pred.device)
             se_sum = allreduce_forward_identity_backward(se_sum, "sp1-sp2")
-            count = allreduce_forward_identity_backward(count, "sp1-sp2")
             rmse = torch.sqrt(se_sum / count)
             if self.temporal_average:
                 while rmse.dim() > 1:
@@ -168,10 +187,8 @@ class WeightedMSE(nn.Module):
     def forward(self, pred, target):
         w = self.weights if self.weights is not None else torch.ones(1, 1, device=pred.device)
         se_sum = ops.weighted_se_per_channel(pred, target, w)
-        count = torch.tensor(float(pred.shape[-2] * pred.shape[-1]), dtype=torch.float32,
-                             device=pred.device)
+        count = global_pixel_count(pred.shape[-2], pred.shape[-1], pred.device)
         se_sum = allreduce_forward_identity_backward(se_sum, "sp1-sp2")
-        count = allreduce_forward_identity_backward(count, "sp1-sp2")
         mse = se_sum / count
         if self.temporal_average:
             while mse.dim() > 1:

@@ -41,6 +41,8 @@ def _weight_t(params: Sequence[torch.Tensor], w: torch.Tensor) -> torch.Tensor:
         return hit[1]
     t = w.t().contiguous()
     _wt_cache[key] = (ver, t)
+    ps, dt, n, k = list(params), w.dtype, t.shape[1], t.shape[0]
+    wcache.register_derived(("T", key), ps, t, lambda: wcache.get_cat(ps, dt).reshape(n, k).t())
     return t
 
 

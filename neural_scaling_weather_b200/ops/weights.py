@@ -9,13 +9,17 @@ and the result is cached until the parameter's version counter changes.
 from __future__ import annotations
 
 import weakref
-from typing import Dict, Sequence, Tuple
+from typing import Callable, Dict, Sequence, Tuple
 
 import torch
 
 # id(param) -> (weak reference to param, shadow); tensors cannot be dict keys by value
 _shadows: Dict[int, Tuple["weakref.ref", torch.Tensor]] = {}
 _cache: Dict[Tuple, Tuple[Tuple[int, ...], torch.Tensor]] = {}
+# derived tensors (concatenations, transposes) with the function that rebuilds them and the
+# parameters they come from; refresh_derived() rewrites them in place after an optimizer step,
+# so a CUDA graph that captured them keeps reading current weights
+_derived: Dict[Tuple, Tuple[Tuple["weakref.ref", ...], torch.Tensor, Callable[[], torch.Tensor]]] = {}
 
 
 def register_shadow(param: torch.Tensor, shadow: torch.Tensor) -> None:
@@ -32,6 +36,38 @@ def _shadow_of(param: torch.Tensor):
 def clear() -> None:
     _shadows.clear()
     _cache.clear()
+    _derived.clear()
+
+
+def register_derived(key: Tuple, params: Sequence[torch.Tensor], t: torch.Tensor,
+                     rebuild: Callable[[], torch.Tensor]) -> None:
+    _derived[key] = (tuple(weakref.ref(p) for p in params), t, rebuild)
+
+
+def refresh_derived() -> None:
+    """Recompute every cached concatenation / transpose in place (concatenations first: the
+    transposes are built from them) and mark them current.  Called after each optimizer step
+    when training runs from captured CUDA graphs."""
+    dead = []
+    for order in (0, 1):
+        for key, (refs, t, rebuild) in list(_derived.items()):
+            if (key[0] == "T") != bool(order):
+                continue
+            params = [r() for r in refs]
+            if any(p is None for p in params):
+                dead.append(key)
+                continue
+            with torch.no_grad():
+                t.copy_(rebuild())
+            ver = tuple(p._version for p in params)
+            if key[0] == "T":
+                from . import fused  # transposes live in the fused operators' cache
+
+                fused._wt_cache[key[1]] = (ver, t)
+            else:
+                _cache[key] = (ver, t)
+    for key in dead:
+        _derived.pop(key, None)
 
 
 def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
@@ -50,6 +86,7 @@ def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         return hit[1]
     t = param.detach().to(dtype)
     _cache[key] = (ver, t)
+    register_derived(key, [param], t, lambda: param.detach().to(dtype))
     return t
 
 
@@ -69,4 +106,8 @@ def get_cat(params: Sequence[torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
              for p, s in zip(params, sh)]
     t = torch.cat(parts, dim=0)
     _cache[key] = (ver, t)
+    ps = list(params)
+    register_derived(key, ps, t, lambda: torch.cat(
+        [s if (s is not None and s.dtype == dtype) else p.detach().to(dtype)
+         for p, s in zip(ps, [_shadow_of(q) for q in ps])], dim=0))
     return t

@@ -213,6 +213,9 @@ class Trainer:
         self.optimizer = set_optimizer(cfg, model, shadow_dtype=shadow, space=self.space)
         self.scheduler = set_scheduler(cfg, self.optimizer)
         self.norms = ShardedNorm(self.space)
+        self.use_cuda_graphs = bool(cfg.train.get("cuda_graphs", False))
+        self._graph, self._graph_calls, self._static, self._static_loss = None, 0, None, None
+        self._graph_pool, self._graph_stream = None, None
         self.gscaler = torch.amp.GradScaler(
             "cuda", enabled=self.amp_enabled and self.amp_dtype == torch.float16)
         self.loss_func = get_loss(cfg, self.metadata).to(self.device)
@@ -328,24 +331,80 @@ class Trainer:
             self.grad += norm * coef
         opt.zero_grad(set_to_none=False)
 
+    def _micro_batch(self, inputs, targets):
+        """Forward, loss and backward of one micro-batch (gradients accumulate in place)."""
+        with profile_range("forward pass"):
+            with torch.autocast(self.device.type, dtype=self.amp_dtype, enabled=self.amp_enabled):
+                gen = self.model(inputs)
+                loss = self.loss_func(gen, targets)
+            self.train_loss += loss.detach()
+            loss = loss / self.gradient_accum_steps
+        with profile_range("backward pass"):
+            self.gscaler.scale(loss).backward()
+        return loss
+
+    def _graphable(self, is_optimizer_step: bool) -> bool:
+        """Micro-batches that can replay a captured CUDA graph: CUDA, no fp16 loss scaling, and
+        not the one whose backward launches the data-parallel gradient reduction."""
+        if not self.use_cuda_graphs or self.device.type != "cuda" or self.gscaler.is_enabled():
+            return False
+        return self.model.reducer is None or not is_optimizer_step
+
+    def _graph_step(self, inputs, targets):
+        """Replay the captured micro-batch graph on this batch (capturing it on the third call;
+        the first two run eagerly so every cache and workspace exists before capture)."""
+        if self._graph is None:
+            # warm-up and capture run on one side stream, so the autograd accumulation nodes the
+            # captured backward uses live on the capture stream
+            self._graph_calls += 1
+            if self._graph_stream is None:
+                self._graph_stream = torch.cuda.Stream(device=self.device)
+            s = self._graph_stream
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            if self._graph_calls <= 2:
+                with torch.cuda.stream(s):
+                    loss = self._micro_batch(inputs, targets).detach()
+                torch.cuda.current_stream(self.device).wait_stream(s)
+                return loss
+            try:
+                with torch.cuda.stream(s):
+                    self._static = (inputs.clone(), targets.clone())
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=self._graph_pool, stream=s):
+                    self._static_loss = self._micro_batch(*self._static).detach()
+                torch.cuda.current_stream(self.device).wait_stream(s)
+                self._graph = g
+            except Exception as e:  # capture unsupported here: stay eager
+                logging.warning(f"CUDA graph capture failed ({type(e).__name__}: {e}); running eagerly")
+                self.use_cuda_graphs = False
+                self._graph, self._static = None, None
+                torch.cuda.synchronize()
+                self.optimizer.zero_grad(set_to_none=False)
+                self.train_loss.zero_()
+                return self._micro_batch(inputs, targets)
+        self._static[0].copy_(inputs, non_blocking=True)
+        self._static[1].copy_(targets, non_blocking=True)
+        self._graph.replay()
+        return self._static_loss
+
     def train_step(self, batch, is_optimizer_step: bool):
-        """One micro-batch forward/backward (and the optimizer step on the last one)."""
+        """One micro-batch forward/backward (and the optimizer step on the last one).  With
+        ``train.cuda_graphs`` the micro-batch replays one captured CUDA graph (host launch
+        overhead removed); derived weight copies are refreshed in place after each step."""
+        graphed = self._graphable(is_optimizer_step)
         sync_ctx = self.model.no_sync() if (self.model.reducer is not None and not is_optimizer_step) else nullcontext()
         with profile_range(f"iter {self.iters}"):
             with sync_ctx:
                 with profile_range("data preproc"):
                     inputs, targets = self.preprocessor(batch, device=self.device)
-                with profile_range("forward pass"):
-                    with torch.autocast(self.device.type, dtype=self.amp_dtype, enabled=self.amp_enabled):
-                        gen = self.model(inputs)
-                        loss = self.loss_func(gen, targets)
-                    self.train_loss += loss.detach()
-                    loss = loss / self.gradient_accum_steps
-                with profile_range("backward pass"):
-                    self.gscaler.scale(loss).backward()
+                loss = self._graph_step(inputs, targets) if graphed else self._micro_batch(inputs, targets).detach()
             with profile_range("optimizer"):
                 if is_optimizer_step:
                     self.optimizer_step()
+                    if self.use_cuda_graphs:
+                        from ..ops import weights as wcache
+
+                        wcache.refresh_derived()
         return loss
 
     def train_one_epoch(self):

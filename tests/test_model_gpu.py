@@ -72,3 +72,46 @@ def test_trainer_steps_on_gpu(tmp_path):
     import torch.distributed as dist
 
     dist.destroy_process_group()
+
+
+def test_trainer_cuda_graph_matches_eager(tmp_path):
+    """Micro-batches replayed from a captured CUDA graph (derived weight copies refreshed in
+    place after each optimizer step) follow the eager loss and parameter trajectory."""
+    import os
+
+    import torch.distributed as dist
+
+    from neural_scaling_weather_b200.ops import weights as wcache
+    from neural_scaling_weather_b200.training.trainer import Trainer
+
+    os.environ.setdefault("MASTER_PORT", "29534")
+    results = []
+    for graphs in (False, True):
+        wcache.clear()
+        cfg = C.compose("default", [
+            f"hydra.run.dir={tmp_path}/g{int(graphs)}", "parallelism.backend=nccl", "model.embed_dim=128",
+            "model.depth=2", "model.num_heads=2", "model.window_size=[4,8]", "model.patch_size=2",
+            "data.synthetic.nlat=32", "data.synthetic.nlon=64", "data.synthetic.n_samples=40", "data.levels=[500]",
+            "data.batch_size=4", "optimizer=adamw", "optimizer.scheduler=null", "train.amp_dtype=bf16",
+            "train.clip_grad_norm=1.0", "logging.log_to_wandb=false", "train.seed=1", "train.save_checkpoint=false",
+            f"train.cuda_graphs={'true' if graphs else 'false'}"])
+        t = Trainer(cfg)
+        t.init_exp_dir(t.exp_dir)
+        t.build()
+        it = iter(t.train_data_loader)
+        batches = [next(it).to("cuda") for _ in range(4)]
+        losses = []
+        for step in range(5):
+            for i in range(t.gradient_accum_steps):
+                loss = t.train_step(batches[(step + i) % 4], is_optimizer_step=(i == t.gradient_accum_steps - 1))
+                losses.append(float(loss))
+        if graphs:
+            assert t._graph is not None, "the micro-batch was not captured"
+        flat = torch.cat([p.detach().flatten().float() for p in t.model.parameters()])
+        results.append((losses, flat))
+        assert _ext.require().read_error_flag(True) == 0
+        dist.destroy_process_group()
+    (le, pe), (lg, pg) = results
+    for a, b in zip(le, lg):
+        assert abs(a - b) <= 2e-3 * max(1.0, abs(a)), (le, lg)
+    assert rel(pg, pe) < 2e-3
