@@ -36,7 +36,6 @@ from .. import ops
 from ..parallel import comm
 from ..parallel.helpers import offsets
 from ..parallel.mappings import (
-    allreduce_forward_identity_backward,
     identity_forward_allreduce_backward,
     roll_forward_reverseroll_backward,
 )
@@ -116,11 +115,10 @@ class MLP(nn.Module):
             h = F.dropout(h, self.drop, True)
         if tp == 1 and not (self.drop > 0 and self.training):
             return ops.linear(h, self.fc2.weight, self.bias2.bias, residual=residual)
-        y = ops.linear(h, self.fc2.weight)
-        y = allreduce_forward_identity_backward(y, "tp")
-        y = y + self.bias2.bias.to(y.dtype)
-        if self.drop > 0 and self.training:
-            y = F.dropout(y, self.drop, True)
+        if not (self.drop > 0 and self.training):  # row-parallel fc2 with the tp all-reduce fused
+            return ops.linear_allreduce(h, self.fc2.weight, self.bias2.bias, residual=residual, group="tp")
+        y = ops.linear_allreduce(h, self.fc2.weight, self.bias2.bias, group="tp")
+        y = F.dropout(y, self.drop, True)
         return y if residual is None else y + residual
 
 
@@ -185,13 +183,13 @@ class Block(nn.Module):
         tp = comm.get_size("tp")
         if tp == 1 and not roll:
             return ops.linear(o, attn.proj.weight, attn.biasproj.bias, residual=skip)
-        y = ops.linear(o, attn.proj.weight)
-        y = allreduce_forward_identity_backward(y, "tp")
-        y = y + attn.biasproj.bias.to(y.dtype)
-        if roll:
-            y = roll_forward_reverseroll_backward(
-                y, self.shift_size, (-3, -2), ["sp1", "sp2"],
-                shapes=(self.sp1_shapes, self.sp2_shapes))
+        # row-parallel proj: the tp all-reduce is fused into the GEMM where the group allows
+        if not roll:
+            return ops.linear_allreduce(o, attn.proj.weight, attn.biasproj.bias, residual=skip, group="tp")
+        y = ops.linear_allreduce(o, attn.proj.weight, attn.biasproj.bias, group="tp")
+        y = roll_forward_reverseroll_backward(
+            y, self.shift_size, (-3, -2), ["sp1", "sp2"],
+            shapes=(self.sp1_shapes, self.sp2_shapes))
         return y if skip is None else y + skip
 
     def forward(self, x: torch.Tensor, condition: Optional[torch.Tensor] = None) -> torch.Tensor:

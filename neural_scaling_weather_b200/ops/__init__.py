@@ -64,6 +64,25 @@ def rms_norm_with_skip(x: torch.Tensor, w: torch.Tensor, eps: Optional[float] = 
     return rms_norm_skip_cuda(x, w, eps)
 
 
+def linear_allreduce(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                     residual: Optional[torch.Tensor] = None, group: str = "tp") -> torch.Tensor:
+    """Row-parallel linear: ``all_reduce_group(x W^T) + bias + residual``.  On CUDA with a
+    symmetric-memory group of 2..8 GPUs the all-reduce runs inside the GEMM's epilogue over
+    NVLink peer memory; otherwise GEMM, then the NCCL all-reduce mapping, then the adds."""
+    from ..parallel import symm
+    from ..parallel.mappings import allreduce_forward_identity_backward
+
+    if _use_cuda(x) and symm.available(group):
+        from .fused import linear_allreduce_cuda
+
+        return linear_allreduce_cuda(x, weight, bias, residual, group)
+    y = linear(x, weight)
+    y = allreduce_forward_identity_backward(y, group)
+    if bias is not None:
+        y = y + bias.to(y.dtype)
+    return y if residual is None else y + residual
+
+
 def linear(x: torch.Tensor, weight: TensorOrParts, bias: Optional[TensorOrParts] = None,
            residual: Optional[torch.Tensor] = None, activation: Optional[str] = None):
     """``act(x W^T + b) + residual``; ``weight``/``bias`` may be lists concatenated on N."""

@@ -88,6 +88,54 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, doub
   return {dx, part.sum(0)};
 }
 
+// ------------------------------------------------------------------------------ GEMM + all-reduce
+// D = sum over the ranks of A_r B_r^T (+ bias + residual), the reduction done in the GEMM's
+// epilogue over NVLink peer memory.  part_ptrs / flag_ptrs: every rank's symmetric partial
+// buffer (>= M * N elements of A's dtype) and flag words, in rank order; rank: this rank.
+Tensor gemm_allreduce(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor> residual,
+                      std::vector<int64_t> part_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank) {
+  need_cuda(A, "A");
+  need_cuda(B, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_allreduce: A [M,K], B [N,K]");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous(), "gemm_allreduce: contiguous operands");
+  TORCH_CHECK(part_ptrs.size() == flag_ptrs.size() && part_ptrs.size() >= 2 && part_ptrs.size() <= 8,
+              "gemm_allreduce: 2..8 ranks");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  auto D = torch::empty({M, N}, A.options());
+  nsw::GemmArgs g{};
+  g.A = A.data_ptr();
+  g.B = B.data_ptr();
+  g.D = D.data_ptr();
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.lda = K;
+  g.ldb = K;
+  g.ldd = N;
+  g.alpha = 1.f;
+  g.dtype = dt_code(A);
+  g.res_period = M;
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N, "gemm_allreduce: fp32 bias [N]");
+    g.bias = bias->data_ptr<float>();
+  }
+  if (residual) {
+    TORCH_CHECK(residual->is_contiguous() && residual->numel() == M * N && residual->scalar_type() == A.scalar_type(),
+                "gemm_allreduce: residual [M, N] in A's dtype");
+    g.residual = residual->data_ptr();
+    g.ldr = N;
+  }
+  g.ar_world = (int)part_ptrs.size();
+  g.ar_rank = (int)rank;
+  for (int r = 0; r < g.ar_world; ++r) {
+    g.ar_part[r] = reinterpret_cast<void*>(part_ptrs[r]);
+    g.ar_flags[r] = reinterpret_cast<uint32_t*>(flag_ptrs[r]);
+  }
+  TORCH_CHECK(nsw::gemm_tcgen05_supported(g), "gemm_allreduce: shape/alignment not supported");
+  check(nsw::gemm_tcgen05(g, stream(), 1), "gemm_allreduce");
+  return D;
+}
+
 // ------------------------------------------------------------------------------ GEMM
 Tensor gemm(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor> residual,
             int64_t res_period, int64_t act, c10::optional<Tensor> preact, bool out_f32, double alpha,
@@ -391,6 +439,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("res_period") = 0, py::arg("act") = 0, py::arg("preact") = py::none(), py::arg("out_f32") = false,
         py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("impl") = 0);
   m.def("gemm_supported", &gemm_supported);
+  m.def("gemm_allreduce", &gemm_allreduce, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(),
+        py::arg("residual") = py::none(), py::arg("part_ptrs"), py::arg("flag_ptrs"), py::arg("rank"));
   m.def("bias_act_residual", &bias_act_residual);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("col_sum", &col_sum);

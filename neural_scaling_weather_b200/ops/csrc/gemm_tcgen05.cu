@@ -96,6 +96,9 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// named barrier of the epilogue warps only (the producer / MMA warps keep running)
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory"); }
+
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
   // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO), LBO unused (1),
   // descriptor version 1, layout type 2 (SWIZZLE_128B).
@@ -160,6 +163,36 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t* r) {
                : "memory");
 }
 
+// system-scope flag publication / observation (peer GPUs over NVLink)
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// wait (bounded) until *p >= v (wrap-safe); false on timeout (error recorded)
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* p, uint32_t v, int* err) {
+  if ((int)(ld_acquire_sys(p) - v) >= 0) return true;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t spin = 0;; ++spin) {
+    if ((int)(ld_acquire_sys(p) - v) >= 0) return true;
+    if ((spin & 63u) == 63u) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 4000000000ull) {
+        record_error(err, kErrWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+
 // TMA store of a 32 x 32 tile (SWIZZLE_64B staging in smem) and its bulk-group bookkeeping
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -192,7 +225,22 @@ struct EpiParams {
   int out_f32;
   int accumulate;
   float alpha;
+  // Tensor-parallel all-reduce fused into the epilogue (ar_world > 1; 16-bit D, no
+  // pre-activation / GELU): each rank's CTA drains its tile as a 16-bit partial into its own
+  // symmetric buffer ar_part[rank], releases the accumulator, publishes a per-tile ready flag to
+  // every peer, and once all ranks' partials of the tile are published sums them with peer
+  // loads over NVLink before bias / residual / store.  Flags (uint32 words): [0] the epoch of
+  // the last finished launch, [1] CTAs of this rank that finished (all launches), [2 + r] CTAs
+  // of rank r that finished reading this rank's partials (all launches), [kArFlagBase + r * tiles
+  // + t] the epoch in which rank r published its partial of tile t.  Epochs increase by one per
+  // launch and counters by the grid size, so nothing is ever reset (and a captured CUDA graph
+  // replays correctly); every rank launches the same grid.
+  int ar_world, ar_rank;
+  int64_t ar_tiles;
+  void* ar_part[8];
+  uint32_t* ar_flags[8];
 };
+constexpr int kArFlagBase = 16;
 
 // Epilogue of one warp for one accumulator tile: rows [row_base, row_base + 32) (the warp's
 // TMEM lane quadrant) and columns [n0 + half * BN/2, n0 + (half + 1) * BN/2).
@@ -321,6 +369,87 @@ struct EpiWarp {
     ++ring;
   }
 
+  // All-reduce mode, step 1: this warp's part of the accumulator as a 16-bit partial in the
+  // rank's own symmetric buffer (this lane's row, 64 contiguous bytes per 32-column chunk).
+  __device__ __forceinline__ void drain_partial(const EpiParams& ep, uint32_t t_row, int64_t row_base, int64_t n0,
+                                                int half, int lane) {
+    const int64_t row = row_base + lane;
+    T* part = reinterpret_cast<T*>(ep.ar_part[ep.ar_rank]);
+#pragma unroll
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = half * kChunks + cc;
+      uint32_t r[32];
+      tmem_ld32(t_row + (uint32_t)(c * 32), r);
+      const int64_t nb = n0 + c * 32;
+      if (nb >= ep.N || row >= ep.M) continue;
+      float f[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) * ep.alpha;
+      uint4* dst = reinterpret_cast<uint4*>(part + row * ep.N + nb);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) dst[v] = pack8<T>(&f[8 * v]);
+    }
+  }
+
+  // All-reduce mode, step 2 (all ranks' partials of the tile published): sum them (peer loads),
+  // add bias and residual, store D through the TMA-store staging ring.
+  __device__ __forceinline__ void reduce_store(const EpiParams& ep, T* stg, int64_t row_base, int64_t n0, int half,
+                                               int lane, uint32_t& ring) {
+    const int64_t row = row_base + lane;
+    const bool row_ok = row < ep.M;
+#pragma unroll 1
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = half * kChunks + cc;
+      const int64_t nb = n0 + c * 32;
+      if (nb >= ep.N) continue;  // warp-uniform
+      float f[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = 0.f;
+      if (row_ok) {
+        for (int q = 0; q < ep.ar_world; ++q) {
+          // start with the next rank so the ranks do not all read rank 0 at once
+          const int r = (ep.ar_rank + 1 + q) % ep.ar_world;
+          const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.ar_part[r]) + row * ep.N + nb);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            float x[8];
+            unpack8<T>(src[v], x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[8 * v + i] += x[i];
+          }
+        }
+        if (ep.bias) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(ep.bias + nb) + v);
+            f[4 * v] += b4.x;
+            f[4 * v + 1] += b4.y;
+            f[4 * v + 2] += b4.z;
+            f[4 * v + 3] += b4.w;
+          }
+        }
+        if (ep.residual) {
+          const uint4* rp = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                           (row % ep.res_period) * ep.ldr + nb);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            float x[8];
+            unpack8<T>(__ldg(rp + v), x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[8 * v + i] += x[i];
+          }
+        }
+      }
+      if (ep.tma_out) {
+        stage_store(&ep.map_d, f, stg, lane, (int)nb, (int)row_base, ring);
+      } else if (row_ok) {
+        uint4* dp = reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) dp[v] = pack8<T>(&f[8 * v]);
+      }
+    }
+  }
+
   // Ragged column edge, fp32 output, or no TMA maps: per-row stores of this lane's row.
   __device__ __forceinline__ void direct_stores(const EpiParams& ep, float* f, int64_t row, bool row_ok, int64_t nb,
                                                 bool full) {
@@ -382,6 +511,7 @@ struct Smem {
   alignas(1024) T stage[kEpiWarps][2 * 32 * kStageRow];  // two 2 KB staging buffers per epilogue warp
   uint32_t tmem_base;
   int abort_flag;
+  int epi_stop;  // all-reduce epilogue: written by its leader only, read after a named barrier
 };
 
 template <typename T, int BN, int STAGES>
@@ -483,6 +613,77 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc_phase ^= 1;
         }
       }
+    }
+  } else if (ep.ar_world > 1) {
+    // ------------------------------------------------------------------ epilogue + all-reduce
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;
+    const bool leader = ew == 0 && lane == 0;  // publishes and observes flags for the CTA
+    T* stg = S.stage[ew];
+    uint32_t ring = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    uint32_t* my_flags = ep.ar_flags[ep.ar_rank];
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_flags) + 1u;
+    bool ok = true;
+    if (leader) S.epi_stop = 0;
+    epi_sync();
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int64_t m0 = (tile / n_tiles) * BM;
+      const int64_t n0 = (tile % n_tiles) * BN;
+      const int64_t row_base = m0 + q * 32;
+      EpiWarp<T, BN> epi;
+      // every epilogue warp takes both named barriers of every tile it enters, and all of them
+      // leave the loop on the leader's decision, so no warp is left waiting at a barrier
+      const bool have = mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err);
+      if (have) {
+        tc_fence_after();
+        epi.drain_partial(ep, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half,
+                          lane);
+      } else {
+        *abort_flag = 1;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && have) mbar_arrive(&S.tmem_empty[acc]);  // the MMAs of the next tile may start
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+      epi_sync();  // the whole tile's partial is written
+      if (leader) {
+        bool go = !*abort_flag;
+        if (go) {
+          __threadfence_system();
+          for (int r = 0; r < ep.ar_world; ++r)
+            if (r != ep.ar_rank) st_release_sys(ep.ar_flags[r] + kArFlagBase + ep.ar_rank * ep.ar_tiles + tile, epoch);
+          for (int r = 0; r < ep.ar_world && go; ++r)
+            if (r != ep.ar_rank) go = wait_flag_geq(my_flags + kArFlagBase + r * ep.ar_tiles + tile, epoch, err);
+          if (!go) *abort_flag = 1;
+        }
+        S.epi_stop = go ? 0 : 1;
+      }
+      epi_sync();
+      if (*reinterpret_cast<volatile int*>(&S.epi_stop)) {
+        ok = false;
+        break;
+      }
+      epi.reduce_store(ep, stg, row_base, n0, half, lane, ring);
+    }
+    if (lane == 0) bulk_wait_all();
+    // this CTA has read its peers' partials; before the launch ends, every CTA of every peer has
+    // read this rank's partials (the next launch overwrites them)
+    epi_sync();
+    if (leader) {
+      __threadfence_system();
+      for (int r = 0; r < ep.ar_world; ++r)
+        if (r != ep.ar_rank) red_release_sys_add(ep.ar_flags[r] + 2 + ep.ar_rank, 1u);
+      const uint32_t target = epoch * gridDim.x;
+      for (int r = 0; r < ep.ar_world; ++r)
+        if (r != ep.ar_rank) wait_flag_geq(my_flags + 2 + r, target, err);
+      // the last CTA of this launch on this rank advances the epoch (all CTAs have read it)
+      if (atomicAdd(my_flags + 1, 1u) == target - 1u) atomicExch(my_flags, epoch);
     }
   } else {
     // ------------------------------------------------------------------ epilogue
@@ -814,6 +1015,12 @@ static EpiParams epi_params(const GemmArgs& a) {
   ep.out_f32 = a.out_f32;
   ep.accumulate = a.accumulate;
   ep.alpha = a.alpha;
+  ep.ar_world = a.ar_world;
+  ep.ar_rank = a.ar_rank;
+  for (int r = 0; r < 8; ++r) {
+    ep.ar_part[r] = r < a.ar_world ? a.ar_part[r] : nullptr;
+    ep.ar_flags[r] = r < a.ar_world ? a.ar_flags[r] : nullptr;
+  }
   return ep;
 }
 
@@ -861,7 +1068,8 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   CUtensorMap ma, mb;
   if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
   if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN, a.dtype)) return cudaErrorInvalidValue;
-  const EpiParams ep = epi_params(a);
+  EpiParams ep = epi_params(a);
+  ep.ar_tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
   const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                          ((uint32_t)(BM >> 4) << 24);
@@ -886,6 +1094,12 @@ int gemm_tcgen05_supported(const GemmArgs& a) {
   if (a.preact && (reinterpret_cast<uintptr_t>(a.preact) & 15)) return 0;
   if (a.accumulate && !a.out_f32) return 0;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  if (a.ar_world > 1) {  // fused all-reduce: plain (bias / residual) epilogue, whole 32-column chunks
+    if (a.ar_world > 8 || a.ar_rank < 0 || a.ar_rank >= a.ar_world) return 0;
+    if (a.preact || a.act || a.out_f32 || a.accumulate || a.N % 32) return 0;
+    for (int r = 0; r < a.ar_world; ++r)
+      if (!a.ar_part[r] || !a.ar_flags[r] || (reinterpret_cast<uintptr_t>(a.ar_part[r]) & 15)) return 0;
+  }
   return tc::get_encode() != nullptr;
 }
 
@@ -898,7 +1112,8 @@ cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl) {
   if (!gemm_tcgen05_supported(a)) return cudaErrorInvalidValue;
   const bool wide = a.N > 128;
   const bool light = a.act == 0 && !a.residual && !a.preact;
-  const bool pair = impl == 2 || (impl == 0 && wide && a.M > tc::BM && light);
+  // the fused all-reduce lives in the single-CTA kernel's epilogue
+  const bool pair = a.ar_world <= 1 && (impl == 2 || (impl == 0 && wide && a.M > tc::BM && light));
   if (a.dtype == kBF16) {
     if (pair) return tc::launch2<__nv_bfloat16, 6>(a, s);
     return wide ? tc::launch<__nv_bfloat16, 256, 4>(a, s) : tc::launch<__nv_bfloat16, 128, 6>(a, s);

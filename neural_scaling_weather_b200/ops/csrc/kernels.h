@@ -111,6 +111,12 @@ struct GemmArgs {
   int out_f32;          // D in fp32 instead of dtype
   float alpha;
   int accumulate;       // D += result (fp32 output only)
+  // tensor-parallel all-reduce fused into the epilogue (ar_world > 1): ar_part[r] / ar_flags[r]
+  // are rank r's symmetric partial buffer ([M, N] in dtype) and flag words (peer pointers)
+  int ar_world;
+  int ar_rank;
+  void* ar_part[8];
+  uint32_t* ar_flags[8];
 };
 cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl = 0);
 int gemm_tcgen05_supported(const GemmArgs& a);

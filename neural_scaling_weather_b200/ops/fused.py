@@ -411,3 +411,48 @@ def weighted_se_per_channel_cuda(x, y, area_w):
     ext = require()
     return ext.weighted_se_per_plane(x.detach().contiguous(), y.detach().contiguous(),
                                      area_w.detach().float().contiguous().view(-1))
+
+
+# ---------------------------------------------------------------------------- GEMM + all-reduce
+class _LinearAllReduce(torch.autograd.Function):
+    """y = all_reduce_group(x W^T) + b + residual with the reduction inside the GEMM epilogue
+    (peer loads of every rank's partial tile over NVLink, tile by tile, while the next tile's
+    MMAs run).  Backward is the row-parallel linear's: the all-reduce passes gradients through."""
+
+    @staticmethod
+    def forward(ctx, x, residual, group, w, b):
+        from ..parallel import symm
+
+        ext = require()
+        dt = _cdtype(x)
+        K = x.shape[-1]
+        x2 = x.reshape(-1, K).to(dt).contiguous()
+        W = wcache.get(w, dt)
+        M, N = x2.shape[0], W.shape[0]
+        bufs = symm.allreduce_buffers(group, M, N, dt, x.device)
+        res2 = residual.reshape(-1, N).to(dt).contiguous() if residual is not None else None
+        bias = b.detach().float().contiguous() if b is not None else None
+        y = ext.gemm_allreduce(x2, W, bias, res2, bufs.part_ptrs, bufs.flag_ptrs, bufs.rank)
+        ctx.save_for_backward(x2)
+        ctx.w, ctx.W = w, W
+        ctx.has_b = b is not None
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        ctx.res_dtype = residual.dtype if residual is not None else None
+        return y.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        ext = require()
+        (x2,) = ctx.saved_tensors
+        W = ctx.W
+        N = W.shape[0]
+        dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
+        dx = gemm(dy2, _weight_t([ctx.w], W)).view(ctx.x_shape).to(ctx.x_dtype) if ctx.needs_input_grad[0] else None
+        dW = wgrad(dy2, x2).reshape(ctx.w.shape)
+        db = ext.col_sum(dy2) if ctx.has_b else None
+        dres = dy.to(ctx.res_dtype) if ctx.res_dtype is not None else None
+        return dx, dres, None, dW, db
+
+
+def linear_allreduce_cuda(x, w, b, residual, group):
+    return _LinearAllReduce.apply(x, residual, group, w, b)

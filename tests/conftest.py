@@ -21,3 +21,6 @@ def _reset_comm():
     yield
     comm.reset()
     weights.clear()
+    from neural_scaling_weather_b200.parallel import symm
+
+    symm.reset()

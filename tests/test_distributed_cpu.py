@@ -224,3 +224,14 @@ def test_config0_sp2_training_matches_single_rank(tmp_path):
     b = torch.load(tmp_path / "sp2.pt")
     for k in a:
         assert torch.allclose(a[k], b[k], atol=1e-5, rtol=1e-4), k
+
+
+def test_fused_collectives_not_available_without_cuda_group():
+    """The symmetric-memory path is only taken for CUDA groups of 2..8 ranks; elsewhere the
+    row-parallel linear falls back to GEMM + all-reduce mapping."""
+    from neural_scaling_weather_b200.parallel import symm
+
+    assert symm.available("tp") is False
+    symm.disable("tp", "test")
+    assert symm.available("tp") is False
+    symm.reset()

@@ -38,3 +38,11 @@ def test_bench_two_gpus_small():
     assert lines, r.stdout[-3000:] + r.stderr[-3000:]
     d = json.loads(lines[-1])
     assert d["n_gpus"] == 2 and d["value"] > 0
+
+
+def test_fused_gemm_allreduce_two_gpus():
+    """Tensor-parallel GEMM with the all-reduce in its epilogue over NVLink peer memory."""
+    if NGPU < 2:
+        pytest.skip("needs 2 GPUs")
+    r = _torchrun(2, ["tests/mp_fused_tp_worker.py"])
+    assert "FUSED_TP_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
