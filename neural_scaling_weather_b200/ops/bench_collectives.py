@@ -1,0 +1,83 @@
+"""Timing of the fused tensor-parallel GEMM + all-reduce against GEMM then NCCL all-reduce.
+
+``python -m torch.distributed.run --nproc-per-node N -m neural_scaling_weather_b200.ops.bench_collectives``
+(N = 2..8 GPUs of one node).  Shape: a row-parallel projection of the Swin p4-e1024 block
+(64800 tokens, 1024 outputs, 1024 / N inputs per rank) with bias and residual.  Times are CUDA
+events on each rank around several launches, reported as the maximum over ranks; the roofline
+is the slower of the GEMM at the measured bf16 rate and the bytes a rank must pull over NVLink
+(its peers' 16-bit partials, (N - 1) / N of the output) at 770 GB/s per direction.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--M", type=int, default=64800)
+    ap.add_argument("--N", type=int, default=1024)
+    ap.add_argument("--K", type=int, default=1024, help="full input width (split over the ranks)")
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from . import _ext, linear_allreduce
+    from ..parallel import comm, symm
+
+    comm.init_model_parallel_info(tp=world, sp1=1, sp2=1, dp=1)
+    ext = _ext.require()
+    M, N, K = a.M, a.N, a.K // world
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = torch.nn.Parameter(0.02 * torch.randn(N, K, device=dev))
+    b = torch.nn.Parameter(torch.zeros(N, device=dev))
+    res = torch.randn(M, N, device=dev).bfloat16()
+    wb = w.detach().bfloat16()
+
+    def fused():
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return linear_allreduce(x, w, b, residual=res, group="tp")
+
+    def baseline():
+        y = ext.gemm(x, wb)
+        dist.all_reduce(y, group=comm.get_group("tp"))
+        return y + b.detach().bfloat16() + res
+
+    out = {}
+    for name, fn in (("fused", fused), ("gemm_then_nccl", baseline)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        out[name] = round(ms.item(), 4)
+    assert ext.read_error_flag(True) == 0
+    flops = 2.0 * M * N * K
+    peer_bytes = (world - 1) * M * N * 2
+    roof_ms = max(flops / 1649.8e12, peer_bytes / 770e9) * 1e3
+    if rank == 0:
+        print(json.dumps({"op": "row-parallel linear + all-reduce", "world": world, "M": M, "N": N, "K_per_rank": K,
+                          "fused_ms": out["fused"], "gemm_then_nccl_ms": out["gemm_then_nccl"],
+                          "roofline_ms": round(roof_ms, 4), "fused_of_roofline": round(roof_ms / out["fused"], 3)}))
+    symm.reset()
+    comm.reset()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
