@@ -99,10 +99,12 @@ def bench_block_gemms(a):
         ("fwd qkv +bias", lambda: ext.gemm(x, W["qkv"], b["qkv"], impl=a.impl), M, 3 * E, E),
         ("fwd proj +bias+res", lambda: ext.gemm(x, W["proj"], b["proj"], res, impl=a.impl), M, E, E),
         ("fwd fc1 +bias+gelu(+preact)", lambda: ext.gemm(x, W["fc1"], b["fc1"], None, 0, 1, pre, impl=a.impl), M, 4 * E, E),
+        ("fwd fc1 +bias+gelu(+gelu')", lambda: ext.gemm(x, W["fc1"], b["fc1"], None, 0, 3, pre, impl=a.impl), M, 4 * E, E),
         ("fwd fc2 +bias+res", lambda: ext.gemm(h4, W["fc2"], b["fc2"], res, impl=a.impl), M, E, 4 * E),
         ("dgrad qkv", lambda: ext.gemm(g3, Wt["qkv"], impl=a.impl), M, E, 3 * E),
         ("dgrad proj", lambda: ext.gemm(x, Wt["proj"], impl=a.impl), M, E, E),
         ("dgrad fc2 *gelu'(u)", lambda: ext.gemm(x, Wt["fc2"], None, u, 0, 2, impl=a.impl), M, 4 * E, E),
+        ("dgrad fc2 *aux", lambda: ext.gemm(x, Wt["fc2"], None, u, 0, 4, impl=a.impl), M, 4 * E, E),
         ("dgrad fc2 plain", lambda: ext.gemm(x, Wt["fc2"], impl=a.impl), M, 4 * E, E),
         ("dgrad fc1", lambda: ext.gemm(h4, Wt["fc1"], impl=a.impl), M, E, 4 * E),
         ("wgrad fc1 cublas", lambda: torch.mm(h4.t(), x, out_dtype=torch.float32), 4 * E, E, M),
@@ -110,7 +112,7 @@ def bench_block_gemms(a):
     tot = 0.0
     for name, fn, m, n, k in cases:
         ms = timeit(fn, a.iters)
-        if "plain" not in name and "wgrad" not in name:
+        if "plain" not in name and "wgrad" not in name and "(+preact)" not in name and "gelu'(u)" not in name:
             tot += ms
         report(name, ms, 2.0 * m * n * k, None)
     print(json.dumps({"block_fwd_plus_dgrad_ms": round(tot, 3)}))

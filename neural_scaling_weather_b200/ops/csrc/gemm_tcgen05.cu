@@ -2,7 +2,10 @@
 //
 //   D[m, n] = epilogue( alpha * sum_k A[m, k] * B[n, k] )
 //   epilogue: (+ bias[n]) -> (store pre-activation) -> (GELU) -> (+ residual[m % P, n])
-//             or, with act == 2, (* GELU'(aux[m, n])) for the MLP backward (aux in `residual`)
+//             or, with act == 2, (* GELU'(aux[m, n])) for the MLP backward (aux in `residual`);
+//             act == 3: GELU with GELU'(u) (not u) written as the pre-activation output, and
+//             act == 4: (* aux[m, n]) -- the MLP forward / backward pair that keeps the erf and
+//             exponential out of the backward GEMM
 //             -> bf16/fp16 store, or fp32 store / fp32 accumulate (D += ...)
 //
 // A [M, K] and B [N, K] are K-major (row-major with K contiguous), bf16 or fp16.
@@ -320,7 +323,18 @@ struct EpiWarp {
           direct_stores(ep, f, row, row_ok, nb, full);
         } else {
           const int m_tile = (int)row_base, n_tile = (int)nb;
-          if (ep.preact) stage_store(&ep.map_pre, f, stg, lane, n_tile, m_tile, ring);
+          if (ep.act == 3) {  // GELU, and GELU'(u) kept for the backward (one erf / exp per element)
+            float g[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const GeluParts gp = gelu_parts_fast(f[j]);
+              g[j] = gp.cdf + f[j] * gp.pdf;
+              f[j] *= gp.cdf;
+            }
+            if (ep.preact) stage_store(&ep.map_pre, g, stg, lane, n_tile, m_tile, ring);
+          } else if (ep.preact) {
+            stage_store(&ep.map_pre, f, stg, lane, n_tile, m_tile, ring);
+          }
           if (ep.act == 1) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
@@ -341,6 +355,9 @@ struct EpiWarp {
               if (ep.act == 2) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) f[8 * v + j] *= gelu_grad_fast(rr8[j]);
+              } else if (ep.act == 4) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[8 * v + j] *= rr8[j];
               } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
@@ -456,9 +473,9 @@ struct EpiWarp {
     if (!row_ok) return;
     if (ep.preact) {
       T* pp = reinterpret_cast<T*>(ep.preact) + row * ep.ldd + nb;
-      for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(f[j]);
+      for (int j = 0; j < 32 && nb + j < ep.N; ++j) pp[j] = from_f<T>(ep.act == 3 ? gelu_grad_fast(f[j]) : f[j]);
     }
-    if (ep.act == 1) {
+    if (ep.act == 1 || ep.act == 3) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
     }
@@ -466,6 +483,8 @@ struct EpiWarp {
       const T* rp = reinterpret_cast<const T*>(ep.residual) + (row % ep.res_period) * ep.ldr + nb;
       if (ep.act == 2) {
         for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] *= gelu_grad_fast(to_f(rp[j]));
+      } else if (ep.act == 4) {
+        for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] *= to_f(rp[j]);
       } else {
         for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += to_f(rp[j]);
       }

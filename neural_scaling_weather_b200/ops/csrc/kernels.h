@@ -106,7 +106,7 @@ struct GemmArgs {
   const void* residual; // [*, N] (ldr) or null; row index = m % res_period
   int64_t ldr, res_period;
   void* preact;         // optional [M, N] pre-activation output (ldd)
-  int act;              // 0 none, 1 gelu, 2 multiply by gelu'(residual) (MLP backward)
+  int act;              // 0 none, 1 gelu, 2 * gelu'(residual), 3 gelu + gelu'(u) as preact, 4 * residual
   int dtype;            // kBF16 / kF16 (A, B, D, residual, preact)
   int out_f32;          // D in fp32 instead of dtype
   float alpha;

@@ -210,9 +210,11 @@ def linear_cuda(x, weight, bias=None, residual=None, activation=None):
 class _MLP(torch.autograd.Function):
     """fc1 + bias + GELU -> fc2 + bias (+ residual) with a fused backward.
 
-    Forward: two tcgen05 GEMMs (the first saves the pre-activation u and the GELU output h).
-    Backward: du = (dy @ W2) * GELU'(u) in ONE GEMM epilogue (no separate GELU-backward pass),
-    dx = du @ W1; weight gradients by cuBLAS with fp32 output.
+    Forward: two tcgen05 GEMMs; the first's epilogue writes h = GELU(u) and, from the same
+    erf / exp, GELU'(u) (saved for backward instead of u).
+    Backward: du = (dy @ W2) * GELU'(u) in ONE GEMM epilogue (a plain multiply by the saved
+    tensor), dx = du @ W1; weight gradients by cuBLAS with fp32 output.  Shapes the tcgen05
+    kernel cannot take save u and use the GELU-backward kernel.
     """
 
     @staticmethod
@@ -227,7 +229,10 @@ class _MLP(torch.autograd.Function):
         H = W1.shape[0]
         needs_grad = any(ctx.needs_input_grad)
         u = torch.empty(x2.shape[0], H, dtype=dt, device=x.device) if needs_grad else None
-        h = gemm(x2, W1, b1.detach().float(), None, 0, 1, u)
+        x2 = x2.contiguous()
+        ctx.aux_is_grad = ext.gemm_supported(x2, W1, False)
+        # act 3: u holds GELU'(pre-activation); act 1: u holds the pre-activation itself
+        h = gemm(x2, W1, b1.detach().float(), None, 0, 3 if ctx.aux_is_grad else 1, u)
         res2 = residual.reshape(-1, N).to(dt).contiguous() if residual is not None else None
         y = gemm(h, W2, b2.detach().float(), res2)
         ctx.save_for_backward(x2, u, h)
@@ -245,7 +250,12 @@ class _MLP(torch.autograd.Function):
         dW2 = wgrad(dy2, h)
         db2 = ext.col_sum(dy2)
         W2t = _weight_t([ctx.w2], ctx.W2)
-        if ext.gemm_supported(dy2, W2t, False):
+        if ctx.aux_is_grad:
+            if ext.gemm_supported(dy2, W2t, False):
+                du = ext.gemm(dy2, W2t, None, u, 0, 4)  # epilogue: * GELU'(u) (saved)
+            else:
+                du = (gemm(dy2, W2t).float() * u.float()).to(u.dtype)
+        elif ext.gemm_supported(dy2, W2t, False):
             du = ext.gemm(dy2, W2t, None, u, 0, 2)  # epilogue: * GELU'(u)
         else:
             du = ext.gelu_bwd(gemm(dy2, W2t).contiguous(), u)

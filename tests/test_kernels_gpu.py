@@ -60,6 +60,15 @@ def test_gemm_epilogues(impl, _ext_loaded):
     assert rel(y, torch.nn.functional.gelu(u)) < 1e-2
     y2 = _ext_loaded.gemm(a, b, bias, res, impl=impl)
     assert rel(y2, u + res.float()) < 1e-2
+    # act 3: GELU with GELU'(u) as the saved tensor; act 4: multiply by the saved tensor
+    g = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    y4 = _ext_loaded.gemm(a, b, bias, None, 0, 3, g, impl=impl)
+    uu = u.clone().requires_grad_()
+    torch.nn.functional.gelu(uu).sum().backward()
+    assert rel(y4, torch.nn.functional.gelu(u)) < 1e-2
+    assert rel(g, uu.grad) < 1e-2
+    y5 = _ext_loaded.gemm(a, b, None, g, 0, 4, impl=impl)
+    assert rel(y5, (a.float() @ b.float().t()) * g.float()) < 1e-2
     # broadcast residual (period)
     pos = torch.randn(128, N, device=DEV, dtype=torch.bfloat16)
     a3 = a[:512].contiguous()
