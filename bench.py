@@ -176,26 +176,23 @@ def native(args, rank, world, local):
     _, batches, _ = make_batches(2, "cuda")
     dev_batches = batches
 
-    def step(src, pinned):
+    def step(src):
         last = None
         for i in range(accum):
-            b = src[i % len(src)]
-            if pinned:
-                b = b.to("cuda", non_blocking=True)
-            last = tr.train_step(b, is_optimizer_step=(i == accum - 1))
+            last = tr.train_step(src[i % len(src)], is_optimizer_step=(i == accum - 1))
         return last
 
     torch.cuda.synchronize()
     for _ in range(args.warmup):
-        step(dev_batches, False)
+        step(dev_batches)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
 
     # launch count (one extra step under the profiler, outside the timed region)
-    launches = count_launches(lambda: step(dev_batches, False))
+    launches = count_launches(lambda: step(dev_batches))
     if args.breakdown and rank == 0:
-        kernel_breakdown(lambda: step(dev_batches, False), args.breakdown)
+        kernel_breakdown(lambda: step(dev_batches), args.breakdown)
 
     sampler = ClockSampler(gpus=list(range(world)) if world > 1 else [torch.cuda.current_device()])
     if rank == 0:
@@ -206,7 +203,7 @@ def native(args, rank, world, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        step(dev_batches, False)
+        step(dev_batches)
     e1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -217,18 +214,28 @@ def native(args, rank, world, local):
 
     e2e = None
     if not args.no_e2e:
+        from neural_scaling_weather_b200.data import device_prefetch
+
         _, host_batches, _ = make_batches(2, "cuda", pinned=True)
-        for _ in range(1):
-            step(host_batches, True)
-            tr.train_loss.item()
+        dev = torch.device("cuda", torch.cuda.current_device())
+
+        def run_steps(n):
+            # the framework's input path: pinned host batches, each copied to the device one
+            # micro-batch ahead on a copy stream (data.device_prefetch), as Trainer.train_one_epoch
+            # does; the step's loss is read back to the host after every optimizer step
+            src = (host_batches[i % len(host_batches)] for i in range(n * accum))
+            for i, b in enumerate(device_prefetch(src, dev)):
+                tr.train_step(b, is_optimizer_step=(i % accum == accum - 1))
+                if i % accum == accum - 1:
+                    float(tr.train_loss.item())  # device -> host read of the step's result
+
+        run_steps(1)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
-        for _ in range(args.steps):
-            step(host_batches, True)
-            float(tr.train_loss.item())  # device -> host read of the step's result
+        run_steps(args.steps)
         f1.record()
         torch.cuda.synchronize()
         e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
@@ -236,7 +243,8 @@ def native(args, rank, world, local):
         e2e = {"value": args.global_batch / (e_ms / 1000.0), "unit": "samples/s",
                "h2d_bytes_per_step": int(bi), "d2h_bytes_per_step": 4 * world,
                "ms_per_step": e_ms,
-               "path": "Trainer.train_step on pinned-host batches + loss.item() each step"}
+               "path": "Trainer.train_step on pinned-host batches through data.device_prefetch (H2D one "
+                       "micro-batch ahead on a copy stream) + loss.item() each step"}
 
     rollout_ms = None
     if not args.no_rollout and rank == 0:
@@ -380,9 +388,13 @@ def reference(args, rank, world, local):
     _, batches, inv = make_batches(2, "cuda")
     from contextlib import nullcontext
 
-    def step():
+    def step(src=None):
+        loss = None
         for i in range(accum):
-            b = batches[i % len(batches)]
+            if src is None:
+                b = batches[i % len(batches)]
+            else:  # the reference PreProcessor's send_to_device path: batch.to(device)
+                b = src[i % len(src)].to(device)
             b = torch.cat([b, inv.expand(1, 2, -1, -1, -1)], dim=2)
             inputs, targets = b[:, :1], b[:, 1:, :N_CH]
             ctx = model.no_sync() if (world > 1 and i < accum - 1) else nullcontext()
@@ -395,6 +407,7 @@ def reference(args, rank, world, local):
             tr_cls.clip_grad_norm(fake, model, max_norm=1.0)
         opt.step()
         model.zero_grad(set_to_none=True)
+        return loss
 
     for _ in range(args.warmup):
         step()
@@ -414,7 +427,26 @@ def reference(args, rank, world, local):
         dist.barrier()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     clocks = sampler.stop() if rank == 0 else None
-    return ms, clocks
+    e2e = None
+    if not args.no_e2e:
+        host = [b.cpu().pin_memory() for b in batches]
+        float(step(host).item())
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            float(step(host).item())  # device -> host read of the step's result
+        f1.record()
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+        e2e = {"value": args.global_batch / (e_ms / 1000.0), "unit": "samples/s",
+               "h2d_bytes_per_step": int(host[0].numel() * host[0].element_size() * accum * world),
+               "d2h_bytes_per_step": 4 * world, "ms_per_step": e_ms,
+               "path": "reference model/optimizer step on pinned-host batches moved by batch.to(device) "
+                       "(its PreProcessor) + loss.item() each step"}
+    return ms, clocks, e2e
 
 
 # ----------------------------------------------------------------------------- main
@@ -433,13 +465,13 @@ def main():
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "reference source not present in baseline/_ref"}))
             return
-        ms, clocks = res
+        ms, clocks, e2e = res
         if rank == 0:
             print(json.dumps({
                 "impl": "reference", "metric": METRIC, "value": args.global_batch / (ms / 1000.0),
                 "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic", "clocks": clocks,
+                "dtype": "bf16", "data": "synthetic", "clocks": clocks, "e2e": e2e,
                 "config": {"model": "swin-p4-e1024-d16", "global_batch": args.global_batch, "seq_len": 64800,
                            "parallelism": f"dp{world}", "path": "reference vanilla (no TE), torch.compile'd helpers, DDP"},
             }))

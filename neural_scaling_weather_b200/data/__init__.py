@@ -8,7 +8,8 @@
 
 from __future__ import annotations
 
-from typing import Optional, Tuple, Union
+from collections import deque
+from typing import Deque, Iterable, Iterator, Optional, Tuple, Union
 
 import torch
 import torch.nn as nn
@@ -43,6 +44,49 @@ def get_data_loader(cfg, dataset, mode: str = "train"):
     from .era5hdf5 import make_hdf5_loader
 
     return make_hdf5_loader(cfg, dataset, mode)
+
+
+def device_prefetch(batches: Iterable[torch.Tensor], device, depth: int = 1) -> Iterator[torch.Tensor]:
+    """Yield ``batches`` on ``device``, copying the next ``depth`` host batches on a side stream
+    while the current one is consumed (the role of the DALI pipeline's device prefetch queue,
+    ``utils/dataloaders/era5hdf5_dali.py:70-100`` of the reference).  Host batches should be pinned for the copies to be
+    asynchronous; batches already on the device, and every batch when ``device`` is not CUDA,
+    pass through unchanged."""
+    device = torch.device(device)
+    if device.type != "cuda":
+        yield from batches
+        return
+    it = iter(batches)
+    stream = torch.cuda.Stream(device=device)
+    pending: Deque = deque()
+
+    def issue() -> bool:
+        try:
+            b = next(it)
+        except StopIteration:
+            return False
+        if b.is_cuda:
+            pending.append((b, None))
+            return True
+        stream.wait_stream(torch.cuda.current_stream(device))  # the buffer it reuses is free
+        with torch.cuda.stream(stream):
+            d = b.to(device, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        pending.append((d, ev))
+        return True
+
+    for _ in range(depth):
+        if not issue():
+            break
+    while pending:
+        d, ev = pending.popleft()
+        cur = torch.cuda.current_stream(device)
+        if ev is not None:
+            cur.wait_event(ev)
+            d.record_stream(cur)  # allocated on the copy stream, used on the compute stream
+        issue()
+        yield d
 
 
 def get_preprocessor(cfg, dataset):

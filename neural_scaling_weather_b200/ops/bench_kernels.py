@@ -66,11 +66,11 @@ def bench_gemm(a):
     M, N, K = a.M, a.N, a.K
     A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
-    bias = torch.randn(N, device="cuda") if a.epilogue in ("bias", "gelu") else None
-    pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16) if a.epilogue == "gelu" else None
-    res = torch.randn(M, N, device="cuda", dtype=torch.bfloat16) if a.epilogue == "residual" else None
-    act = 1 if a.epilogue == "gelu" else 0
-    fn = lambda: ext.gemm(A, B, bias, res, 0, act, pre)  # noqa: E731
+    bias = torch.randn(N, device="cuda") if a.epilogue in ("bias", "gelu", "gelu_grad") else None
+    pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16) if a.epilogue in ("gelu", "gelu_grad") else None
+    res = torch.randn(M, N, device="cuda", dtype=torch.bfloat16) if a.epilogue in ("residual", "aux") else None
+    act = {"gelu": 1, "gelu_grad": 3, "aux": 4}.get(a.epilogue, 0)
+    fn = lambda: ext.gemm(A, B, bias, res, 0, act, pre, impl=a.impl)  # noqa: E731
     ms = timeit(fn, a.iters)
     nbytes = 2 * (M * K + N * K + M * N * (1 + (pre is not None) + (res is not None)))
     r = report(f"gemm_tcgen05[{a.epilogue}] {M}x{N}x{K}", ms, 2.0 * M * N * K, nbytes)
@@ -189,7 +189,7 @@ def main():
     ap.add_argument("--H", type=int, default=180)
     ap.add_argument("--W", type=int, default=360)
     ap.add_argument("--heads", type=int, default=16)
-    ap.add_argument("--epilogue", default="bias", choices=["none", "bias", "gelu", "residual"])
+    ap.add_argument("--epilogue", default="bias", choices=["none", "bias", "gelu", "gelu_grad", "residual", "aux"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true")
     ap.add_argument("--impl", type=int, default=0,

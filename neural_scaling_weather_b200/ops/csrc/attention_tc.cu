@@ -1,25 +1,18 @@
-// Shifted-window attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Shifted-window attention on the 5th-generation tensor cores (tcgen05 + TMEM), forward and
+// backward, specialised for head_dim 64 and windows of at most 176 tokens (T*wh*ww <= 176).
 //
-// Same contract and numerics as the mma.sync forward in attention.cu (gathered window
-// tokens by index arithmetic, QK-RMSNorm in shared memory, additive -100 latitude-wrap
-// mask, exp2-domain softmax, log2-domain LSE for the backward), specialised for the
-// production geometry: head_dim 64 and windows of at most 176 tokens (T*wh*ww <= 176).
-//
-// One CTA of 4 warps owns one (window, head); two CTAs fit per SM (76 KB smem, 256 TMEM
-// columns each).  Per 128-row query tile t (one or two tiles):
-//   S_t = Qhat_t Khat^T        tcgen05.mma kind::f16, M=128, N=NK (keys rounded to 16),
-//                              both operands K-major 128-byte-swizzled smem, fp32 in TMEM;
-//   softmax                    each thread owns one query row (its TMEM lane): reads S in
-//                              16-column chunks (tcgen05.ld), row max, exp2, row sum, and
-//                              writes P as packed bf16 pairs back over the front of S
-//                              (tcgen05.st) -- P never touches shared memory;
-//   O_t = P_t V                tcgen05.mma with A read from TMEM and B = V as an MN-major
-//                              swizzled smem operand (V rows are keys with d contiguous,
-//                              exactly the MN-major canonical layout), fp32 in TMEM;
-//   epilogue                   tcgen05.ld of the O row, 1/rowsum, bf16, 16-byte stores to
-//                              the token's grid position; LSE per row.
-// One mbarrier tracks the MMA completions (tcgen05.commit); its waits are bounded by a
-// %globaltimer budget and record kErrWaitTimeout in the device error word on expiry.
+// Same contract and numerics as the mma.sync kernels in attention.cu (QK-RMSNorm, additive -100
+// latitude-wrap mask, exp2-domain softmax, log2-domain LSE in window order for the backward).
+// Both kernels are persistent (one CTA of 16 warps per SM walking (window, head) items, heads
+// fastest) and bring a window's q/k/v rows in with TMA box loads of a 4-D [B*T, H, W, C] view of
+// the token-major activations: one box per time step, split where the shifted window wraps at
+// the grid edge, so shift, partition and reverse are never materialised.  S, P, O and the
+// gradients live in TMEM; operands are 128-byte-swizzled shared-memory tiles (K-major, or
+// MN-major where a transpose is needed).  Every mbarrier wait is bounded by a %globaltimer
+// budget and records kErrWaitTimeout in the device error word on expiry.
+// Reference behaviour: models/swin_helpers.py:27-70 (window_partition / window_reverse),
+// :203-250 (WindowAttention.forward: QK norm, scaled_dot_product_attention with the mask) and
+// :380-420 (the shifted block's roll and attn_mask).
 #include <float.h>
 
 #include "common.cuh"
@@ -34,22 +27,8 @@ namespace attn_tc {
 constexpr int HD = 64;
 constexpr int ROW_B = HD * 2;        // 128 bytes per row (one swizzle row)
 constexpr int MAXL = 176;            // keys padded to a multiple of 16, at most 176
-constexpr int Q_ROWS = 256;          // two query tiles of 128
-constexpr int O_COL = 192;           // TMEM column of the O accumulator
-constexpr int TMEM_COLS = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;
-
-struct __align__(1024) Smem {
-  unsigned char q[Q_ROWS * ROW_B];  // 32 KB, K-major SW128 (two M=128 tiles)
-  unsigned char k[MAXL * ROW_B];    // 22 KB, K-major SW128 (B of S = Q K^T)
-  unsigned char v[MAXL * ROW_B];    // 22 KB, MN-major SW128 (B of O = P V)
-  int tok[MAXL];
-  signed char lab[MAXL];
-  uint64_t bar;
-  uint32_t tmem_base;
-  int aborted;
-};
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(row * ROW_B + ((chunk ^ (row & 7)) << 4));
@@ -173,206 +152,6 @@ __device__ __forceinline__ int label(const AttnGeom& g, const WinPos& p, int i) 
   const int iy = (i % (g.wh * g.ww)) / g.ww;
   return g.row_offset + p.wy * g.wh + iy >= g.h_global - g.mask_shift ? 1 : 0;
 }
-
-__global__ void __launch_bounds__(128, 2)
-    fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
-               __nv_bfloat16* __restrict__ out, float* __restrict__ lse, AttnGeom g, int* err) {
-  extern __shared__ unsigned char smem_raw[];
-  Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int L = g.T * g.wh * g.ww;
-  const int NK = (L + 15) & ~15;
-  const int ntiles = (L + 127) / 128;
-  const int bw = blockIdx.x, h = blockIdx.y;
-  const int nww = g.W / g.ww, nwh = g.H / g.wh;
-  WinPos p;
-  p.wx = bw % nww;
-  p.wy = (bw / nww) % nwh;
-  p.b = bw / (nww * nwh);
-
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar)));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  // token table and labels
-  const int lab0 = label(g, p, 0);
-  int mixed = 0;
-  for (int i = tid; i < MAXL; i += blockDim.x) {
-    S.tok[i] = i < L ? (int)token(g, p, i) : 0;
-    const int lb = i < L ? label(g, p, i) : -1;
-    S.lab[i] = (signed char)lb;
-    mixed |= (i < L && lb != lab0);
-  }
-  mixed = __syncthreads_or(mixed);
-
-  // gather Q (256 rows), K and V (NK rows) into the swizzled layouts; zero the padding
-  const int64_t C = (int64_t)g.nh * HD;
-  const __nv_bfloat16* base = qkv + (int64_t)h * HD;
-  for (int idx = tid; idx < (Q_ROWS + 2 * MAXL) * 8; idx += blockDim.x) {
-    const int row_all = idx >> 3, c = idx & 7;
-    unsigned char* dst;
-    int r, part;
-    if (row_all < Q_ROWS) {
-      r = row_all;
-      part = 0;
-      dst = S.q + swz(r, c);
-    } else if (row_all < Q_ROWS + MAXL) {
-      r = row_all - Q_ROWS;
-      part = 1;
-      dst = S.k + swz(r, c);
-    } else {
-      r = row_all - Q_ROWS - MAXL;
-      part = 2;
-      dst = S.v + swz(r, c);
-    }
-    if (r < L) {
-      const __nv_bfloat16* src = base + (int64_t)S.tok[r] * g.qkv_stride + part * C + c * 8;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-    } else {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
-  // QK-RMSNorm in place (thread per row)
-  for (int rr = tid; rr < 2 * L; rr += blockDim.x) {
-    const bool isq = rr < L;
-    const int r = isq ? rr : rr - L;
-    unsigned char* row = isq ? S.q : S.k;
-    const float* w = isq ? qw : kw;
-    float f[8][8];
-    float ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(row + swz(r, c)), f[c]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss += f[c][i] * f[c][i];
-    }
-    const float rs = rsqrtf(ss / (float)HD + FLT_EPSILON);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) f[c][i] *= rs * __ldg(w + c * 8 + i);
-      *reinterpret_cast<uint4*>(row + swz(r, c)) = pack8<__nv_bfloat16>(f[c]);
-    }
-  }
-  // generic-proxy smem writes -> visible to the tensor core (async proxy)
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tmem = S.tmem_base;
-  const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NK >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-  const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
-                        ((uint32_t)(128 >> 4) << 24);
-  const float sl2 = g.scale * kLog2e;
-  const float ml2 = -100.f * kLog2e;
-  uint32_t parity = 0;
-  bool ok = true;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-  for (int t = 0; t < ntiles && ok; ++t) {
-    if (tid == 0) {
-      fence_after();
-#pragma unroll
-      for (int ks = 0; ks < HD / 16; ++ks)
-        mma_ss(tmem, desc_kmajor(S.q + t * 128 * ROW_B + ks * 32), desc_kmajor(S.k + ks * 32), id_s, ks > 0);
-      commit(&S.bar);
-    }
-    __syncwarp();
-    ok = __syncthreads_and(wait_bar(&S.bar, parity, err));  // CTA-uniform outcome
-    parity ^= 1;
-    if (!ok) break;
-    fence_after();
-    // ---- softmax of row r (this thread's TMEM lane)
-    const int r = t * 128 + warp * 32 + lane;
-    const int lr = r < L ? S.lab[r] : 0;
-    const uint32_t trow = tmem + lane_base;
-    float m = -INFINITY;
-    for (int j = 0; j < NK / 16; ++j) {
-      float v[16];
-      ld16(trow + 16 * j, v);
-      const bool plain = !mixed && 16 * j + 16 <= L;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float s = v[i] * sl2;
-        if (!plain) {
-          const int key = 16 * j + i;
-          const int lk = S.lab[key];
-          if (lk < 0) s = -INFINITY;
-          else if (lk != lr) s += ml2;
-        }
-        m = fmaxf(m, s);
-      }
-    }
-    float l = 0.f;
-    for (int j = 0; j < NK / 16; ++j) {
-      float v[16];
-      ld16(trow + 16 * j, v);
-      const bool plain = !mixed && 16 * j + 16 <= L;
-      uint32_t pk[8];
-#pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        float s0 = v[i] * sl2, s1 = v[i + 1] * sl2;
-        if (!plain) {
-          const int k0 = 16 * j + i;
-          const int l0 = S.lab[k0], l1 = S.lab[k0 + 1];
-          if (l0 < 0) s0 = -INFINITY;
-          else if (l0 != lr) s0 += ml2;
-          if (l1 < 0) s1 = -INFINITY;
-          else if (l1 != lr) s1 += ml2;
-        }
-        const float p0 = ex2(s0 - m), p1 = ex2(s1 - m);
-        l += p0 + p1;
-        pk[i >> 1] = pack_bf16(p0, p1);
-      }
-      st8(trow + 8 * j, pk);  // P over the front of S: column 8j < 16j, already read
-    }
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    fence_before();
-    __syncthreads();
-    // ---- O = P V
-    if (tid == 0) {
-      fence_after();
-      for (int ks = 0; ks < NK / 16; ++ks)
-        mma_ts(tmem + O_COL, tmem + 8 * ks, desc_mnmajor(S.v + ks * 16 * ROW_B), id_o, ks > 0);
-      commit(&S.bar);
-    }
-    __syncwarp();
-    ok = __syncthreads_and(wait_bar(&S.bar, parity, err));
-    parity ^= 1;
-    if (!ok) break;
-    fence_after();
-    float o[64];
-    ld32(trow + O_COL, o);
-    ld32(trow + O_COL + 32, o + 32);
-    if (r < L) {
-      const float il = 1.f / l;
-      __nv_bfloat16* dst = out + (int64_t)S.tok[r] * g.out_stride + (int64_t)h * HD;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float f8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f8[i] = o[c * 8 + i] * il;
-        reinterpret_cast<uint4*>(dst)[c] = pack8<__nv_bfloat16>(f8);
-      }
-      lse[((int64_t)bw * g.nh + h) * L + r] = m + __log2f(l);
-    }
-    fence_before();
-    __syncthreads();  // S/P and O columns are reused by the next tile
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
-}
-
 
 // ============================================================================ backward
 // Persistent: one CTA (16 warps) per SM walks a contiguous range of (window, head) items, heads
@@ -695,7 +474,7 @@ __device__ __forceinline__ void load_window(unsigned char* buf, const BoxMaps& m
 
 // Token rows and mask labels of window `w`; returns whether the window mixes labels.
 __device__ __forceinline__ int build_table(const AttnGeom& g, int64_t w, int nww, int nwh, int L, int* tok,
-                                           signed char* lab, int tid) {
+                                           signed char* lab, int tid, short* wr = nullptr) {
   WinPos p;
   p.wx = (int)(w % nww);
   p.wy = (int)((w / nww) % nwh);
@@ -705,6 +484,7 @@ __device__ __forceinline__ int build_table(const AttnGeom& g, int64_t w, int nww
   int mx = 0;
   for (int j = tid; j < MAXL; j += BWD_THREADS) {
     const int i = j < L ? win_row(g, wl, j) : 0;
+    if (wr) wr[j] = (short)i;
     tok[j] = j < L ? (int)token(g, p, i) : 0;
     const int lb = j < L ? label(g, p, i) : -1;
     lab[j] = (signed char)lb;
@@ -1104,6 +884,361 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BWD_TMEM_COLS));
 }
 
+// ============================================================================ forward
+// Persistent: one CTA (16 warps) per SM walks a contiguous range of (window, head) items, heads
+// fastest (the backward's order).  The q, k and v rows of item i+1 arrive by TMA box loads into
+// the second buffer set while item i computes.  Warp w reads TMEM lanes 32*(w%4).. and column
+// group w/4, as in the backward.  Query tile 0 is rows [0,128), tile 1 rows [NK-128, NK) (its
+// rows < 128 are computed again and not stored).  Per item:
+//   QK-RMSNorm of the q and k rows in place (two threads per row)
+//   S_t = Qhat_t Khat^T     both tiles issued at once -> TMEM S_COL[t] (K-major operands)
+//   softmax of tile t       row max and row sum combined over the four column groups through
+//                           shared memory; P = exp2(S*scale*log2e + mask - max) packed to bf16
+//                           over the front of S_t in TMEM (tcgen05.st)
+//   O_t = P_t V             A = P from TMEM, B = V MN-major -> TMEM O_COL[t]; tile 0's O
+//                           product runs during tile 1's softmax
+//   epilogue                O/rowsum to bf16 rows in shared memory, then whole 128-byte rows to
+//                           each token's position; lse = max + log2(sum) in window order
+constexpr int FWD_THREADS = 512;
+constexpr int FWD_TMEM_COLS = 512;
+__device__ __forceinline__ uint32_t s_col(int t) { return t == 0 ? 0u : 192u; }
+__device__ __forceinline__ uint32_t o_col(int t) { return t == 0 ? 384u : 448u; }
+
+struct __align__(1024) SmemF {
+  unsigned char q[2][ROWBUF];  // item-parity buffer sets; K-major SW128 rows, normalized in place
+  unsigned char k[2][ROWBUF];
+  unsigned char v[2][ROWBUF];  // MN-major B operand of O = P V (the same SW128 rows)
+  unsigned char stg[2][128 * ROW_B];  // bf16 O rows of query tile 0 / 1
+  int tok[2][MAXL];
+  short wr[2][MAXL];  // window-order index of smem row j (the lse layout)
+  signed char lab[2][MAXL];
+  float red[2][4][128];  // per-column-group row max / row sum
+  float qwv[HD];
+  float kwv[HD];
+  uint64_t bar_s[2];  // S of query tile 0 / 1 complete
+  uint64_t bar_o[2];  // O of query tile 0 / 1 complete
+  uint64_t bar_ld;    // an item's q/k/v rows landed
+  uint32_t tmem_base;
+};
+
+// Scaled, masked logits (log2 domain; padding keys -inf) of this warp's keys [16 c0, 16 (c0 + NCH))
+// of one row, read from TMEM.
+template <int NCH>
+__device__ __forceinline__ void logits(uint32_t taddr, const signed char* lab, int c0, int lr, float sl2, float ml2,
+                                       int mixed, int L, float* sv) {
+  ld_cols<NCH>(taddr + 16 * c0, sv);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int j = c0 + c;
+    if (!mixed && 16 * j + 16 <= L) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sv[16 * c + i] *= sl2;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int lk = lab[16 * j + i];
+        sv[16 * c + i] = lk < 0 ? -INFINITY : fmaf(sv[16 * c + i], sl2, lk != lr ? ml2 : 0.f);
+      }
+    }
+  }
+}
+
+template <int NCH>
+__device__ __forceinline__ float row_max(uint32_t taddr, const signed char* lab, int c0, int lr, float sl2, float ml2,
+                                         int mixed, int L) {
+  float sv[16 * NCH];
+  logits<NCH>(taddr, lab, c0, lr, sl2, ml2, mixed, L, sv);
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 16 * NCH; ++i) m = fmaxf(m, sv[i]);
+  return m;
+}
+
+// P = exp2(s - m) of the same keys (logits read again from TMEM rather than kept in registers
+// across the block barrier), packed to bf16 pairs in pk; returns their fp32 sum.
+template <int NCH>
+__device__ __forceinline__ float probs(uint32_t taddr, const signed char* lab, int c0, int lr, float sl2, float ml2,
+                                       int mixed, int L, float m, uint32_t* pk) {
+  float sv[16 * NCH];
+  logits<NCH>(taddr, lab, c0, lr, sl2, ml2, mixed, L, sv);
+  float l = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8 * NCH; ++i) {
+    const float p0 = ex2(sv[2 * i] - m), p1 = ex2(sv[2 * i + 1] - m);
+    l += p0 + p1;
+    pk[i] = pack_bf16(p0, p1);
+  }
+  return l;
+}
+
+template <int NCH>
+__device__ __forceinline__ void store_p(uint32_t taddr, int c0, const uint32_t* pk) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) st8(taddr + 8 * (c0 + c), pk + 8 * c);
+}
+
+__global__ void __launch_bounds__(FWD_THREADS, 1)
+    fwd_kernel(const __grid_constant__ BoxMaps box_qkv, const float* __restrict__ qw, const float* __restrict__ kw,
+               __nv_bfloat16* __restrict__ out, float* __restrict__ lse, AttnGeom g, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  SmemF& S = *reinterpret_cast<SmemF*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lg = warp & 3;   // TMEM lane quarter
+  const int cg = warp >> 2;  // column group: keys [48 cg, 48 cg + 48), O columns [16 cg, 16 cg + 16)
+  const int L = g.T * g.wh * g.ww;
+  const int NK = (L + 15) & ~15;
+  const int ntiles = (L + 127) / 128;
+  const int nww = g.W / g.ww, nwh = g.H / g.wh;
+  const int C = g.nh * HD;
+  const int64_t n_items = (int64_t)g.B * nwh * nww * g.nh;
+  const int64_t i_begin = n_items * blockIdx.x / gridDim.x;
+  const int64_t i_end = n_items * (blockIdx.x + 1) / gridDim.x;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+                 "r"(FWD_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int t = 0; t < 2; ++t) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar_s[t])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar_o[t])));
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&S.bar_ld)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // rows [L, max(NK,128)) of every operand buffer stay zero (the loads write rows < L only)
+  const int pad_rows = max(NK, 128);
+  for (int idx = tid; idx < (pad_rows - L) * 8; idx += FWD_THREADS) {
+    const int r = L + (idx >> 3), c = idx & 7;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int b2 = 0; b2 < 2; ++b2) {
+      *reinterpret_cast<uint4*>(S.q[b2] + swz(r, c)) = z;
+      *reinterpret_cast<uint4*>(S.k[b2] + swz(r, c)) = z;
+      *reinterpret_cast<uint4*>(S.v[b2] + swz(r, c)) = z;
+    }
+  }
+  if (tid < HD) {
+    S.qwv[tid] = qw[tid];
+    S.kwv[tid] = kw[tid];
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem_base;
+  const uint32_t trow = tmem + ((uint32_t)(lg * 32) << 16);
+  const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NK >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                        ((uint32_t)(128 >> 4) << 24);
+  const float sl2 = g.scale * kLog2e;
+  const float ml2 = -100.f * kLog2e;
+  const int rt = lg * 32 + lane;  // row within a 128-row tile
+  const int c0 = 3 * cg, nch = max(0, min(3, NK / 16 - c0));
+  uint32_t ph = 0, ld_parity = 0;
+  bool ok = true;
+  bool ld_pending = false;
+  int tcur = 0;
+  int64_t win = i_begin / g.nh;
+  int mixed = 0;
+  if (i_begin < i_end) {
+    mixed = build_table(g, win, nww, nwh, L, S.tok[0], S.lab[0], tid, S.wr[0]);
+    if (tid == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.bar_ld)),
+                   "r"(3 * L * ROW_B)
+                   : "memory");
+    __syncthreads();
+    ld_pending = true;
+    if (lane == 0 && warp < 3) {
+      const int h0 = (int)(i_begin - win * g.nh);
+      unsigned char* buf = warp == 0 ? S.q[0] : warp == 1 ? S.k[0] : S.v[0];
+      load_window(buf, box_qkv, &S.bar_ld, warp * C + h0 * HD, win_load(g, win, nww, nwh), g);
+    }
+  }
+
+  int b = 0;  // buffer set of the current item
+  for (int64_t item = i_begin; item < i_end && ok; ++item) {
+    const int h = (int)(item - win * g.nh);
+    const bool has_next = item + 1 < i_end;
+    const int64_t nwin = (item + 1) / g.nh;
+    const int ntab = nwin == win ? tcur : 1 - tcur;
+    int mixed_n = mixed;
+    const int* tok = S.tok[tcur];
+    const short* wr = S.wr[tcur];
+    const signed char* lab = S.lab[tcur];
+    unsigned char* qb_ = S.q[b];
+    unsigned char* kb_ = S.k[b];
+    ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar_ld, ld_parity, err) : true);
+    ld_parity ^= 1;
+    ld_pending = false;
+    if (!ok) break;
+    // the next item's table and rows: its buffer set was last read by this CTA's previous
+    // item, whose MMAs have all completed
+    if (has_next) {
+      if (nwin != win) mixed_n = build_table(g, nwin, nww, nwh, L, S.tok[ntab], S.lab[ntab], tid, S.wr[ntab]);
+      if (tid == 0)
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.bar_ld)),
+                     "r"(3 * L * ROW_B)
+                     : "memory");
+      __syncthreads();
+      ld_pending = true;
+      if (lane == 0 && warp < 3) {
+        const int nh_ = (int)(item + 1 - nwin * g.nh);
+        unsigned char* buf = warp == 0 ? S.q[1 - b] : warp == 1 ? S.k[1 - b] : S.v[1 - b];
+        load_window(buf, box_qkv, &S.bar_ld, warp * C + nh_ * HD, win_load(g, nwin, nww, nwh), g);
+      }
+    }
+    // QK-RMSNorm in place, two threads per row (four 16-byte chunks each)
+    for (int base = 0; base < 4 * L; base += FWD_THREADS) {
+      const int idx = base + tid;
+      const bool act = idx < 4 * L;
+      const int rr = act ? idx >> 1 : 0, half = idx & 1;
+      const bool isq = rr < L;
+      const int r = isq ? rr : rr - L;
+      unsigned char* row = isq ? qb_ : kb_;
+      const float* w = isq ? S.qwv : S.kwv;
+      float f[4][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(row + swz(r, 4 * half + c)), f[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += f[c][i] * f[c][i];
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float rs = rsqrtf(ss / (float)HD + FLT_EPSILON);
+      if (act) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[c][i] *= rs * w[(4 * half + c) * 8 + i];
+          *reinterpret_cast<uint4*>(row + swz(r, 4 * half + c)) = pack8<__nv_bfloat16>(f[c]);
+        }
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      fence_after();
+      for (int t = 0; t < ntiles; ++t) {
+        const int qrow = t == 0 ? 0 : NK - 128;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_ss(tmem + s_col(t), desc_kmajor(qb_ + qrow * ROW_B + ks * 32), desc_kmajor(kb_ + ks * 32), id_s,
+                 ks > 0);
+        commit(&S.bar_s[t]);
+      }
+    }
+    __syncwarp();
+    float m_t[2] = {0.f, 0.f}, l_t[2] = {1.f, 1.f};
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t >= ntiles) break;
+      const int qrow = t == 0 ? 0 : NK - 128;
+      const int lo = t * 128;
+      const int r = qrow + rt;
+      const int lr = r < L ? lab[r] : 0;
+      // warps whose rows are all padding, or all recomputed rows of tile 1, skip the softmax:
+      // each O row depends on its own P row only, and those rows are not stored
+      const bool warp_live = qrow + lg * 32 + 31 >= lo && qrow + lg * 32 < L;  // warp-uniform
+      ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar_s[t], ph, err) : true);
+      if (!ok) break;
+      fence_after();
+      uint32_t pk[24];
+      float mx = -INFINITY;
+      const uint32_t ts = trow + s_col(t);
+      if (warp_live) {
+        if (nch == 3) mx = row_max<3>(ts, lab, c0, lr, sl2, ml2, mixed, L);
+        else if (nch == 2) mx = row_max<2>(ts, lab, c0, lr, sl2, ml2, mixed, L);
+        else if (nch == 1) mx = row_max<1>(ts, lab, c0, lr, sl2, ml2, mixed, L);
+      }
+      S.red[0][cg][rt] = mx;
+      __syncthreads();
+      const float m = fmaxf(fmaxf(S.red[0][0][rt], S.red[0][1][rt]), fmaxf(S.red[0][2][rt], S.red[0][3][rt]));
+      float ls = 0.f;
+      if (warp_live) {
+        if (nch == 3) ls = probs<3>(ts, lab, c0, lr, sl2, ml2, mixed, L, m, pk);
+        else if (nch == 2) ls = probs<2>(ts, lab, c0, lr, sl2, ml2, mixed, L, m, pk);
+        else if (nch == 1) ls = probs<1>(ts, lab, c0, lr, sl2, ml2, mixed, L, m, pk);
+      }
+      S.red[1][cg][rt] = ls;
+      // every warp's logits of this tile are read: P may overwrite the front of S
+      fence_before();
+      __syncthreads();
+      fence_after();
+      m_t[t] = m;
+      l_t[t] = S.red[1][0][rt] + S.red[1][1][rt] + S.red[1][2][rt] + S.red[1][3][rt];
+      if (warp_live) {
+        if (nch == 3) store_p<3>(ts, c0, pk);
+        else if (nch == 2) store_p<2>(ts, c0, pk);
+        else if (nch == 1) store_p<1>(ts, c0, pk);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        fence_after();
+        for (int ks = 0; ks < NK / 16; ++ks)
+          mma_ts(tmem + o_col(t), tmem + s_col(t) + 8 * ks, desc_mnmajor(S.v[b] + ks * 16 * ROW_B), id_o, ks > 0);
+        commit(&S.bar_o[t]);
+      }
+      __syncwarp();
+    }
+    if (!ok) break;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t >= ntiles) break;
+      const int qrow = t == 0 ? 0 : NK - 128;
+      const int lo = t * 128;
+      const int r = qrow + rt;
+      const bool warp_live = qrow + lg * 32 + 31 >= lo && qrow + lg * 32 < L;  // warp-uniform
+      ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar_o[t], ph, err) : true);
+      if (!ok) break;
+      fence_after();
+      unsigned char* st = S.stg[t];
+      if (warp_live) {
+        float o[16];
+        ld16(trow + o_col(t) + 16 * cg, o);
+        const float il = 1.f / l_t[t];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] *= il;
+        *reinterpret_cast<uint4*>(st + swz(rt, 2 * cg)) = pack8<__nv_bfloat16>(o);
+        *reinterpret_cast<uint4*>(st + swz(rt, 2 * cg + 1)) = pack8<__nv_bfloat16>(o + 8);
+        if (cg == 0 && r >= lo && r < L) lse[item * L + wr[r]] = m_t[t] + __log2f(l_t[t]);
+      }
+      __syncthreads();
+      const int c = tid & 7;
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int row = (tid >> 3) + 64 * k2;
+        const int rr = qrow + row;
+        if (rr >= lo && rr < L)
+          *reinterpret_cast<uint4*>(out + (int64_t)tok[rr] * g.out_stride + (int64_t)h * HD + 8 * c) =
+              *reinterpret_cast<const uint4*>(st + swz(row, c));
+      }
+    }
+    if (!ok) break;
+    ph ^= 1;
+    b ^= 1;
+    tcur = ntab;
+    win = nwin;
+    mixed = mixed_n;
+    fence_before();
+    __syncthreads();  // S, O and the staging rows are rewritten by the next item
+    fence_after();
+  }
+  // after an error, let loads still in flight land before the shared memory is released
+  // (bounded; a second timeout is not recorded again)
+  if (!ok && ld_pending && tid == 0) wait_bar(&S.bar_ld, ld_parity, nullptr);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FWD_TMEM_COLS));
+}
+
 }  // namespace attn_tc
 
 bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype) {
@@ -1194,11 +1329,19 @@ cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw
 
 cudaError_t window_attn_fwd_tc(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
                                const AttnGeom& g, cudaStream_t s) {
-  const size_t smem = sizeof(attn_tc::Smem) + 1024;
+  const size_t smem = sizeof(attn_tc::SmemF) + 1024;
   auto k = attn_tc::fwd_kernel;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid(g.B * (g.H / g.wh) * (g.W / g.ww), g.nh);
-  k<<<grid, 128, smem, s>>>((const __nv_bfloat16*)qkv, qw, kw, (__nv_bfloat16*)out, lse, g, device_error_flag());
+  int dev = 0, sms = 0;
+  NSW_CUDA_CHECK(cudaGetDevice(&dev));
+  NSW_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t n_tok = (int64_t)g.B * g.T * g.H * g.W;
+  if (n_tok >= (1LL << 31) - 1) return cudaErrorInvalidValue;
+  attn_tc::BoxMaps b_qkv;
+  if (!window_box_maps(&b_qkv, qkv, g, g.qkv_stride)) return cudaErrorInvalidValue;
+  const int64_t items = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww) * g.nh;
+  const int grid = (int)std::min<int64_t>(items, sms);
+  k<<<grid, attn_tc::FWD_THREADS, smem, s>>>(b_qkv, qw, kw, (__nv_bfloat16*)out, lse, g, device_error_flag());
   return cudaGetLastError();
 }
 

@@ -27,23 +27,9 @@ def _cdtype(x: torch.Tensor) -> torch.dtype:
     return x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
 
 
-_wt_cache = {}
-
-
 def _weight_t(params: Sequence[torch.Tensor], w: torch.Tensor) -> torch.Tensor:
-    """Cached contiguous transpose of a (concatenated) weight, keyed on versions."""
-    if not all(isinstance(p, torch.nn.Parameter) for p in params):
-        return w.t().contiguous()
-    key = tuple(id(p) for p in params)
-    ver = tuple(p._version for p in params)
-    hit = _wt_cache.get(key)
-    if hit is not None and hit[0] == ver and hit[1].dtype == w.dtype:
-        return hit[1]
-    t = w.t().contiguous()
-    _wt_cache[key] = (ver, t)
-    ps, dt, n, k = list(params), w.dtype, t.shape[1], t.shape[0]
-    wcache.register_derived(("T", key), ps, t, lambda: wcache.get_cat(ps, dt).reshape(n, k).t())
-    return t
+    """Cached contiguous transpose of a (concatenated) weight, keyed on the live parameters."""
+    return wcache.get_t(params, w)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, residual=None, res_period: int = 0,
@@ -169,6 +155,8 @@ class _Linear(torch.autograd.Function):
         N = W.shape[0]
         dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
         du = ext.gelu_bwd(dy2, pre) if ctx.act else dy2
+        # bias gradient first: the rows of du written last are still in L2
+        db = ext.col_sum(du) if ctx.nb else None
         dx = None
         if ctx.needs_input_grad[0]:
             Wt = _weight_t(ctx.params, W)
@@ -182,7 +170,6 @@ class _Linear(torch.autograd.Function):
             off += n
         grads_b: List[torch.Tensor] = []
         if ctx.nb:
-            db = ext.col_sum(du)
             off = 0
             for n in ctx.bsizes:
                 grads_b.append(db[off:off + n])
@@ -247,8 +234,8 @@ class _MLP(torch.autograd.Function):
         x2, u, h = ctx.saved_tensors
         N = ctx.W2.shape[0]
         dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
+        db2 = ext.col_sum(dy2)  # before the GEMMs: the rows of dy written last are still in L2
         dW2 = wgrad(dy2, h)
-        db2 = ext.col_sum(dy2)
         W2t = _weight_t([ctx.w2], ctx.W2)
         if ctx.aux_is_grad:
             if ext.gemm_supported(dy2, W2t, False):
@@ -259,8 +246,8 @@ class _MLP(torch.autograd.Function):
             du = ext.gemm(dy2, W2t, None, u, 0, 2)  # epilogue: * GELU'(u)
         else:
             du = ext.gelu_bwd(gemm(dy2, W2t).contiguous(), u)
-        dW1 = wgrad(du, x2)
         db1 = ext.col_sum(du)
+        dW1 = wgrad(du, x2)
         dx = None
         if ctx.needs_input_grad[0]:
             W1t = _weight_t([ctx.w1], ctx.W1)
@@ -337,8 +324,8 @@ class _PatchEmbed(torch.autograd.Function):
         (cols,) = ctx.saved_tensors
         N, C, H, Wd, p, h, wn, E, xdt, has_add, add_dt, period = ctx.meta
         dy2 = dy.reshape(-1, E).to(cols.dtype).contiguous()
-        dW = wgrad(dy2, cols).view(ctx.w_param.shape)
         db = ext.col_sum(dy2) if ctx.has_b else None
+        dW = wgrad(dy2, cols).view(ctx.w_param.shape)
         dadd = None
         if has_add:
             dadd = dy2.float().view(-1, period, E).sum(0).view(-1, h, wn, E).to(add_dt)
@@ -458,8 +445,8 @@ class _LinearAllReduce(torch.autograd.Function):
         N = W.shape[0]
         dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
         dx = gemm(dy2, _weight_t([ctx.w], W)).view(ctx.x_shape).to(ctx.x_dtype) if ctx.needs_input_grad[0] else None
-        dW = wgrad(dy2, x2).reshape(ctx.w.shape)
         db = ext.col_sum(dy2) if ctx.has_b else None
+        dW = wgrad(dy2, x2).reshape(ctx.w.shape)
         dres = dy.to(ctx.res_dtype) if ctx.res_dtype is not None else None
         return dx, dres, None, dW, db
 

@@ -15,10 +15,13 @@ import torch
 
 # id(param) -> (weak reference to param, shadow); tensors cannot be dict keys by value
 _shadows: Dict[int, Tuple["weakref.ref", torch.Tensor]] = {}
-_cache: Dict[Tuple, Tuple[Tuple[int, ...], torch.Tensor]] = {}
-# derived tensors (concatenations, transposes) with the function that rebuilds them and the
-# parameters they come from; refresh_derived() rewrites them in place after an optimizer step,
-# so a CUDA graph that captured them keeps reading current weights
+# key -> (weak references to the source parameters, their versions, cached tensor).  A hit
+# needs the SAME live parameter objects: ids are reused once a parameter is freed, so an id
+# alone could hand a new model the cached copy of an old one.
+_cache: Dict[Tuple, Tuple[Tuple["weakref.ref", ...], Tuple[int, ...], torch.Tensor]] = {}
+# derived tensors (casts, concatenations, transposes) with the function that rebuilds them and
+# the parameters they come from; refresh_derived() rewrites them in place after an optimizer
+# step, so a CUDA graph that captured them keeps reading current weights
 _derived: Dict[Tuple, Tuple[Tuple["weakref.ref", ...], torch.Tensor, Callable[[], torch.Tensor]]] = {}
 
 
@@ -39,15 +42,34 @@ def clear() -> None:
     _derived.clear()
 
 
-def register_derived(key: Tuple, params: Sequence[torch.Tensor], t: torch.Tensor,
-                     rebuild: Callable[[], torch.Tensor]) -> None:
-    _derived[key] = (tuple(weakref.ref(p) for p in params), t, rebuild)
+def _versions(params: Sequence[torch.Tensor]) -> Tuple[int, ...]:
+    return tuple(p._version for p in params)
+
+
+def _lookup(key: Tuple, params: Sequence[torch.Tensor]):
+    hit = _cache.get(key)
+    if hit is None:
+        return None
+    refs, ver, t = hit
+    if len(refs) != len(params) or any(r() is not p for r, p in zip(refs, params)):
+        return None
+    if ver != _versions(params) or t.data_ptr() == 0:
+        return None
+    return t
+
+
+def _store(key: Tuple, params: Sequence[torch.Tensor], t: torch.Tensor,
+           rebuild: Callable[[], torch.Tensor]) -> torch.Tensor:
+    refs = tuple(weakref.ref(p) for p in params)
+    _cache[key] = (refs, _versions(params), t)
+    _derived[key] = (refs, t, rebuild)
+    return t
 
 
 def refresh_derived() -> None:
-    """Recompute every cached concatenation / transpose in place (concatenations first: the
-    transposes are built from them) and mark them current.  Called after each optimizer step
-    when training runs from captured CUDA graphs."""
+    """Recompute every cached cast / concatenation / transpose in place (casts and
+    concatenations first: the transposes are built from them) and mark them current.  Called
+    after each optimizer step when training runs from captured CUDA graphs."""
     dead = []
     for order in (0, 1):
         for key, (refs, t, rebuild) in list(_derived.items()):
@@ -59,15 +81,10 @@ def refresh_derived() -> None:
                 continue
             with torch.no_grad():
                 t.copy_(rebuild())
-            ver = tuple(p._version for p in params)
-            if key[0] == "T":
-                from . import fused  # transposes live in the fused operators' cache
-
-                fused._wt_cache[key[1]] = (ver, t)
-            else:
-                _cache[key] = (ver, t)
+            _cache[key] = (refs, _versions(params), t)
     for key in dead:
         _derived.pop(key, None)
+        _cache.pop(key, None)
 
 
 def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
@@ -80,14 +97,10 @@ def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     if sh is not None and sh.dtype == dtype:
         return sh
     key = (id(param), dtype)
-    ver = (param._version,)
-    hit = _cache.get(key)
-    if hit is not None and hit[0] == ver and hit[1].data_ptr() != 0:
-        return hit[1]
-    t = param.detach().to(dtype)
-    _cache[key] = (ver, t)
-    register_derived(key, [param], t, lambda: param.detach().to(dtype))
-    return t
+    t = _lookup(key, [param])
+    if t is not None:
+        return t
+    return _store(key, [param], param.detach().to(dtype), lambda: param.detach().to(dtype))
 
 
 def get_cat(params: Sequence[torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
@@ -96,18 +109,29 @@ def get_cat(params: Sequence[torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
         return get(params[0], dtype)
     if not all(isinstance(p, torch.nn.Parameter) for p in params):
         return torch.cat([p.detach().to(dtype) for p in params], dim=0)
-    key = (tuple(id(p) for p in params), dtype)
-    ver = tuple(p._version for p in params)
-    sh = [_shadow_of(p) for p in params]
-    hit = _cache.get(key)
-    if hit is not None and hit[0] == ver:
-        return hit[1]
-    parts = [s if (s is not None and s.dtype == dtype) else p.detach().to(dtype)
-             for p, s in zip(params, sh)]
-    t = torch.cat(parts, dim=0)
-    _cache[key] = (ver, t)
     ps = list(params)
-    register_derived(key, ps, t, lambda: torch.cat(
-        [s if (s is not None and s.dtype == dtype) else p.detach().to(dtype)
-         for p, s in zip(ps, [_shadow_of(q) for q in ps])], dim=0))
-    return t
+    key = (tuple(id(p) for p in ps), dtype)
+    t = _lookup(key, ps)
+    if t is not None:
+        return t
+
+    def build():
+        return torch.cat([s if (s is not None and s.dtype == dtype) else p.detach().to(dtype)
+                          for p, s in zip(ps, [_shadow_of(q) for q in ps])], dim=0)
+
+    return _store(key, ps, build(), build)
+
+
+def get_t(params: Sequence[torch.Tensor], w: torch.Tensor) -> torch.Tensor:
+    """Contiguous transpose of ``w``, the (concatenated, possibly reshaped) compute-dtype copy
+    of ``params``, cached on the parameters' versions (data-gradient GEMM operand)."""
+    if not all(isinstance(p, torch.nn.Parameter) for p in params):
+        return w.t().contiguous()
+    ps = list(params)
+    key = ("T", tuple(id(p) for p in ps), w.dtype)
+    t = _lookup(key, ps)
+    if t is not None:
+        return t
+    t = w.t().contiguous()
+    dt, n, k = w.dtype, t.shape[1], t.shape[0]
+    return _store(key, ps, t, lambda: get_cat(ps, dt).reshape(n, k).t())

@@ -39,7 +39,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from .. import config as C
-from ..data import get_data_loader, get_dataset, get_preprocessor
+from ..data import device_prefetch, get_data_loader, get_dataset, get_preprocessor
 from ..losses import get_loss, get_metric
 from ..models.swin import get_model, strip_module_prefix
 from ..parallel import comm
@@ -415,7 +415,8 @@ class Trainer:
         if self.epoch == getattr(ds, "ckpt_epoch", -1):
             n_batches = max(0, n_batches - max(ds.resume_skip_batches, ds.iterations_to_skip))
         n_accum = n_batches - (n_batches % self.gradient_accum_steps)
-        for batch_idx, batch in enumerate(self.train_data_loader):
+        # host batches are copied to the device one batch ahead, on a side stream
+        for batch_idx, batch in enumerate(device_prefetch(self.train_data_loader, self.device)):
             if self._nan_seen():
                 logging.warning("NaN detected; stopping")
                 self._stop = True

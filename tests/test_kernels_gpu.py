@@ -296,6 +296,8 @@ TC_CASES = [
     (2, 1, 27, 36, 3, (9, 18), (4, 9), True),
     (1, 1, 16, 32, 2, (8, 16), (4, 8), True),
     (1, 2, 8, 16, 2, (4, 8), (2, 4), True),
+    # several (window, head) items per persistent CTA: head and window changes, next-item loads
+    (1, 1, 90, 360, 4, (9, 18), (4, 9), True),
 ]
 
 
@@ -312,6 +314,7 @@ def test_window_attention_tcgen05_forward(case, _ext_loaded):
     gi = [B, T, H, W, nh, hd, win[0], win[1], shift[0], shift[1], int(mask), shift[0], 0, H]
     out_tc, lse_tc = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 2)
     out_mma, lse_mma = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 1)
+    assert _ext_loaded.read_error_flag(True) == 0
     ref = reference.window_attention(qkv.float(), qw, kw, nh, hd, geom, hd ** -0.5)
     assert rel(out_tc.view_as(ref), ref) < 2e-2
     assert rel(out_tc, out_mma) < 1e-2

@@ -115,3 +115,17 @@ def test_trainer_cuda_graph_matches_eager(tmp_path):
     for a, b in zip(le, lg):
         assert abs(a - b) <= 2e-3 * max(1.0, abs(a)), (le, lg)
     assert rel(pg, pe) < 2e-3
+
+
+def test_device_prefetch_copies_ahead_on_a_side_stream():
+    from neural_scaling_weather_b200.data import device_prefetch
+
+    src = [torch.randn(3, 1000).pin_memory() for _ in range(6)] + [torch.ones(2, device="cuda")]
+    seen = []
+    for i, d in enumerate(device_prefetch(iter(src), "cuda", depth=2)):
+        assert d.is_cuda
+        seen.append(d.clone() * 2)  # consumed on the compute stream
+    torch.cuda.synchronize()
+    assert len(seen) == len(src)
+    for a, b in zip(seen, src):
+        assert torch.equal(a.cpu(), b.cpu() * 2)

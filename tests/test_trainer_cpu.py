@@ -122,3 +122,34 @@ def test_synthetic_loader_semantics():
     assert len(resumed) == len(full) - 5
     assert torch.equal(resumed[0], full[5])
     assert len([x for x in loader2]) == len(full)
+
+
+def test_weight_cache_needs_the_same_live_parameter():
+    """A cached cast / transpose is served only for the parameter object it was made from:
+    ids are reused after a parameter is freed (a new model built in the same process)."""
+    from neural_scaling_weather_b200.ops import weights
+
+    p1 = torch.nn.Parameter(torch.randn(4, 3))
+    t1 = weights.get_t([p1], p1.detach())
+    assert t1.shape == (3, 4)
+    assert weights.get_t([p1], p1.detach()) is t1  # cached
+    refs, ver, t = weights._cache[("T", (id(p1),), torch.float32)]
+    p2 = torch.nn.Parameter(torch.randn(5, 2))
+    # an entry left by another parameter under p2's id is not used
+    weights._cache[("T", (id(p2),), torch.float32)] = (refs, (p2._version,), t)
+    assert weights.get_t([p2], p2.detach()).shape == (2, 5)
+    c1 = weights.get(p1, torch.bfloat16)
+    weights._cache[(id(p2), torch.bfloat16)] = weights._cache[(id(p1), torch.bfloat16)]
+    c2 = weights.get(p2, torch.bfloat16)
+    assert c1.shape == (4, 3) and c2.shape == (5, 2)
+    with torch.no_grad():
+        p1.add_(1.0)  # a new version is rebuilt
+    assert torch.equal(weights.get(p1, torch.bfloat16), p1.detach().to(torch.bfloat16))
+
+
+def test_device_prefetch_passes_through_on_cpu():
+    from neural_scaling_weather_b200.data import device_prefetch
+
+    src = [torch.full((2, 3), float(i)) for i in range(5)]
+    out = list(device_prefetch(iter(src), "cpu"))
+    assert len(out) == 5 and all(a is b for a, b in zip(out, src))
