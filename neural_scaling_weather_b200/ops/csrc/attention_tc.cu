@@ -93,11 +93,12 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 __device__ __forceinline__ void ld16(uint32_t taddr, float* f) {
   uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(r[i]);
 }
@@ -105,13 +106,14 @@ __device__ __forceinline__ void ld32(uint32_t taddr, float* f) {
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]);
 }
@@ -296,6 +298,9 @@ template <>
 __device__ __forceinline__ void ld_cols<2>(uint32_t taddr, float* f) {
   ld32(taddr, f);
 }
+// Two loads and one wait in one statement: the outputs are early-clobber, because the first load
+// writes its registers asynchronously while the second still has to read its address operand;
+// without it the compiler may give that operand a register the first load overwrites.
 template <>
 __device__ __forceinline__ void ld_cols<3>(uint32_t taddr, float* f) {
   uint32_t r[48];
@@ -305,12 +310,12 @@ __device__ __forceinline__ void ld_cols<3>(uint32_t taddr, float* f) {
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47},"
       " [%49];\n"
       "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
+      : "=&r"(r[0]), "=&r"(r[1]), "=&r"(r[2]), "=&r"(r[3]), "=&r"(r[4]), "=&r"(r[5]), "=&r"(r[6]), "=&r"(r[7]),
+        "=&r"(r[8]), "=&r"(r[9]), "=&r"(r[10]), "=&r"(r[11]), "=&r"(r[12]), "=&r"(r[13]), "=&r"(r[14]), "=&r"(r[15]),
+        "=&r"(r[16]), "=&r"(r[17]), "=&r"(r[18]), "=&r"(r[19]), "=&r"(r[20]), "=&r"(r[21]), "=&r"(r[22]), "=&r"(r[23]),
+        "=&r"(r[24]), "=&r"(r[25]), "=&r"(r[26]), "=&r"(r[27]), "=&r"(r[28]), "=&r"(r[29]), "=&r"(r[30]), "=&r"(r[31]),
+        "=&r"(r[32]), "=&r"(r[33]), "=&r"(r[34]), "=&r"(r[35]), "=&r"(r[36]), "=&r"(r[37]), "=&r"(r[38]), "=&r"(r[39]),
+        "=&r"(r[40]), "=&r"(r[41]), "=&r"(r[42]), "=&r"(r[43]), "=&r"(r[44]), "=&r"(r[45]), "=&r"(r[46]), "=&r"(r[47])
       : "r"(taddr), "r"(taddr + 32)
       : "memory");
 #pragma unroll
@@ -891,24 +896,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // group w/4, as in the backward.  Query tile 0 is rows [0,128), tile 1 rows [NK-128, NK) (its
 // rows < 128 are computed again and not stored).  Per item:
 //   QK-RMSNorm of the q and k rows in place (two threads per row)
-//   S_t = Qhat_t Khat^T     both tiles issued at once -> TMEM S_COL[t] (K-major operands)
+//   S_t = Qhat_t Khat^T     both tiles issued at once -> TMEM s_col(t) (K-major operands)
 //   softmax of tile t       row max and row sum combined over the four column groups through
 //                           shared memory; P = exp2(S*scale*log2e + mask - max) packed to bf16
-//                           over the front of S_t in TMEM (tcgen05.st)
-//   O_t = P_t V             A = P from TMEM, B = V MN-major -> TMEM O_COL[t]; tile 0's O
-//                           product runs during tile 1's softmax
+//                           into `ps` (K-major 128-byte-swizzled blocks of 64 keys)
+//   O_t = P_t V             A = P K-major, B = V MN-major -> TMEM o_col(t); tile 0's O product
+//                           runs during tile 1's softmax (P_1 is written once it has finished)
 //   epilogue                O/rowsum to bf16 rows in shared memory, then whole 128-byte rows to
 //                           each token's position; lse = max + log2(sum) in window order
 constexpr int FWD_THREADS = 512;
 constexpr int FWD_TMEM_COLS = 512;
-__device__ __forceinline__ uint32_t s_col(int t) { return t == 0 ? 0u : 192u; }
-__device__ __forceinline__ uint32_t o_col(int t) { return t == 0 ? 384u : 448u; }
+// TMEM columns: S_0 [0, 176), O_0 [192, 256), S_1 [256, 432), O_1 [448, 512).
+__device__ __forceinline__ uint32_t s_col(int t) { return t == 0 ? 0u : 256u; }
+__device__ __forceinline__ uint32_t o_col(int t) { return t == 0 ? 192u : 448u; }
 
 struct __align__(1024) SmemF {
   unsigned char q[2][ROWBUF];  // item-parity buffer sets; K-major SW128 rows, normalized in place
   unsigned char k[2][ROWBUF];
   unsigned char v[2][ROWBUF];  // MN-major B operand of O = P V (the same SW128 rows)
-  unsigned char stg[2][128 * ROW_B];  // bf16 O rows of query tile 0 / 1
+  unsigned char ps[3 * PS_BLOCK];  // P of the current query tile, [128 rows x 64 keys] SW128 blocks
+  unsigned char stg[128 * ROW_B];   // bf16 O rows of one query tile
   int tok[2][MAXL];
   short wr[2][MAXL];  // window-order index of smem row j (the lse layout)
   signed char lab[2][MAXL];
@@ -921,16 +928,19 @@ struct __align__(1024) SmemF {
   uint32_t tmem_base;
 };
 
-// Scaled, masked logits (log2 domain; padding keys -inf) of this warp's keys [16 c0, 16 (c0 + NCH))
-// of one row, read from TMEM.
-template <int NCH>
+// Scaled, masked logits (log2 domain; padding keys -inf) of this warp's 48 keys [16 c0, 16 c0 + 48)
+// of one row, read from TMEM.  Keys at or beyond NK (the last group reads past the S columns into
+// unused TMEM) are -inf without a label lookup.
 __device__ __forceinline__ void logits(uint32_t taddr, const signed char* lab, int c0, int lr, float sl2, float ml2,
-                                       int mixed, int L, float* sv) {
-  ld_cols<NCH>(taddr + 16 * c0, sv);
+                                       int mixed, int L, int NK, float* sv) {
+  ld_cols<3>(taddr + 16 * c0, sv);
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
+  for (int c = 0; c < 3; ++c) {
     const int j = c0 + c;
-    if (!mixed && 16 * j + 16 <= L) {
+    if (16 * j >= NK) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sv[16 * c + i] = -INFINITY;
+    } else if (!mixed && 16 * j + 16 <= L) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) sv[16 * c + i] *= sl2;
     } else {
@@ -943,27 +953,25 @@ __device__ __forceinline__ void logits(uint32_t taddr, const signed char* lab, i
   }
 }
 
-template <int NCH>
 __device__ __forceinline__ float row_max(uint32_t taddr, const signed char* lab, int c0, int lr, float sl2, float ml2,
-                                         int mixed, int L) {
-  float sv[16 * NCH];
-  logits<NCH>(taddr, lab, c0, lr, sl2, ml2, mixed, L, sv);
+                                         int mixed, int L, int NK) {
+  float sv[48];
+  logits(taddr, lab, c0, lr, sl2, ml2, mixed, L, NK, sv);
   float m = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < 16 * NCH; ++i) m = fmaxf(m, sv[i]);
+  for (int i = 0; i < 48; ++i) m = fmaxf(m, sv[i]);
   return m;
 }
 
 // P = exp2(s - m) of the same keys (logits read again from TMEM rather than kept in registers
 // across the block barrier), packed to bf16 pairs in pk; returns their fp32 sum.
-template <int NCH>
 __device__ __forceinline__ float probs(uint32_t taddr, const signed char* lab, int c0, int lr, float sl2, float ml2,
-                                       int mixed, int L, float m, uint32_t* pk) {
-  float sv[16 * NCH];
-  logits<NCH>(taddr, lab, c0, lr, sl2, ml2, mixed, L, sv);
+                                       int mixed, int L, int NK, float m, uint32_t* pk) {
+  float sv[48];
+  logits(taddr, lab, c0, lr, sl2, ml2, mixed, L, NK, sv);
   float l = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8 * NCH; ++i) {
+  for (int i = 0; i < 24; ++i) {
     const float p0 = ex2(sv[2 * i] - m), p1 = ex2(sv[2 * i + 1] - m);
     l += p0 + p1;
     pk[i] = pack_bf16(p0, p1);
@@ -971,10 +979,15 @@ __device__ __forceinline__ float probs(uint32_t taddr, const signed char* lab, i
   return l;
 }
 
-template <int NCH>
-__device__ __forceinline__ void store_p(uint32_t taddr, int c0, const uint32_t* pk) {
+// This row's P for keys [16 c0, 16 c0 + 48) into the K-major P tile (192 keys wide).
+__device__ __forceinline__ void store_p(unsigned char* ps, int rt, int c0, const uint32_t* pk) {
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) st8(taddr + 8 * (c0 + c), pk + 8 * c);
+  for (int c = 0; c < 3; ++c) {
+    const int key = 16 * (c0 + c);
+    *reinterpret_cast<uint4*>(ps + ps_off(rt, key)) = make_uint4(pk[8 * c], pk[8 * c + 1], pk[8 * c + 2], pk[8 * c + 3]);
+    *reinterpret_cast<uint4*>(ps + ps_off(rt, key + 8)) =
+        make_uint4(pk[8 * c + 4], pk[8 * c + 5], pk[8 * c + 6], pk[8 * c + 7]);
+  }
 }
 
 __global__ void __launch_bounds__(FWD_THREADS, 1)
@@ -1019,6 +1032,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       *reinterpret_cast<uint4*>(S.v[b2] + swz(r, c)) = z;
     }
   }
+  // rows of the P tile that no warp writes (padding rows) stay finite
+  for (int idx = tid; idx < 3 * PS_BLOCK / 16; idx += FWD_THREADS)
+    reinterpret_cast<uint4*>(S.ps)[idx] = make_uint4(0, 0, 0, 0);
   if (tid < HD) {
     S.qwv[tid] = qw[tid];
     S.kwv[tid] = kw[tid];
@@ -1035,7 +1051,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   const float sl2 = g.scale * kLog2e;
   const float ml2 = -100.f * kLog2e;
   const int rt = lg * 32 + lane;  // row within a 128-row tile
-  const int c0 = 3 * cg, nch = max(0, min(3, NK / 16 - c0));
+  const int c0 = 3 * cg;
   uint32_t ph = 0, ld_parity = 0;
   bool ok = true;
   bool ld_pending = false;
@@ -1149,39 +1165,27 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       uint32_t pk[24];
       float mx = -INFINITY;
       const uint32_t ts = trow + s_col(t);
-      if (warp_live) {
-        if (nch == 3) mx = row_max<3>(ts, lab, c0, lr, sl2, ml2, mixed, L);
-        else if (nch == 2) mx = row_max<2>(ts, lab, c0, lr, sl2, ml2, mixed, L);
-        else if (nch == 1) mx = row_max<1>(ts, lab, c0, lr, sl2, ml2, mixed, L);
-      }
+      if (warp_live && c0 * 16 < NK) mx = row_max(ts, lab, c0, lr, sl2, ml2, mixed, L, NK);
       S.red[0][cg][rt] = mx;
       __syncthreads();
       const float m = fmaxf(fmaxf(S.red[0][0][rt], S.red[0][1][rt]), fmaxf(S.red[0][2][rt], S.red[0][3][rt]));
       float ls = 0.f;
-      if (warp_live) {
-        if (nch == 3) ls = probs<3>(ts, lab, c0, lr, sl2, ml2, mixed, L, m, pk);
-        else if (nch == 2) ls = probs<2>(ts, lab, c0, lr, sl2, ml2, mixed, L, m, pk);
-        else if (nch == 1) ls = probs<1>(ts, lab, c0, lr, sl2, ml2, mixed, L, m, pk);
-      }
+      if (warp_live && c0 * 16 < NK) ls = probs(ts, lab, c0, lr, sl2, ml2, mixed, L, NK, m, pk);
       S.red[1][cg][rt] = ls;
-      // every warp's logits of this tile are read: P may overwrite the front of S
-      fence_before();
-      __syncthreads();
-      fence_after();
+      // the P tile is free once the previous tile's O product has read it
+      ok = __syncthreads_and((warp == 0 && t > 0) ? wait_bar(&S.bar_o[0], ph, err) : true);
+      if (!ok) break;
       m_t[t] = m;
       l_t[t] = S.red[1][0][rt] + S.red[1][1][rt] + S.red[1][2][rt] + S.red[1][3][rt];
-      if (warp_live) {
-        if (nch == 3) store_p<3>(ts, c0, pk);
-        else if (nch == 2) store_p<2>(ts, c0, pk);
-        else if (nch == 1) store_p<1>(ts, c0, pk);
-      }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      if (warp_live && c0 * 16 < NK) store_p(S.ps, rt, c0, pk);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
       __syncthreads();
       if (tid == 0) {
         fence_after();
         for (int ks = 0; ks < NK / 16; ++ks)
-          mma_ts(tmem + o_col(t), tmem + s_col(t) + 8 * ks, desc_mnmajor(S.v[b] + ks * 16 * ROW_B), id_o, ks > 0);
+          mma_ss(tmem + o_col(t), desc_kmajor(S.ps + (ks >> 2) * PS_BLOCK + (ks & 3) * 32),
+                 desc_mnmajor(S.v[b] + ks * 16 * ROW_B), id_o, ks > 0);
         commit(&S.bar_o[t]);
       }
       __syncwarp();
@@ -1197,7 +1201,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       ok = __syncthreads_and(warp == 0 ? wait_bar(&S.bar_o[t], ph, err) : true);
       if (!ok) break;
       fence_after();
-      unsigned char* st = S.stg[t];
+      unsigned char* st = S.stg;  // reused by tile 1 after the barrier above
       if (warp_live) {
         float o[16];
         ld16(trow + o_col(t) + 16 * cg, o);
