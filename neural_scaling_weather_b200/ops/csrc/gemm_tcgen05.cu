@@ -207,6 +207,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -218,6 +219,7 @@ __device__ __forceinline__ void tc_fence_after() {
 struct EpiParams {
   CUtensorMap map_d;    // TMA store maps (32 x 32 box, SWIZZLE_64B) of D and the pre-activation;
   CUtensorMap map_pre;  // used when tma_out is set (16-bit D, N % 8 == 0)
+  CUtensorMap map_res;  // TMA load map of the residual / aux tensor (same box and swizzle)
   int tma_out;
   void* D;
   int64_t M, N, ldd;
@@ -251,30 +253,6 @@ constexpr int kArFlagBase = 16;
 template <typename T, int BN>
 struct EpiWarp {
   static constexpr int kChunks = BN / 64;
-  uint4 pre_res[kChunks][4];
-
-  // Residual / aux prefetch into registers, issued before the accumulator wait.
-  __device__ __forceinline__ void prefetch(const EpiParams& ep, int64_t row_base, int64_t n0, int half, int lane) {
-    // Prefetch this warp's residual/aux strip (32 rows x BN/2 columns) into registers in
-    // the coalesced layout (lane -> row sub_r + 8 i, 8-column group sub_c) BEFORE waiting
-    // for the accumulator, so the global latency hides behind this tile's MMAs.
-    const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
-    const bool res_vec = ep.residual != nullptr && !ep.out_f32;
-    if (res_vec) {
-#pragma unroll
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int64_t nbp = n0 + (half * kChunks + cc) * 32;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int64_t rr = row_base + sub_r + 8 * i;
-          pre_res[cc][i] = make_uint4(0, 0, 0, 0);
-          if (rr < ep.M && nbp + 32 <= ep.N)
-            pre_res[cc][i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
-                                                            (rr % ep.res_period) * ep.ldr + nbp + sub_c);
-        }
-      }
-    }
-  }
 
   // TMEM -> registers -> fused bias / GELU / residual -> stores.  Full 32-column chunks of a
   // 16-bit D leave through TMA stores: the warp writes the chunk into one of its two 2 KB staging
@@ -341,13 +319,24 @@ struct EpiWarp {
             for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
           }
           if (ep.residual) {
-            // coalesced prefetch layout -> this lane's row, through a staging buffer
+            // (the kernel's RT form brings residual tiles in by TMA; this is the fallback)
+            // coalesced loads (lane -> row sub_r + 8 i, 8-column group sub_c) -> this lane's row,
+            // through a staging buffer
+            uint4 rv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int64_t rr = row_base + sub_r + 8 * i;
+              rv[i] = make_uint4(0, 0, 0, 0);
+              if (rr < ep.M)
+                rv[i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                       (rr % ep.res_period) * ep.ldr + nb + sub_c);
+            }
             T* buf = stg + (ring & 1) * (32 * kStageRow);
             if (lane == 0) bulk_wait_read_1();
             __syncwarp();
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-              *reinterpret_cast<uint4*>(buf + stg_off(sub_r + 8 * i, sub_c >> 3)) = pre_res[cc][i];
+              *reinterpret_cast<uint4*>(buf + stg_off(sub_r + 8 * i, sub_c >> 3)) = rv[i];
             __syncwarp();
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -368,6 +357,86 @@ struct EpiWarp {
           }
           stage_store(&ep.map_d, f, stg, lane, n_tile, m_tile, ring);
         }
+      }
+      if (cc + 1 < kChunks) tmem_wait_ld(r[(cc + 1) & 1]);
+    }
+  }
+
+  // Residual / aux by TMA (the kernel's RT form): lane 0 loads the warp's kChunks 32 x 32 tiles of
+  // the residual into the warp's kChunks buffers (same SWIZZLE_64B layout as the output staging)
+  // before the accumulator wait; the drain reads each lane's row there, combines it with the
+  // accumulator row, writes the result back in place and stores it by TMA from the same buffer.
+  // Earlier stores from these buffers must have read them first.  Returns the bytes expected.
+  __device__ __forceinline__ static void issue_res(const EpiParams& ep, T* bufs, uint64_t* bar, int64_t row_base,
+                                                   int64_t n0, int half, int lane) {
+    if (lane != 0) return;
+    bulk_wait_read_0();
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int cc = 0; cc < kChunks; ++cc)
+      if (n0 + (half * kChunks + cc) * 32 < ep.N) bytes += 32 * kStageRow * sizeof(T);
+    mbar_expect_tx(bar, bytes);
+    const int rrow = (int)(row_base % ep.res_period);
+#pragma unroll
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int64_t nb = n0 + (half * kChunks + cc) * 32;
+      if (nb < ep.N) tma_load_2d(bufs + cc * 32 * kStageRow, &ep.map_res, bar, (int)nb, rrow);
+    }
+  }
+
+  __device__ __forceinline__ void drain_res(const EpiParams& ep, T* bufs, uint32_t t_row, int64_t row_base,
+                                            int64_t n0, int half, int lane) {
+    uint32_t r[2][32];
+    tmem_ld32_async(t_row + (uint32_t)(half * kChunks * 32), r[0]);
+    tmem_wait_ld(r[0]);
+#pragma unroll
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = half * kChunks + cc;
+      uint32_t* rc = r[cc & 1];
+      if (cc + 1 < kChunks) tmem_ld32_async(t_row + (uint32_t)((c + 1) * 32), r[(cc + 1) & 1]);
+      const int64_t nb = n0 + c * 32;
+      if (nb < ep.N) {  // warp-uniform
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(rc[j]) * ep.alpha;
+        if (ep.bias) {
+          if (nb + 32 <= ep.N) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const float4 b4 = __ldg(reinterpret_cast<const float4*>(ep.bias + nb) + v);
+              f[4 * v] += b4.x;
+              f[4 * v + 1] += b4.y;
+              f[4 * v + 2] += b4.z;
+              f[4 * v + 3] += b4.w;
+            }
+          } else {
+            for (int j = 0; j < 32 && nb + j < ep.N; ++j) f[j] += ep.bias[nb + j];
+          }
+        }
+        if (ep.act == 1) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = gelu_fast(f[j]);
+        }
+        T* buf = bufs + cc * 32 * kStageRow;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float rr8[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(buf + stg_off(lane, v)), rr8);
+          if (ep.act == 2) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[8 * v + j] *= gelu_grad_fast(rr8[j]);
+          } else if (ep.act == 4) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[8 * v + j] *= rr8[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[8 * v + j] += rr8[j];
+          }
+          *reinterpret_cast<uint4*>(buf + stg_off(lane, v)) = pack8<T>(&f[8 * v]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) tma_store_2d(&ep.map_d, buf, (int)nb, (int)row_base);
       }
       if (cc + 1 < kChunks) tmem_wait_ld(r[(cc + 1) & 1]);
     }
@@ -520,21 +589,25 @@ struct EpiWarp {
   }
 };
 
-template <typename T, int BN, int STAGES>
+// RT (residual by TMA): one 2 KB buffer per 32-column chunk of a warp's half tile (the residual
+// tile lands there and the result leaves from there); otherwise two 2 KB staging buffers per warp.
+template <typename T, int BN, int STAGES, bool RT>
 struct Smem {
+  static constexpr int kBufs = RT ? BN / 64 : 2;
   alignas(1024) T a[STAGES][BM * BK];
   alignas(1024) T b[STAGES][BN * BK];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
-  alignas(1024) T stage[kEpiWarps][2 * 32 * kStageRow];  // two 2 KB staging buffers per epilogue warp
+  uint64_t res_full[kEpiWarps];  // RT: a warp's residual tiles landed
+  alignas(1024) T stage[kEpiWarps][kBufs * 32 * kStageRow];
   uint32_t tmem_base;
   int abort_flag;
   int epi_stop;  // all-reduce epilogue: written by its leader only, read after a named barrier
 };
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool RT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 int64_t M, int64_t N, int64_t K, const __grid_constant__ EpiParams ep, uint32_t idesc,
@@ -543,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // align the working area to 1024 B (the swizzle atom)
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  auto& S = *reinterpret_cast<Smem<T, BN, STAGES>*>(base);
+  auto& S = *reinterpret_cast<Smem<T, BN, STAGES, RT>*>(base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int64_t n_tiles = (N + BN - 1) / BN;
@@ -560,6 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&S.tmem_full[a], 1);
       mbar_init(&S.tmem_empty[a], kEpiWarps);
     }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&S.res_full[w], 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
@@ -714,16 +788,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ring = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t res_phase = 0;
+    bool res_pending = false;
     for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int64_t m0 = (tile / n_tiles) * BM;
       const int64_t n0 = (tile % n_tiles) * BN;
       const int64_t row_base = m0 + q * 32;
       EpiWarp<T, BN> epi;
-      epi.prefetch(ep, row_base, n0, half, lane);
+      if constexpr (RT) {
+        EpiWarp<T, BN>::issue_res(ep, stg, &S.res_full[ew], row_base, n0, half, lane);
+        res_pending = true;
+      }
       if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
       tc_fence_after();
-      epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half, lane,
-                ring);
+      if constexpr (RT) {
+        if (!mbar_wait(&S.res_full[ew], res_phase, abort_flag, err)) break;
+        res_phase ^= 1;
+        res_pending = false;
+        epi.drain_res(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half,
+                      lane);
+      } else {
+        epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half,
+                  lane, ring);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);
@@ -733,6 +820,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_all();  // the warp's TMA stores have completed
+    // after an abort, residual loads still in flight land before the shared memory is released
+    // (bounded; not recorded again)
+    if (RT && res_pending && lane == 0) {
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try_wait(&S.res_full[ew], res_phase) && globaltimer() - t0 < kWaitBudgetNs) {
+      }
+    }
   }
 
   tc_fence_before();
@@ -929,7 +1023,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int64_t n0 = (tile % n_tiles) * BN2;
       const int64_t row_base = m0 + q * 32;
       EpiWarp<T, BN2> epi;
-      epi.prefetch(ep, row_base, n0, half, lane);
       if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
       tc_fence_after();
       epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN2), row_base, n0, half, lane,
@@ -1083,18 +1176,20 @@ static cudaError_t launch2(const GemmArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool RT = false>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   CUtensorMap ma, mb;
   if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
   if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN, a.dtype)) return cudaErrorInvalidValue;
   EpiParams ep = epi_params(a);
+  if (RT && !make_store_map(&ep.map_res, const_cast<void*>(a.residual), ep.res_period, a.N, a.ldr, a.dtype))
+    return cudaErrorInvalidValue;
   ep.ar_tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
   const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                          ((uint32_t)(BM >> 4) << 24);
-  const size_t smem = sizeof(Smem<T, BN, STAGES>) + 1024;
-  auto k = gemm_kernel<T, BN, STAGES>;
+  const size_t smem = sizeof(Smem<T, BN, STAGES, RT>) + 1024;
+  auto k = gemm_kernel<T, BN, STAGES, RT>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   int grid = sm_count();
@@ -1134,11 +1229,19 @@ cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl) {
   const bool light = a.act == 0 && !a.residual && !a.preact;
   // the fused all-reduce lives in the single-CTA kernel's epilogue
   const bool pair = a.ar_world <= 1 && (impl == 2 || (impl == 0 && wide && a.M > tc::BM && light));
+  // residual / aux epilogue with the residual tiles brought in by TMA (three pipeline stages
+  // leave room for one 2 KB buffer per 32-column chunk and epilogue warp); impl 3 forces the
+  // fallback that loads residual chunks with plain loads in the drain
+  const int64_t period = a.res_period > 0 ? a.res_period : a.M;
+  const bool rt = wide && a.residual && !a.preact && a.act != 3 && !a.out_f32 && a.ar_world <= 1 && !pair &&
+                  impl != 3 && a.N % 8 == 0 && period % 32 == 0;
   if (a.dtype == kBF16) {
     if (pair) return tc::launch2<__nv_bfloat16, 6>(a, s);
+    if (rt) return tc::launch<__nv_bfloat16, 256, 3, true>(a, s);
     return wide ? tc::launch<__nv_bfloat16, 256, 4>(a, s) : tc::launch<__nv_bfloat16, 128, 6>(a, s);
   }
   if (pair) return tc::launch2<__half, 6>(a, s);
+  if (rt) return tc::launch<__half, 256, 3, true>(a, s);
   return wide ? tc::launch<__half, 256, 4>(a, s) : tc::launch<__half, 128, 6>(a, s);
 }
 

@@ -82,6 +82,27 @@ def test_gemm_epilogues(impl, _ext_loaded):
     assert rel(out, base + 0.5 * (a.float() @ b.float().t())) < 1e-3
 
 
+@pytest.mark.parametrize("M,N", [(512, 512), (1024, 1000), (4096, 4096)])
+@pytest.mark.parametrize("impl", [1, 3])
+def test_gemm_residual_epilogues(M, N, impl, _ext_loaded):
+    """impl 1 (M % 32 == 0, N > 128): residual / aux tiles arrive by TMA into the epilogue buffers;
+    impl 3: the fallback that loads them with plain loads in the drain."""
+    torch.manual_seed(2)
+    K = 256
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.1
+    bias = torch.randn(N, device=DEV)
+    res = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    acc = a.float() @ b.float().t()
+    u = acc + bias
+    assert rel(_ext_loaded.gemm(a, b, bias, res, impl=impl), u + res.float()) < 1e-2
+    assert rel(_ext_loaded.gemm(a, b, None, res, 0, 4, impl=impl), acc * res.float()) < 1e-2
+    r = res.float().requires_grad_()
+    torch.nn.functional.gelu(r).sum().backward()
+    assert rel(_ext_loaded.gemm(a, b, None, res, 0, 2, impl=impl), acc * r.grad) < 1e-2
+    assert rel(_ext_loaded.gemm(a, b, bias, res, 0, 1, impl=impl), torch.nn.functional.gelu(u) + res.float()) < 1e-2
+
+
 # --------------------------------------------------------------------------- RMSNorm
 @pytest.mark.parametrize("rows,n", [(333, 64), (333, 1024), (333, 2048), (777, 4096), (20011, 1024),
                                     (70000, 1024)])
