@@ -100,7 +100,9 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 }
 
 // named barrier of the epilogue warps only (the producer / MMA warps keep running)
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory"); }
+__device__ __forceinline__ void epi_sync(int warps = kEpiWarps) {
+  asm volatile("bar.sync 1, %0;" ::"r"(warps * 32) : "memory");
+}
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
   // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO), LBO unused (1),
@@ -250,28 +252,47 @@ constexpr int kArFlagBase = 16;
 
 // Epilogue of one warp for one accumulator tile: rows [row_base, row_base + 32) (the warp's
 // TMEM lane quadrant) and columns [n0 + half * BN/2, n0 + (half + 1) * BN/2).
+// The 32-column chunks of a tile one epilogue warp drains: begin, begin + step, ... (n of them).
+// Eight warps: two per TMEM lane quadrant, each a contiguous half of the columns.  Twelve warps:
+// three per quadrant, warp j taking chunks j, j + 3, j + 6.
+struct ChunkSet {
+  int begin, step, n;
+};
+
 template <typename T, int BN>
 struct EpiWarp {
-  static constexpr int kChunks = BN / 64;
+  static constexpr int kChunks = BN / 64;  // most chunks one warp drains
 
   // TMEM -> registers -> fused bias / GELU / residual -> stores.  Full 32-column chunks of a
   // 16-bit D leave through TMA stores: the warp writes the chunk into one of its two 2 KB staging
   // buffers (32 rows x 64 bytes, SWIZZLE_64B) and lane 0 issues one bulk tensor store, so no
   // lane loads the tile back or issues global stores; the TMEM read of the next chunk is in
   // flight meanwhile.  `ring` counts this warp's staging uses across tiles.
+  // DB: double-buffered TMEM reads (the next chunk's load in flight while this one is
+  // processed); without it (twelve epilogue warps, 128 registers) each chunk is loaded and waited
+  // for in turn and the other warps of the quadrant cover the latency.
+  template <bool DB = true>
   __device__ __forceinline__ void drain(const EpiParams& ep, T* stg, uint32_t t_row, int64_t row_base, int64_t n0,
-                                        int half, int lane, uint32_t& ring) {
+                                        ChunkSet cs, int lane, uint32_t& ring) {
     const int sub_r = lane >> 2, sub_c = (lane & 3) * 8;
     const int64_t row = row_base + lane;
     const bool row_ok = row < ep.M;
-    uint32_t r[2][32];
-    tmem_ld32_async(t_row + (uint32_t)(half * kChunks * 32), r[0]);
-    tmem_wait_ld(r[0]);
+    uint32_t r[DB ? 2 : 1][32];
+    if (DB) {
+      tmem_ld32_async(t_row + (uint32_t)(cs.begin * 32), r[0]);
+      tmem_wait_ld(r[0]);
+    }
 #pragma unroll
     for (int cc = 0; cc < kChunks; ++cc) {
-      const int c = half * kChunks + cc;
-      uint32_t* rc = r[cc & 1];
-      if (cc + 1 < kChunks) tmem_ld32_async(t_row + (uint32_t)((c + 1) * 32), r[(cc + 1) & 1]);
+      if (cc >= cs.n) break;
+      const int c = cs.begin + cc * cs.step;
+      uint32_t* rc = r[DB ? (cc & 1) : 0];
+      if (!DB) {
+        tmem_ld32_async(t_row + (uint32_t)(c * 32), rc);
+        tmem_wait_ld(rc);
+      } else if (cc + 1 < cs.n) {
+        tmem_ld32_async(t_row + (uint32_t)((c + cs.step) * 32), r[(cc + 1) & 1]);
+      }
       const int64_t nb = n0 + c * 32;
       if (nb < ep.N) {  // warp-uniform
         const bool full = nb + 32 <= ep.N;
@@ -358,7 +379,7 @@ struct EpiWarp {
           stage_store(&ep.map_d, f, stg, lane, n_tile, m_tile, ring);
         }
       }
-      if (cc + 1 < kChunks) tmem_wait_ld(r[(cc + 1) & 1]);
+      if (DB && cc + 1 < cs.n) tmem_wait_ld(r[(cc + 1) & 1]);
     }
   }
 
@@ -368,32 +389,39 @@ struct EpiWarp {
   // accumulator row, writes the result back in place and stores it by TMA from the same buffer.
   // Earlier stores from these buffers must have read them first.  Returns the bytes expected.
   __device__ __forceinline__ static void issue_res(const EpiParams& ep, T* bufs, uint64_t* bar, int64_t row_base,
-                                                   int64_t n0, int half, int lane) {
+                                                   int64_t n0, ChunkSet cs, int lane) {
     if (lane != 0) return;
     bulk_wait_read_0();
     uint32_t bytes = 0;
-#pragma unroll
-    for (int cc = 0; cc < kChunks; ++cc)
-      if (n0 + (half * kChunks + cc) * 32 < ep.N) bytes += 32 * kStageRow * sizeof(T);
+    for (int cc = 0; cc < cs.n; ++cc)
+      if (n0 + (cs.begin + cc * cs.step) * 32 < ep.N) bytes += 32 * kStageRow * sizeof(T);
     mbar_expect_tx(bar, bytes);
     const int rrow = (int)(row_base % ep.res_period);
-#pragma unroll
-    for (int cc = 0; cc < kChunks; ++cc) {
-      const int64_t nb = n0 + (half * kChunks + cc) * 32;
+    for (int cc = 0; cc < cs.n; ++cc) {
+      const int64_t nb = n0 + (cs.begin + cc * cs.step) * 32;
       if (nb < ep.N) tma_load_2d(bufs + cc * 32 * kStageRow, &ep.map_res, bar, (int)nb, rrow);
     }
   }
 
+  template <bool DB = true>
   __device__ __forceinline__ void drain_res(const EpiParams& ep, T* bufs, uint32_t t_row, int64_t row_base,
-                                            int64_t n0, int half, int lane) {
-    uint32_t r[2][32];
-    tmem_ld32_async(t_row + (uint32_t)(half * kChunks * 32), r[0]);
-    tmem_wait_ld(r[0]);
+                                            int64_t n0, ChunkSet cs, int lane) {
+    uint32_t r[DB ? 2 : 1][32];
+    if (DB) {
+      tmem_ld32_async(t_row + (uint32_t)(cs.begin * 32), r[0]);
+      tmem_wait_ld(r[0]);
+    }
 #pragma unroll
     for (int cc = 0; cc < kChunks; ++cc) {
-      const int c = half * kChunks + cc;
-      uint32_t* rc = r[cc & 1];
-      if (cc + 1 < kChunks) tmem_ld32_async(t_row + (uint32_t)((c + 1) * 32), r[(cc + 1) & 1]);
+      if (cc >= cs.n) break;
+      const int c = cs.begin + cc * cs.step;
+      uint32_t* rc = r[DB ? (cc & 1) : 0];
+      if (!DB) {
+        tmem_ld32_async(t_row + (uint32_t)(c * 32), rc);
+        tmem_wait_ld(rc);
+      } else if (cc + 1 < cs.n) {
+        tmem_ld32_async(t_row + (uint32_t)((c + cs.step) * 32), r[(cc + 1) & 1]);
+      }
       const int64_t nb = n0 + c * 32;
       if (nb < ep.N) {  // warp-uniform
         float f[32];
@@ -438,7 +466,7 @@ struct EpiWarp {
         __syncwarp();
         if (lane == 0) tma_store_2d(&ep.map_d, buf, (int)nb, (int)row_base);
       }
-      if (cc + 1 < kChunks) tmem_wait_ld(r[(cc + 1) & 1]);
+      if (DB && cc + 1 < cs.n) tmem_wait_ld(r[(cc + 1) & 1]);
     }
   }
 
@@ -591,24 +619,24 @@ struct EpiWarp {
 
 // RT (residual by TMA): one 2 KB buffer per 32-column chunk of a warp's half tile (the residual
 // tile lands there and the result leaves from there); otherwise two 2 KB staging buffers per warp.
-template <typename T, int BN, int STAGES, bool RT>
+template <typename T, int BN, int STAGES, bool RT, int EW>
 struct Smem {
-  static constexpr int kBufs = RT ? BN / 64 : 2;
+  static constexpr int kBufs = RT ? (EW == 8 ? BN / 64 : (BN / 32 + EW / 4 - 1) / (EW / 4)) : 2;
   alignas(1024) T a[STAGES][BM * BK];
   alignas(1024) T b[STAGES][BN * BK];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
-  uint64_t res_full[kEpiWarps];  // RT: a warp's residual tiles landed
-  alignas(1024) T stage[kEpiWarps][kBufs * 32 * kStageRow];
+  uint64_t res_full[EW];  // RT: a warp's residual tiles landed
+  alignas(1024) T stage[EW][kBufs * 32 * kStageRow];
   uint32_t tmem_base;
   int abort_flag;
   int epi_stop;  // all-reduce epilogue: written by its leader only, read after a named barrier
 };
 
-template <typename T, int BN, int STAGES, bool RT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int BN, int STAGES, bool RT, int EW>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 int64_t M, int64_t N, int64_t K, const __grid_constant__ EpiParams ep, uint32_t idesc,
                 int* err) {
@@ -616,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // align the working area to 1024 B (the swizzle atom)
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  auto& S = *reinterpret_cast<Smem<T, BN, STAGES, RT>*>(base);
+  auto& S = *reinterpret_cast<Smem<T, BN, STAGES, RT, EW>*>(base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int64_t n_tiles = (N + BN - 1) / BN;
@@ -631,9 +659,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&S.tmem_full[a], 1);
-      mbar_init(&S.tmem_empty[a], kEpiWarps);
+      mbar_init(&S.tmem_empty[a], EW);
     }
-    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&S.res_full[w], 1);
+    for (int w = 0; w < EW; ++w) mbar_init(&S.res_full[w], 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
@@ -708,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (ep.ar_world > 1) {
+  } else if (EW == 8 && ep.ar_world > 1) {
     // ------------------------------------------------------------------ epilogue + all-reduce
     const int ew = warp - 2;
     const int q = warp & 3;
@@ -782,8 +810,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue
     const int ew = warp - 2;
-    const int q = warp & 3;         // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;       // which half of the BN columns
+    const int q = warp & 3;   // TMEM lane quadrant this warp may access
+    const int j = ew >> 2;    // this warp's index among the warps of its quadrant
+    ChunkSet cs;
+    if (EW == 8) {
+      cs = {j * (BN / 64), 1, BN / 64};
+    } else {
+      constexpr int G = EW / 4;
+      cs = {j, G, (BN / 32 - j + G - 1) / G};
+    }
     T* stg = S.stage[ew];
     uint32_t ring = 0;
     int acc = 0;
@@ -796,7 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row_base = m0 + q * 32;
       EpiWarp<T, BN> epi;
       if constexpr (RT) {
-        EpiWarp<T, BN>::issue_res(ep, stg, &S.res_full[ew], row_base, n0, half, lane);
+        EpiWarp<T, BN>::issue_res(ep, stg, &S.res_full[ew], row_base, n0, cs, lane);
         res_pending = true;
       }
       if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
@@ -805,11 +840,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&S.res_full[ew], res_phase, abort_flag, err)) break;
         res_phase ^= 1;
         res_pending = false;
-        epi.drain_res(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half,
-                      lane);
+        epi.template drain_res<EW == 8>(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN),
+                                        row_base, n0, cs, lane);
       } else {
-        epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half,
-                  lane, ring);
+        epi.template drain<EW == 8>(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN),
+                                    row_base, n0, cs, lane, ring);
       }
       tc_fence_before();
       __syncwarp();
@@ -1025,8 +1060,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       EpiWarp<T, BN2> epi;
       if (!mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err)) break;
       tc_fence_after();
-      epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN2), row_base, n0, half, lane,
-                ring);
+      epi.drain(ep, stg, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN2), row_base, n0,
+                ChunkSet{half * EpiWarp<T, BN2>::kChunks, 1, EpiWarp<T, BN2>::kChunks}, lane, ring);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(empty_leader + 8u * acc);
@@ -1176,7 +1211,7 @@ static cudaError_t launch2(const GemmArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <typename T, int BN, int STAGES, bool RT = false>
+template <typename T, int BN, int STAGES, bool RT = false, int EW = 8>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   CUtensorMap ma, mb;
   if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
@@ -1188,13 +1223,13 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
   const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                          ((uint32_t)(BM >> 4) << 24);
-  const size_t smem = sizeof(Smem<T, BN, STAGES, RT>) + 1024;
-  auto k = gemm_kernel<T, BN, STAGES, RT>;
+  const size_t smem = sizeof(Smem<T, BN, STAGES, RT, EW>) + 1024;
+  auto k = gemm_kernel<T, BN, STAGES, RT, EW>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   int grid = sm_count();
   if (tiles < grid) grid = (int)tiles;
-  k<<<grid, kThreads, smem, s>>>(ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag());
+  k<<<grid, 64 + 32 * EW, smem, s>>>(ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag());
   return cudaGetLastError();
 }
 
@@ -1218,30 +1253,44 @@ int gemm_tcgen05_supported(const GemmArgs& a) {
   return tc::get_encode() != nullptr;
 }
 
-// impl: 0 = default, 1 = single CTA, 2 = CTA pair.  The default takes the CTA pair for wide
-// GEMMs whose epilogue is light (bias only): there the pair's lower shared-memory traffic per
-// MMA wins; with GELU / pre-activation / residual epilogues the single-CTA kernel is faster
-// (measured at 64800 x 4096 x 1024), since a pair reuses an accumulator only when both CTAs'
-// epilogues have drained it.
+// impl: 0 = default, 1 = single CTA, 2 = CTA pair, 3 = single CTA with the plain-load residual
+// path, 4 = single CTA with twelve epilogue warps for GELU epilogues.  The default takes the
+// CTA pair for wide GEMMs whose epilogue is light (bias only, or a residual after K >= 2048):
+// there the pair's lower shared-memory traffic per MMA wins; with GELU / pre-activation /
+// residual epilogues after a short mainloop the single-CTA kernel is faster (measured at
+// 64800 x 4096 x 1024), since a pair reuses an accumulator only when both CTAs' epilogues have
+// drained it.
 cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl) {
   if (!gemm_tcgen05_supported(a)) return cudaErrorInvalidValue;
   const bool wide = a.N > 128;
   const bool light = a.act == 0 && !a.residual && !a.preact;
   // the fused all-reduce lives in the single-CTA kernel's epilogue
-  const bool pair = a.ar_world <= 1 && (impl == 2 || (impl == 0 && wide && a.M > tc::BM && light));
+  // a residual-only epilogue after a long mainloop (fc2 forward, K = 4096) also goes to the pair:
+  // its per-SM operand traffic is lower, and the epilogue is a small share of the tile
+  // (measured 0.396 against 0.445 ms at 64800 x 1024 x 4096; at K = 1024 the single CTA wins)
+  const bool long_res = a.residual && a.act == 0 && !a.preact && a.K >= 2048;
+  const bool pair =
+      a.ar_world <= 1 && (impl == 2 || (impl == 0 && wide && a.M > tc::BM && (light || long_res)));
   // residual / aux epilogue with the residual tiles brought in by TMA (three pipeline stages
   // leave room for one 2 KB buffer per 32-column chunk and epilogue warp); impl 3 forces the
   // fallback that loads residual chunks with plain loads in the drain
   const int64_t period = a.res_period > 0 ? a.res_period : a.M;
   const bool rt = wide && a.residual && !a.preact && a.act != 3 && !a.out_f32 && a.ar_world <= 1 && !pair &&
                   impl != 3 && a.N % 8 == 0 && period % 32 == 0;
+  // impl 4: twelve epilogue warps (three per TMEM lane quadrant, 128 registers, single-buffered
+  // TMEM reads) for the GELU / GELU' epilogues; measured within noise of eight at
+  // 64800 x 4096 x 1024 (0.538 against 0.548 ms for GELU, 0.614 against 0.581 ms for GELU' with
+  // the TMA residual), so eight is the default
+  const bool gelu12 = impl == 4 && wide && !pair && a.ar_world <= 1 && (a.act == 1 || a.act == 2);
   if (a.dtype == kBF16) {
     if (pair) return tc::launch2<__nv_bfloat16, 6>(a, s);
-    if (rt) return tc::launch<__nv_bfloat16, 256, 3, true>(a, s);
+    if (rt) return gelu12 ? tc::launch<__nv_bfloat16, 256, 3, true, 12>(a, s) : tc::launch<__nv_bfloat16, 256, 3, true>(a, s);
+    if (gelu12) return tc::launch<__nv_bfloat16, 256, 3, false, 12>(a, s);
     return wide ? tc::launch<__nv_bfloat16, 256, 4>(a, s) : tc::launch<__nv_bfloat16, 128, 6>(a, s);
   }
   if (pair) return tc::launch2<__half, 6>(a, s);
-  if (rt) return tc::launch<__half, 256, 3, true>(a, s);
+  if (rt) return gelu12 ? tc::launch<__half, 256, 3, true, 12>(a, s) : tc::launch<__half, 256, 3, true>(a, s);
+  if (gelu12) return tc::launch<__half, 256, 3, false, 12>(a, s);
   return wide ? tc::launch<__half, 256, 4>(a, s) : tc::launch<__half, 128, 6>(a, s);
 }
 

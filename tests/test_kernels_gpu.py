@@ -45,8 +45,10 @@ def test_gemm_plain(M, N, K, dtype, impl, _ext_loaded):
     assert rel(d, ref) < 1e-2
 
 
-@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("impl", [1, 2, 4])
 def test_gemm_epilogues(impl, _ext_loaded):
+    """impl 1: single CTA; 2: CTA pair; 4: single CTA with twelve epilogue warps for the GELU
+    epilogues."""
     torch.manual_seed(1)
     M, N, K = 515, 512, 256
     a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
@@ -83,10 +85,11 @@ def test_gemm_epilogues(impl, _ext_loaded):
 
 
 @pytest.mark.parametrize("M,N", [(512, 512), (1024, 1000), (4096, 4096)])
-@pytest.mark.parametrize("impl", [1, 3])
+@pytest.mark.parametrize("impl", [1, 3, 4])
 def test_gemm_residual_epilogues(M, N, impl, _ext_loaded):
     """impl 1 (M % 32 == 0, N > 128): residual / aux tiles arrive by TMA into the epilogue buffers;
-    impl 3: the fallback that loads them with plain loads in the drain."""
+    impl 3: the fallback that loads them with plain loads in the drain; impl 4: TMA residual
+    tiles with twelve epilogue warps for the GELU forms."""
     torch.manual_seed(2)
     K = 256
     a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
