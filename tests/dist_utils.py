@@ -1,21 +1,12 @@
 """Run a function on N CPU processes with the gloo backend (multi-rank tests without GPUs)."""
 
 import os
-import socket
 import sys
 import traceback
 
 import torch.multiprocessing as mp
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-
-
-def free_port() -> int:
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
 def _entry(rank, world, port, fn, args, errq):
@@ -31,7 +22,9 @@ def _entry(rank, world, port, fn, args, errq):
         import torch.distributed as dist
 
         torch.set_num_threads(1)
-        dist.init_process_group("gloo", rank=rank, world_size=world)
+        # the parent holds the rendezvous store on this port (bound before any rank started)
+        store = dist.TCPStore("127.0.0.1", port, world_size=world + 1, is_master=False)
+        dist.init_process_group("gloo", store=store, rank=rank, world_size=world)
         try:
             fn(rank, world, *args)
         finally:
@@ -45,9 +38,14 @@ def _entry(rank, world, port, fn, args, errq):
 
 
 def run(fn, world: int, *args, timeout: float = 600):
+    import torch.distributed as dist
+
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    port = free_port()
+    # the parent binds the rendezvous store on an OS-chosen port and keeps it for the run, so no
+    # other process can take the port between choosing it and the ranks' rendezvous
+    store = dist.TCPStore("127.0.0.1", 0, world_size=world + 1, is_master=True, wait_for_workers=False)
+    port = store.port
     procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, errq)) for r in range(world)]
     for p in procs:
         p.start()
@@ -63,6 +61,7 @@ def run(fn, world: int, *args, timeout: float = 600):
         raise AssertionError("worker failure:\n" + "\n".join(f"[rank {r}] {tb}" for r, tb in errors))
     if alive:
         raise AssertionError(f"{len(alive)} workers timed out")
+    del store
     bad = [p.exitcode for p in procs if p.exitcode != 0]
     if bad:
         raise AssertionError(f"worker exit codes {bad}")
