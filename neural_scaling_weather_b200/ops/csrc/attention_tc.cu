@@ -196,7 +196,7 @@ struct __align__(1024) SmemB {
   float rq[MAXL];
   float rk[MAXL];
   float red[4][128];  // per-column-group partial dot products of the norm backward
-  float wq[16][HD];  // per-warp weight-gradient partials of the current item
+  float wq[16][HD];  // per-warp weight-gradient partials, summed over the CTA's items
   float wk[16][HD];
   float qwv[HD];    // norm weights
   float kwv[HD];
@@ -552,6 +552,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
   for (int idx = tid; idx < 3 * PS_BLOCK / 16; idx += BWD_THREADS)
     reinterpret_cast<uint4*>(S.ps)[idx] = make_uint4(0, 0, 0, 0);
+  for (int i = tid; i < 16 * HD; i += BWD_THREADS) {  // weight-gradient slots, summed over all items
+    (&S.wq[0][0])[i] = 0.f;
+    (&S.wk[0][0])[i] = 0.f;
+  }
   if (tid < HD) {
     S.qwv[tid] = qw[tid];
     S.kwv[tid] = kw[tid];
@@ -610,10 +614,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     unsigned char* qn = S.qbuf[1 - raw];   // normalized q
     unsigned char* kx = S.kbuf[raw];
     unsigned char* kn = S.kbuf[1 - raw];
-    for (int i = lane; i < HD; i += 32) {
-      S.wq[warp][i] = 0.f;
-      S.wk[warp][i] = 0.f;
-    }
     // lse rows of this item (items are (window, head) in the forward's lse order; smem row j
     // holds window token win_row(j)); loaded during the previous item except for the first
     if (item == i_begin && tid < L) lse_next = lse[item * L + win_row(g, win_load(g, win, nww, nwh), tid)];
@@ -858,21 +858,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       NSW_STAMP();
     }
     fence_before();
-    __syncthreads();  // all warps' slots are complete
-    if (tid < 2 * HD) {
-      const int col = tid & (HD - 1);
-      float acc = 0.f;
-      if (tid < HD) {
-#pragma unroll
-        for (int w = 0; w < 16; ++w) acc += S.wq[w][col];
-        dqw_part[item * HD + col] = acc;
-      } else {
-#pragma unroll
-        for (int w = 0; w < 16; ++w) acc += S.wk[w][col];
-        dkw_part[item * HD + col] = acc;
-      }
-    }
-    __syncthreads();  // slots are cleared by their warps at the next item's start
+    __syncthreads();  // TMEM and staging are reused by the next item
     raw = 1 - raw;
     tcur = ntab;
     win = nwin;
@@ -885,6 +871,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  // this CTA's QK-norm weight-gradient partial: the warps' slots, summed over all its items
+  if (tid < 2 * HD) {
+    const int col = tid & (HD - 1);
+    float acc = 0.f;
+    if (tid < HD) {
+#pragma unroll
+      for (int w = 0; w < 16; ++w) acc += S.wq[w][col];
+      dqw_part[(int64_t)blockIdx.x * HD + col] = acc;
+    } else {
+#pragma unroll
+      for (int w = 0; w < 16; ++w) acc += S.wk[w][col];
+      dkw_part[(int64_t)blockIdx.x * HD + col] = acc;
+    }
+  }
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BWD_TMEM_COLS));
 }

@@ -407,24 +407,30 @@ std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out
   auto g = make_geom(gi, scale);
   auto dqkv = torch::empty_like(qkv);
   const int64_t nwin = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww);
-  auto qp = torch::empty({nwin * g.nh, (int64_t)g.hd}, qkv.options().dtype(at::kFloat));
-  auto kp = torch::empty_like(qp);
   // impl: 0 = default (tcgen05 where supported), 1 = mma.sync, 2 = tcgen05/TMEM
   const bool tc_ok = nsw::window_attn_fwd_tc_supported(g, dt_code(qkv));
   TORCH_CHECK(impl != 2 || tc_ok, "window_attn_bwd: tcgen05 path needs bf16, head_dim 64, window <= 176 tokens");
-  if (tc_ok && impl != 1) {
+  const bool tc = tc_ok && impl != 1;
+  // QK-norm weight-gradient partial rows: one per CTA of the persistent tcgen05 kernel
+  // (min(items, SMs) CTAs), one per (window, head) item for the mma.sync kernel; q and k partials
+  // share one tensor so a single reduction sums both
+  const int64_t items = nwin * g.nh;
+  const int64_t rows = tc ? std::min<int64_t>(items, at::cuda::getCurrentDeviceProperties()->multiProcessorCount) : items;
+  auto part = torch::empty({2, rows, (int64_t)g.hd}, qkv.options().dtype(at::kFloat));
+  float* qp = part.data_ptr<float>();
+  float* kp = qp + rows * g.hd;
+  if (tc)
     check(nsw::window_attn_bwd_tc(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
-                                  dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp.data_ptr<float>(),
-                                  kp.data_ptr<float>(), g, stream(),
+                                  dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp, kp, g, stream(),
                                   stamps ? reinterpret_cast<long long*>(stamps->data_ptr<int64_t>()) : nullptr),
           "window_attn_bwd_tc");
-    return {dqkv, qp.sum(0), kp.sum(0)};
-  }
-  check(nsw::window_attn_bwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
-                             dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp.data_ptr<float>(),
-                             kp.data_ptr<float>(), g, dt_code(qkv), stream()),
-        "window_attn_bwd");
-  return {dqkv, qp.sum(0), kp.sum(0)};
+  else
+    check(nsw::window_attn_bwd(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                               dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp, kp, g, dt_code(qkv),
+                               stream()),
+          "window_attn_bwd");
+  auto sums = part.sum(1);
+  return {dqkv, sums[0], sums[1]};
 }
 
 }  // namespace

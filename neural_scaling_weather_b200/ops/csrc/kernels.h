@@ -88,6 +88,7 @@ cudaError_t rmsnorm_fwd_tma(const void* x, const float* w, void* y, float* rstd,
 cudaError_t rmsnorm_bwd_tma(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                             float* dw_partial, int partial_rows, int64_t rows, int n, int dtype, float eps,
                             cudaStream_t s, const void* add = nullptr);  // add: optional [rows, n] added to dx
+// dqw_part / dkw_part: one row of head_dim partial sums per CTA, min(items, SM count) rows
 cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw, const void* out,
                                const void* dout, const float* lse, void* dqkv, float* dqw_part, float* dkw_part,
                                const AttnGeom& g, cudaStream_t s, long long* stamps = nullptr);
