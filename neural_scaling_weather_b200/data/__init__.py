@@ -49,44 +49,73 @@ def get_data_loader(cfg, dataset, mode: str = "train"):
 def device_prefetch(batches: Iterable[torch.Tensor], device, depth: int = 1) -> Iterator[torch.Tensor]:
     """Yield ``batches`` on ``device``, copying the next ``depth`` host batches on a side stream
     while the current one is consumed (the role of the DALI pipeline's device prefetch queue,
-    ``utils/dataloaders/era5hdf5_dali.py:70-100`` of the reference).  Host batches should be pinned for the copies to be
-    asynchronous; batches already on the device, and every batch when ``device`` is not CUDA,
-    pass through unchanged."""
+    ``utils/dataloaders/era5hdf5_dali.py:70-100`` of the reference).
+
+    The copies land in a ring of ``depth + 1`` device buffers allocated once (per batch shape),
+    so the steady state allocates nothing and no block waits on another stream's work: a yielded
+    batch is valid until the next one is requested, after which its buffer is refilled.  Copies
+    are ordered with events: the compute stream waits for a batch's copy before using it, and a
+    buffer is refilled only after the work that used it has been enqueued and, on the device,
+    finished.  Host batches should be pinned for the copies to be asynchronous; batches already
+    on the device, and every batch when ``device`` is not CUDA, pass through unchanged."""
     device = torch.device(device)
     if device.type != "cuda":
         yield from batches
         return
     it = iter(batches)
     stream = torch.cuda.Stream(device=device)
+    nbuf = depth + 1
+    ring: list = [None] * nbuf       # device buffers, filled round-robin
+    released: list = [None] * nbuf   # per buffer: compute-stream event after its last use
     pending: Deque = deque()
+    slot = 0
 
     def issue() -> bool:
+        nonlocal slot
         try:
             b = next(it)
         except StopIteration:
             return False
         if b.is_cuda:
-            pending.append((b, None))
+            pending.append((b, None, None))
             return True
-        stream.wait_stream(torch.cuda.current_stream(device))  # the buffer it reuses is free
+        k = slot % nbuf
+        slot += 1
+        cur = torch.cuda.current_stream(device)
+        buf = ring[k]
+        if buf is None or buf.shape != b.shape or buf.dtype != b.dtype:
+            buf = ring[k] = torch.empty(b.shape, dtype=b.dtype, device=device)
+            released[k] = None
+        if released[k] is not None:
+            stream.wait_event(released[k])  # the batch that last used this buffer is done
+        else:
+            stream.wait_stream(cur)  # fresh buffer, allocated on the compute stream
         with torch.cuda.stream(stream):
-            d = b.to(device, non_blocking=True)
+            buf.copy_(b, non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(stream)
-        pending.append((d, ev))
+        pending.append((buf, ev, k))
         return True
 
-    for _ in range(depth):
-        if not issue():
-            break
-    while pending:
-        d, ev = pending.popleft()
-        cur = torch.cuda.current_stream(device)
-        if ev is not None:
-            cur.wait_event(ev)
-            d.record_stream(cur)  # allocated on the copy stream, used on the compute stream
-        issue()
-        yield d
+    try:
+        for _ in range(depth):
+            if not issue():
+                break
+        while pending:
+            d, ev, k = pending.popleft()
+            cur = torch.cuda.current_stream(device)
+            if ev is not None:
+                cur.wait_event(ev)
+            issue()
+            yield d
+            if k is not None:  # the consumer's work on this batch is enqueued on `cur`
+                done = torch.cuda.Event()
+                done.record(cur)
+                released[k] = done
+    finally:
+        # copies still in flight (the consumer stopped early) complete before the ring's memory
+        # can be handed out again on the compute stream
+        torch.cuda.current_stream(device).wait_stream(stream)
 
 
 def get_preprocessor(cfg, dataset):
