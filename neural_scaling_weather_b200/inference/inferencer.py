@@ -32,6 +32,7 @@ from ..models.swin import get_model, strip_module_prefix
 from ..parallel import comm
 from ..parallel.mappings import allgather_forward_split_backward
 from ..training.trainer import experiment_dir
+from ..utils.checkpoint_io import verified_load
 from ..utils.sht import RealSHT, power_spectrum
 
 
@@ -213,6 +214,6 @@ class Inferencer:
                 "ms_per_step": step_ms}
 
     def restore_checkpoint(self, path):
-        ckpt = torch.load(path, map_location=self.device, weights_only=False)
+        ckpt = verified_load(path, map_location=self.device, weights_only=False)
         state = strip_module_prefix(ckpt["model_state"])
         self.model.load_state_dict(state)

@@ -39,6 +39,7 @@ from ..parallel.mappings import (
     identity_forward_allreduce_backward,
     roll_forward_reverseroll_backward,
 )
+from ..utils.checkpoint_io import verified_load
 from ..utils.profiler import profile
 from .layers import (
     BiasLayer,
@@ -373,7 +374,7 @@ def strip_module_prefix(state_dict):
 
 
 def load_model(model, checkpoint_file, map_location="cpu"):
-    ckpt = torch.load(checkpoint_file, map_location=map_location, weights_only=False)
+    ckpt = verified_load(checkpoint_file, map_location=map_location, weights_only=False)
     state = ckpt["model_state"]
     try:
         model.load_state_dict(state)

@@ -19,8 +19,9 @@ B200-specific changes, none of which alter the math:
   host sync inside the loop (the reference has two per step);
 * the NaN check reads the previous micro-batch's loss from a pinned host copy made
   asynchronously, instead of synchronising on the current one;
-* checkpoints are written atomically (temporary file + rename) and the device-timed
-  throughput (samples/s, max over ranks) is logged next to the reference's keys.
+* checkpoints are written atomically (temporary file + rename) with a SHA-256 record that is
+  checked on load (``utils/checkpoint_io.py``), and the throughput (samples/s) and model FLOP
+  rate (TFLOP/s, whole job) are logged next to the reference's keys.
 """
 
 from __future__ import annotations
@@ -45,6 +46,7 @@ from ..models.swin import get_model, strip_module_prefix
 from ..parallel import comm
 from ..parallel.grad_sync import GradReducer, order_params
 from ..parallel.helpers import init_params_for_shared_weights
+from ..utils.checkpoint_io import atomic_save, verified_load  # noqa: F401 (atomic_save re-exported)
 from ..utils.flops import FlopsCalculator
 from ..utils.profiler import init_profiler, profile_range
 from .grad_norm import ShardedNorm
@@ -80,12 +82,6 @@ class DataParallel(nn.Module):
 
     def no_sync(self):
         return self.reducer.no_sync() if self.reducer is not None else nullcontext()
-
-
-def atomic_save(obj, path: str) -> None:
-    tmp = path + ".tmp"
-    torch.save(obj, tmp)
-    os.replace(tmp, path)
 
 
 def experiment_dir(cfg) -> str:
@@ -519,6 +515,9 @@ class Trainer:
         self.logs["grad"] = float(grad.item())
         samples = n_mbs * int(self.cfg.parallelism.micro_batch_size) * comm.get_size("dp")
         self.logs["samples_per_sec"] = samples / max(self.logs["train_time"], 1e-9)
+        # model FLOP rate of the whole job over the interval (forward x 3 for the backward)
+        interval_flops = fwd * 3 * int(self.cfg.train.num_rollout_steps) * n_mbs * comm.get_size("dp")
+        self.logs["tflops_per_sec"] = interval_flops / max(self.logs["train_time"], 1e-9) / 1e12
         if self.log_to_wandb:
             import wandb
 
@@ -594,7 +593,7 @@ class Trainer:
     def restore_checkpoint(self, checkpoint_path, restore_optimizer=True, restore_scheduler=True,
                            restore_dataset=False):
         path = self.modify_checkpoint_path(checkpoint_path)
-        ckpt = torch.load(path, map_location=self.device, weights_only=False)
+        ckpt = verified_load(path, map_location=self.device, weights_only=False)
         state = ckpt["model_state"]
         try:
             self.model.load_state_dict(state)

@@ -153,3 +153,33 @@ def test_device_prefetch_passes_through_on_cpu():
     src = [torch.full((2, 3), float(i)) for i in range(5)]
     out = list(device_prefetch(iter(src), "cpu"))
     assert len(out) == 5 and all(a is b for a, b in zip(out, src))
+
+
+def test_checkpoint_checksum_detects_corruption(tmp_path):
+    """atomic_save records a SHA-256 beside the file; verified_load refuses a corrupted file,
+    completes a record left pending by an interrupted save, and loads record-less files."""
+    import shutil
+
+    from neural_scaling_weather_b200.utils.checkpoint_io import atomic_save, verified_load
+
+    p = str(tmp_path / "ckpt.tar")
+    atomic_save({"a": torch.arange(10)}, p)
+    assert os.path.exists(p + ".sha256") and not os.path.exists(p + ".tmp")
+    assert torch.equal(verified_load(p)["a"], torch.arange(10))
+    # a save interrupted between its two renames: new file in place, its record still pending
+    shutil.copy(p + ".sha256", str(tmp_path / "old.sha256"))
+    atomic_save({"a": torch.arange(12)}, p)
+    os.replace(p + ".sha256", p + ".sha256.tmp")
+    shutil.copy(str(tmp_path / "old.sha256"), p + ".sha256")
+    assert torch.equal(verified_load(p)["a"], torch.arange(12))
+    assert not os.path.exists(p + ".sha256.tmp")
+    # one flipped byte is caught
+    data = bytearray(open(p, "rb").read())
+    data[len(data) // 2] ^= 0xFF
+    open(p, "wb").write(bytes(data))
+    with pytest.raises(RuntimeError, match="SHA-256"):
+        verified_load(p)
+    # files without a record (the reference's checkpoints) load unchecked
+    q = str(tmp_path / "ref.tar")
+    torch.save({"b": 1}, q)
+    assert verified_load(q)["b"] == 1
