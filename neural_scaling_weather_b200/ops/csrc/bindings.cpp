@@ -144,11 +144,17 @@ Tensor gemm(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor
   need_cuda(B, "B");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm: A [M,K], B [N,K]");
   TORCH_CHECK(A.scalar_type() == B.scalar_type(), "gemm: A and B must share a dtype");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous(), "gemm: A and B must be contiguous");
   const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  const auto out_type = out_f32 ? at::kFloat : A.scalar_type();
   Tensor D;
   if (out.has_value() && out->defined()) {
     D = *out;
     need_cuda(D, "out");
+    // the kernel writes M x N elements with leading dimension N from D's first element
+    TORCH_CHECK(D.dim() == 2 && D.size(0) == M && D.size(1) == N && D.is_contiguous(),
+                "gemm: out must be a contiguous [M, N] tensor");
+    TORCH_CHECK(D.scalar_type() == out_type, "gemm: out dtype must be fp32 with out_f32, else A's dtype");
   } else {
     D = torch::empty({M, N}, A.options().dtype(out_f32 ? at::kFloat : A.scalar_type()));
   }
@@ -166,14 +172,19 @@ Tensor gemm(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor
   if (residual.has_value() && residual->defined()) {
     need_cuda(*residual, "residual");
     TORCH_CHECK(residual->scalar_type() == A.scalar_type(), "residual dtype");
+    g.res_period = res_period > 0 ? res_period : M;
+    TORCH_CHECK(residual->is_contiguous() && residual->numel() == g.res_period * N,
+                "gemm: residual must be a contiguous [res_period (or M), N] tensor");
     g.residual = residual->data_ptr();
     g.ldr = N;
-    g.res_period = res_period > 0 ? res_period : M;
   }
   if (preact.has_value() && preact->defined()) {
     need_cuda(*preact, "preact");
+    TORCH_CHECK(preact->is_contiguous() && preact->numel() == M * N && preact->scalar_type() == A.scalar_type(),
+                "gemm: preact must be a contiguous [M, N] tensor of A's dtype");
     g.preact = preact->data_ptr();
   }
+  TORCH_CHECK(!g.bias || bias->numel() == N, "gemm: bias must have N elements");
   g.act = (int)act;
   g.dtype = dt_code(A);
   g.out_f32 = out_f32 ? 1 : 0;
