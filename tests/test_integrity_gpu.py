@@ -116,3 +116,29 @@ def test_model_step_is_deterministic():
     for (name, _), a, b in zip(model.named_parameters(), g1, g2):
         assert torch.equal(a, b), name
     assert _ext.require().read_error_flag(True) == 0
+
+
+def test_bounded_wait_reports_a_peer_that_never_signals():
+    """The fused tensor-parallel GEMM + all-reduce waits for every peer's per-tile flag with a
+    time budget.  Driven on one GPU with a stand-in peer whose flags nothing ever sets, the
+    kernel must give up, record the wait timeout in the device error word and return, leaving
+    the context usable (no fault, trap or hang is involved)."""
+    from neural_scaling_weather_b200.parallel.symm import FLAG_BASE
+
+    ext = _ext.require()
+    ext.read_error_flag(True)
+    torch.manual_seed(5)
+    M, N, K = 256, 256, 64
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=DEV, dtype=torch.bfloat16)
+    tiles = (M // 128) * (N // 256)
+    parts = [torch.zeros(M * N, device=DEV, dtype=torch.bfloat16) for _ in range(2)]
+    flags = [torch.zeros(FLAG_BASE + 2 * tiles, device=DEV, dtype=torch.int32) for _ in range(2)]
+    ext.gemm_allreduce(a, b, None, None, [p.data_ptr() for p in parts], [f.data_ptr() for f in flags], 0)
+    torch.cuda.synchronize()
+    assert ext.read_error_flag(True) == 1  # wait timeout
+    # the context still works
+    d = ext.gemm(a, b, impl=1)
+    ref = a.float() @ b.float().t()
+    assert ((d.float() - ref).norm() / ref.norm()).item() < 1e-2
+    assert ext.read_error_flag(True) == 0
