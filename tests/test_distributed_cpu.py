@@ -235,3 +235,40 @@ def test_fused_collectives_not_available_without_cuda_group():
     symm.disable("tp", "test")
     assert symm.available("tp") is False
     symm.reset()
+
+
+# ----------------------------------------------------------------------------- data sharding
+def _epoch_coverage_worker(rank, world, out_dir):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from neural_scaling_weather_b200.data.synthetic import SyntheticERA5
+    from neural_scaling_weather_b200.parallel import comm
+
+    comm.init_model_parallel_info(tp=1, sp1=1, sp2=1, dp=world)
+    ds = SyntheticERA5(nlat=8, nlon=16, sfc_vars=["a"], pl_vars=[], levels=[], n_times=103, dt_scale=3,
+                       invariants=[], micro_batch_size=1)
+    for epoch in range(2):
+        idx = torch.from_numpy(ds.epoch_indices(epoch).astype(np.int64))
+        parts = [torch.zeros_like(idx) for _ in range(world)]
+        dist.all_gather(parts, idx)
+        if rank == 0:
+            allidx = torch.cat(parts).numpy()
+            # no sample twice in an epoch, every rank the same count, all of them valid starts
+            assert len(np.unique(allidx)) == len(allidx) == world * ds.n_samples_shard
+            assert allidx.min() >= 0 and allidx.max() < ds.n_samples_total
+            # the union is the first world * shard entries of that epoch's global permutation
+            perm = np.random.default_rng(ds.seed + epoch).permutation(ds.n_samples_total)
+            assert np.array_equal(allidx, perm[:world * ds.n_samples_shard])
+        # each window is temporal_context + rollout steps at the dataset's stride
+        hrs = ds.window_hours(int(idx[0]))
+        assert len(hrs) == ds.temporal_context_window + ds.num_rollout_steps
+        assert np.all(np.diff(hrs) == 3)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_epoch_covers_every_sample_once_across_dp_ranks(tmp_path, world):
+    """The DALI-epoch check of the reference (``tests/test_dali_es.py``) for the synthetic
+    loader: one epoch over all dp ranks emits every sample window exactly once."""
+    run(_epoch_coverage_worker, world, str(tmp_path))
