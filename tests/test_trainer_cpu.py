@@ -183,3 +183,49 @@ def test_checkpoint_checksum_detects_corruption(tmp_path):
     q = str(tmp_path / "ref.tar")
     torch.save({"b": 1}, q)
     assert verified_load(q)["b"] == 1
+
+
+def _infer(rank, world, exp_dir, ckpt_dir, out_path, threshold="1e9"):
+    import torch
+
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.inference.inferencer import Inferencer
+
+    cfg = C.compose("default", BASE + [
+        f"hydra.run.dir={exp_dir}", f"inference.checkpoint={ckpt_dir}/checkpoints/ckpt.tar",
+        f"inference.checkpoint_hyperparams={ckpt_dir}/hyperparameters.yaml",
+        "inference.start_date='2018-01-01T00'", "inference.end_date='2018-01-02T12'",
+        "inference.time_horizon_in_hours=12", "inference.spectra_times_in_hours=[6]",
+        f"inference.unstable_rmse_threshold={threshold}"])
+    out = Inferencer(cfg).launch()
+    if rank == 0:
+        torch.save({"rmse": out["rmse"], "acc": out["acc"], "spectra": out["spectra"][6],
+                    "unstable": out["unstable"]}, out_path)
+
+
+def test_inference_rollout_scores_and_dp_split(tmp_path):
+    """Train a tiny model briefly, then roll it out from four initial conditions (every 12 h)
+    to 12 h (the instability cut is lifted: a two-step model is far from the reference's
+    threshold): RMSE / ACC per channel and lead, power spectra at 6 h and the .npy outputs; the ICs
+    split over two dp ranks (round-robin, sums all-reduced) give the single-rank scores."""
+    ckpt_dir = str(tmp_path / "train")
+    run(_train, 1, ckpt_dir, ["optimizer.max_iterations=2", "train.log_every=2"], None, None)
+    one, two = str(tmp_path / "one.pt"), str(tmp_path / "two.pt")
+    run(_infer, 1, str(tmp_path / "inf1"), ckpt_dir, one)
+    run(_infer, 2, str(tmp_path / "inf2"), ckpt_dir, two)
+    a, b = torch.load(one), torch.load(two)
+    n_ch = a["rmse"].shape[0]
+    assert a["rmse"].shape == (n_ch, 2) and a["acc"].shape == (n_ch, 2)
+    assert a["spectra"].shape[:2] == (2, n_ch)
+    assert torch.isfinite(a["rmse"]).all() and (a["rmse"] > 0).all()
+    assert (a["acc"].abs() <= 1 + 1e-5).all()
+    assert a["unstable"] == b["unstable"] == 0
+    for k in ("rmse", "acc", "spectra"):
+        assert torch.allclose(a[k], b[k], rtol=1e-5, atol=1e-7), k
+    assert (tmp_path / "inf1" / "rmse_u10m.npy").exists()
+    assert (tmp_path / "inf1" / "spectra_u10m_6h.npy").exists()
+    # every IC over the cut (threshold 0): all four dropped, counted once across the dp ranks
+    cut = str(tmp_path / "cut.pt")
+    run(_infer, 2, str(tmp_path / "inf3"), ckpt_dir, cut, "0")
+    c = torch.load(cut)
+    assert c["unstable"] == 4 and torch.equal(c["rmse"], torch.zeros_like(c["rmse"]))
