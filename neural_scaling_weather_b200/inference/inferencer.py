@@ -11,8 +11,9 @@ all-reduced over dp and averaged, and ``rmse_{ch}.npy`` / ``spectra_{ch}_{lt}h.n
 written (``:466-560``).
 
 Additions: a latitude-weighted anomaly correlation (ACC) per channel and lead, the choice
-of compute precision (``inference.precision``: ``fp32`` as in the reference, or ``bf16``
-for the fused kernels) and device-timed milliseconds per rollout step.
+of compute precision (``inference.precision``: ``fp32`` as in the reference, computed with
+the plain-PyTorch operators on the GPU, or ``bf16`` / ``fp16`` for the fused kernels) and
+device-timed milliseconds per rollout step.
 """
 
 from __future__ import annotations
@@ -26,6 +27,7 @@ import torch
 import torch.distributed as dist
 
 from .. import config as C
+from .. import ops
 from ..data import get_dataset, get_preprocessor
 from ..losses import anomaly_correlation, get_metric
 from ..models.swin import get_model, strip_module_prefix
@@ -126,10 +128,15 @@ class Inferencer:
             return allgather_forward_split_backward(x, -2, self.metadata["sp_shapes"][0], "sp1")
 
     def _forward(self, inputs):
-        if self.dtype is not None and self.device.type == "cuda":
+        if self.device.type != "cuda":
+            return self.model(inputs)
+        if self.dtype is not None:
             with torch.autocast("cuda", dtype=self.dtype):
                 return self.model(inputs).float()
-        return self.model(inputs)
+        # fp32: the fused kernels compute in 16 bits, so fp32 rollouts use the plain-PyTorch
+        # operators (fp32 arithmetic, as the reference runs inference)
+        with ops.reference_ops():
+            return self.model(inputs)
 
     def inference(self):
         timed = self.device.type == "cuda"

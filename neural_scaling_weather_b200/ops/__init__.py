@@ -8,11 +8,16 @@ optimizer kernels); a CUDA call without the extension raises.
 
 Compute precision on CUDA follows ``torch.autocast``: inside an autocast region (the
 trainer uses one, as the reference does) activations are bf16 (or fp16); parameters stay
-fp32 masters and are cast once per optimizer step into a cached low-precision copy.
+fp32 masters and are cast once per optimizer step into a cached low-precision copy.  The
+kernels compute in 16 bits, so fp32 CUDA inputs outside autocast are also computed in bf16;
+for fp32 arithmetic on the GPU (fp32 inference, as the reference runs it) wrap the call in
+:func:`reference_ops`, which sends CUDA tensors through the plain-PyTorch oracle too.
 """
 
 from __future__ import annotations
 
+import contextlib
+import threading
 from typing import Optional, Sequence, Union
 
 import torch
@@ -32,8 +37,23 @@ def compute_dtype(t: torch.Tensor) -> torch.dtype:
     return t.dtype
 
 
+_mode = threading.local()
+
+
+@contextlib.contextmanager
+def reference_ops():
+    """Within this context every operator runs the plain-PyTorch oracle (:mod:`.reference`),
+    on CUDA tensors too, in the tensors' own precision (fp32 math for fp32 inputs)."""
+    prev = getattr(_mode, "reference", False)
+    _mode.reference = True
+    try:
+        yield
+    finally:
+        _mode.reference = prev
+
+
 def _use_cuda(t: torch.Tensor) -> bool:
-    if not t.is_cuda:
+    if not t.is_cuda or getattr(_mode, "reference", False):
         return False
     require_extension()
     return True
