@@ -57,3 +57,40 @@ def test_drop_path():
     y = drop_path(x, 0.25, training=True)
     kept = (y[:, 0] != 0).float().mean().item()
     assert 0.65 < kept < 0.85 and torch.allclose(y[y != 0], torch.full_like(y[y != 0], 1 / 0.75))
+
+
+def test_profiler_ranks_epoch_window_and_ranges(monkeypatch):
+    """NVTX ranges only on the profiled ranks, and the CUDA-profiler window opens for
+    profile_epoch and closes on the next epoch (calls recorded through stand-ins, no GPU)."""
+    import torch
+
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.utils import profiler as P
+
+    calls = []
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda.profiler, "start", lambda: calls.append("start"))
+    monkeypatch.setattr(torch.cuda.profiler, "stop", lambda: calls.append("stop"))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: calls.append(f"push:{name}"))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append("pop"))
+    cfg = C.create(dict(profiler=dict(enabled=True, profile_ranks=[0], profile_epoch=1)))
+    prof = P.init_profiler(cfg)
+
+    @P.profile("mlp")
+    def f(x):
+        return x + 1
+
+    try:
+        prof.set_epoch(0)
+        assert f(1) == 2
+        prof.set_epoch(1)
+        with P.profile_range("forward pass"):
+            pass
+        prof.set_epoch(2)
+        assert calls == ["push:mlp", "pop", "start", "push:forward pass", "pop", "stop"]
+        calls.clear()
+        prof.current_rank = 1  # not a profiled rank: no ranges, no window
+        prof.set_epoch(1)
+        assert f(2) == 3 and calls == []
+    finally:
+        P._profiler = None
