@@ -1,7 +1,13 @@
 """Drive the unmodified reference code (copied to ``baseline/_ref``) through its own API.
 
 The reference is a plain Python tree without packaging metadata, so ``pip install``
-refuses it; it is placed in ``baseline/_ref`` as a source copy and imported from there.
+refuses it ("Neither 'setup.py' nor 'pyproject.toml' found"); ``ensure_reference()``
+places an unmodified source copy in ``baseline/_ref`` (git-ignored) and it is imported from
+there.  The source location comes from the ``NSW_REFERENCE_SRC`` environment variable, or
+else from the ``reference_path`` key of ``BASELINE.json`` at the repository root.  The copy
+is made by ``__graft_entry__.build()`` and again on demand by ``available()``, so a checkout
+that lacks it (a fresh clone, a GPU box that received the tree) fills it when the source is
+reachable; the copied tree travels with the repository to machines where it is not.
 Packages that its modules import at top level but that are absent on this platform are
 replaced by inert stand-ins registered in ``sys.modules`` *before* the import:
 
@@ -17,7 +23,9 @@ scheduler and the trainer's gradient-norm clipping all run as shipped.
 
 from __future__ import annotations
 
+import json
 import os
+import shutil
 import sys
 import types
 
@@ -81,8 +89,46 @@ def install_stubs():
         sys.modules["torch_harmonics"] = _module("torch_harmonics", RealSHT=RealSHT)
 
 
+def reference_source() -> str | None:
+    """Directory holding the reference's source tree, or None if it is not named anywhere."""
+    src = os.environ.get("NSW_REFERENCE_SRC")
+    if src:
+        return src
+    try:
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            return json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
+
+
+def _is_tree(path) -> bool:
+    return bool(path) and all(os.path.isdir(os.path.join(path, d)) for d in ("models", "distributed", "utils"))
+
+
+def ensure_reference() -> bool:
+    """Copy the reference source tree, unmodified, to ``baseline/_ref`` if it is not there.
+
+    The copy goes to a temporary sibling first and is renamed into place, so a concurrent
+    reader never sees a half-written tree.  Returns whether the copy is present afterwards.
+    """
+    if _is_tree(REF_ROOT):
+        return True
+    src = reference_source()
+    if not _is_tree(src):
+        return False
+    tmp = f"{REF_ROOT}.tmp{os.getpid()}"
+    if os.path.isdir(tmp):
+        shutil.rmtree(tmp)
+    shutil.copytree(src, tmp, ignore=shutil.ignore_patterns(".git", "__pycache__", "*.pyc"))
+    try:
+        os.rename(tmp, REF_ROOT)
+    except OSError:  # another process placed it first
+        shutil.rmtree(tmp, ignore_errors=True)
+    return _is_tree(REF_ROOT)
+
+
 def available() -> bool:
-    return os.path.isdir(os.path.join(REF_ROOT, "models"))
+    return ensure_reference()
 
 
 def import_reference():

@@ -1,6 +1,6 @@
 """Timing of the fused tensor-parallel GEMM + all-reduce against GEMM then NCCL all-reduce.
 
-``python -m torch.distributed.run --nproc-per-node N -m neural_scaling_weather_b200.ops.bench_collectives``
+``python -m torch.distributed.run --nproc-per-node N benchmarks/collectives.py``
 (N = 2..8 GPUs of one node).  Shape: a row-parallel projection of the Swin p4-e1024 block
 (64800 tokens, 1024 outputs, 1024 / N inputs per rank) with bias and residual.  Times are CUDA
 events on each rank around several launches, reported as the maximum over ranks; the roofline
@@ -14,9 +14,12 @@ import argparse
 import datetime
 import json
 import os
+import sys
 
 import torch
 import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
 def main():
@@ -30,8 +33,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    from . import _ext, linear_allreduce
-    from ..parallel import comm, symm
+    from neural_scaling_weather_b200.ops import _ext, linear_allreduce
+    from neural_scaling_weather_b200.parallel import comm, symm
 
     comm.init_model_parallel_info(tp=world, sp1=1, sp2=1, dp=1)
     ext = _ext.require()

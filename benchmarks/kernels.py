@@ -1,6 +1,6 @@
 """Kernel microbenchmarks with roofline fractions.
 
-``python -m neural_scaling_weather_b200.ops.bench_kernels <kernel> [--iters N] [shape flags]``
+``python benchmarks/kernels.py <kernel> [--iters N] [shape flags]``
 
 Each kernel is timed with CUDA events on the launching stream after warm-up, with a
 synchronize on both sides; the inputs of the default shapes are larger than the 126 MB L2.
@@ -14,13 +14,15 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import sys
 
 import torch
 
-from . import _ext
-from .geometry import WindowGeometry
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
 
-ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from neural_scaling_weather_b200.ops import _ext  # noqa: E402
+from neural_scaling_weather_b200.ops.geometry import WindowGeometry  # noqa: E402
 
 
 def peaks():

@@ -168,6 +168,10 @@ class Inferencer:
                         self.spectra[lead][self.ic_count, 1] = power_spectrum(tg, self.sht)[0].float()
                     window = torch.roll(window, shifts=-1, dims=1)
                     window[:, -1].copy_(gen[:, 0])
+                if self.device.type == "cuda":
+                    # a kernel whose bounded wait ran out leaves its outputs incomplete: stop
+                    # before this initial condition's scores are counted
+                    ops._ext.check_device_errors()
                 self.ic_count += 1
 
     def compute_final_metrics(self):

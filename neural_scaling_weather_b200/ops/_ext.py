@@ -46,14 +46,28 @@ def so_path() -> str | None:
     return getattr(ext, "__file__", None) if ext is not None else None
 
 
+ERROR_NAMES = {1: "bounded wait timed out", 2: "index out of bounds", 3: "invalid kernel argument"}
+
+
+class DeviceError(RuntimeError):
+    """A kernel of the extension recorded an error in the device error word: a bounded wait
+    that ran out (its outputs are incomplete) or a rejected argument."""
+
+    def __init__(self, code: int):
+        self.code = int(code)
+        super().__init__(f"device error word set: code {self.code} ({ERROR_NAMES.get(self.code, 'unknown')}); "
+                         "the outputs of the kernels since the last check are not valid")
+
+
 def check_device_errors() -> None:
-    """Raise if a kernel recorded a bounded-wait timeout or a bounds violation."""
+    """Raise :class:`DeviceError` if a kernel recorded a bounded-wait timeout or a bounds
+    violation (a synchronous read of the device error word, which is then cleared)."""
     ext = load()
     if ext is None:
         return
     code = ext.read_error_flag(True)
     if code != 0:
-        raise RuntimeError(f"device-side error flag set: code {code}")
+        raise DeviceError(code)
 
 
 if os.environ.get("NSW_REQUIRE_EXT") == "1":  # pragma: no cover

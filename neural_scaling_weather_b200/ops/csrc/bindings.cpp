@@ -50,6 +50,23 @@ int read_error_flag(bool clear) {
   return v;
 }
 
+// The device error word as a one-element int32 tensor (a view: no copy, not owned), so the
+// host can read it with an asynchronous copy alongside other per-step results.
+Tensor error_word() {
+  int dev = 0;
+  check(cudaGetDevice(&dev), "cudaGetDevice");
+  int* f = nsw::device_error_flag();
+  TORCH_CHECK(f != nullptr, "device error word unavailable");
+  return torch::from_blob(f, {1}, torch::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev));
+}
+
+// Writes a code into the device error word (what a kernel does when a bounded wait runs
+// out); lets tests check that the host-side checks stop a run without any kernel failing.
+void set_error_flag(int code) {
+  int* f = nsw::device_error_flag();
+  check(cudaMemcpy(f, &code, sizeof(int), cudaMemcpyHostToDevice), "set_error_flag");
+}
+
 // ------------------------------------------------------------------------------ norms
 std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
   need_cuda(x, "x");
@@ -449,6 +466,8 @@ std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of neural_scaling_weather_b200";
   m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
+  m.def("error_word", &error_word);
+  m.def("set_error_flag", &set_error_flag);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
         py::arg("eps") = -1.0, py::arg("add") = py::none());

@@ -1227,9 +1227,33 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   auto k = gemm_kernel<T, BN, STAGES, RT, EW>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-  int grid = sm_count();
+  const int threads = 64 + 32 * EW;
+  static int resident = 0;  // co-resident CTAs of this kernel on the whole device
+  if (!resident) {
+    int per_sm = 0;
+    NSW_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, smem));
+    resident = (per_sm > 0 ? per_sm : 1) * sm_count();
+  }
+  int grid = sm_count() < resident ? sm_count() : resident;
   if (tiles < grid) grid = (int)tiles;
-  k<<<grid, 64 + 32 * EW, smem, s>>>(ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag());
+  if (a.ar_world > 1) {
+    // The fused all-reduce ends with every CTA waiting for all CTAs of every rank (read-done
+    // counters), which completes only if the whole grid is resident at once.  A cooperative
+    // launch guarantees that or fails to launch (for example when MPS or another context holds
+    // SMs), instead of leaving the ranks to run into the bounded waits.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag());
+  }
+  k<<<grid, threads, smem, s>>>(ma, mb, a.M, a.N, a.K, ep, idesc, device_error_flag());
   return cudaGetLastError();
 }
 

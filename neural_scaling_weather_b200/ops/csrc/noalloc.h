@@ -22,6 +22,14 @@
 //   * n (the normalised size) must be a multiple of 8 and at most
 //     NSW_NOALLOC_RMSNORM_MAX_N; larger sizes are rejected with NSW_NOALLOC_ERR_TOO_LARGE
 //     before anything is launched.
+//   * dy, x and dx are accessed 16 bytes at a time: their addresses must be multiples of
+//     16 bytes (a row offset into a larger buffer must keep that), otherwise the call
+//     returns NSW_NOALLOC_ERR_BAD_ARG.
+//   * rows == 0 writes zeros to dw (an asynchronous memset on the stream) and launches
+//     no kernel.
+//   * If a CUDA error from an earlier call on this thread is still pending, the call
+//     returns NSW_NOALLOC_ERR_PENDING and launches nothing (the pending error is left for
+//     the caller to read), so that NSW_NOALLOC_ERR_LAUNCH always means this call's launch.
 #pragma once
 
 #include <stdint.h>
@@ -34,6 +42,7 @@
 #define NSW_NOALLOC_ERR_BAD_ARG 1002
 #define NSW_NOALLOC_ERR_SYMBOL 1003
 #define NSW_NOALLOC_ERR_LAUNCH 1004
+#define NSW_NOALLOC_ERR_PENDING 1005
 
 #ifdef __cplusplus
 extern "C" {

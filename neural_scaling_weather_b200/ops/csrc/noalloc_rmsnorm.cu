@@ -139,11 +139,20 @@ extern "C" __attribute__((visibility("default"))) int nsw_rmsnorm_bwd_noalloc(
   if (n > NSW_NOALLOC_RMSNORM_MAX_N) return NSW_NOALLOC_ERR_TOO_LARGE;
   if (n <= 0 || n % 8 != 0 || rows < 0 || !dy || !x || !w || !rstd || !dx || !dw) return NSW_NOALLOC_ERR_BAD_ARG;
   if (dtype != 0 && dtype != 1) return NSW_NOALLOC_ERR_BAD_ARG;
-  if (rows == 0) return NSW_NOALLOC_OK;
+  // dy, x and dx are read and written 16 bytes at a time
+  if (((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) & 15) != 0)
+    return NSW_NOALLOC_ERR_BAD_ARG;
+  // An error left pending by an earlier CUDA call of the caller would otherwise be read back
+  // (and cleared) below as if one of these launches had failed; report it without clearing.
+  if (cudaPeekAtLastError() != cudaSuccess) return NSW_NOALLOC_ERR_PENDING;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {  // no rows: the weight gradient is zero (dw is written, not added)
+    return cudaMemsetAsync(dw, 0, (size_t)n * sizeof(float), s) == cudaSuccess ? NSW_NOALLOC_OK
+                                                                                : NSW_NOALLOC_ERR_LAUNCH;
+  }
   float* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch);
   if (rc != NSW_NOALLOC_OK) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == 0) return launch<__nv_bfloat16>(dy, x, w, rstd, dx, dw, rows, n, s, scratch);
   return launch<__half>(dy, x, w, rstd, dx, dw, rows, n, s, scratch);
 }
@@ -152,9 +161,11 @@ extern "C" __attribute__((visibility("default"))) const char* nsw_noalloc_error_
   switch (code) {
     case NSW_NOALLOC_OK: return "ok";
     case NSW_NOALLOC_ERR_TOO_LARGE: return "n exceeds NSW_NOALLOC_RMSNORM_MAX_N (2048)";
-    case NSW_NOALLOC_ERR_BAD_ARG: return "invalid argument (null pointer, n not a positive multiple of 8, or dtype)";
+    case NSW_NOALLOC_ERR_BAD_ARG:
+      return "invalid argument (null pointer, dy/x/dx not 16-byte aligned, n not a positive multiple of 8, or dtype)";
     case NSW_NOALLOC_ERR_SYMBOL: return "could not obtain the device address of the scratch array";
     case NSW_NOALLOC_ERR_LAUNCH: return "kernel launch failed";
+    case NSW_NOALLOC_ERR_PENDING: return "a CUDA error from an earlier call was already pending; nothing launched";
     default: return "unknown error";
   }
 }

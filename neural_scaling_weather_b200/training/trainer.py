@@ -18,7 +18,11 @@ B200-specific changes, none of which alter the math:
 * the clip coefficient and the logged gradient norm are device tensors: no ``.item()``
   host sync inside the loop (the reference has two per step);
 * the NaN check reads the previous micro-batch's loss from a pinned host copy made
-  asynchronously, instead of synchronising on the current one;
+  asynchronously, instead of synchronising on the current one; the device error word of
+  the extension (set by a kernel whose bounded wait ran out) is copied with it, and a
+  nonzero word stops training with :class:`~..ops._ext.DeviceError`; the word is also read
+  synchronously before every validation/checkpoint and at the end of training, so no
+  checkpoint is written from a step whose kernels gave up;
 * checkpoints are written atomically (temporary file + rename) with a SHA-256 record that is
   checked on load (``utils/checkpoint_io.py``), and the throughput (samples/s) and model FLOP
   rate (TFLOP/s, whole job) are logged next to the reference's keys.
@@ -244,6 +248,12 @@ class Trainer:
                           else max(1, int(cfg.train.log_frequency * self.max_iters)))
         self._loss_host = torch.zeros(1, dtype=torch.float32, pin_memory=self.device.type == "cuda")
         self._loss_evt = None
+        self._err_host = torch.zeros(1, dtype=torch.int32, pin_memory=self.device.type == "cuda")
+        self._err_word = None
+        if self.device.type == "cuda":
+            from ..ops import _ext
+
+            self._err_word = _ext.require().error_word()
         if self.log_to_screen:
             logging.info(f"number of model parameters (M): {count_parameters(self.model)}")
             logging.info(f"number of training steps per epoch: {self.iters_per_epoch}")
@@ -280,22 +290,43 @@ class Trainer:
         if self.log_to_screen:
             logging.info(f"Application time: {time.time() - app:.2f}s")
         self.sync_devices()
+        self.check_device_errors()
 
     _stop = False
 
     def _nan_seen(self) -> bool:
-        """NaN check on the previous micro-batch's accumulated loss (no sync on this one)."""
+        """NaN check on the previous micro-batch's accumulated loss (no sync on this one).
+        Raises :class:`DeviceError` if the device error word copied with that loss is set."""
         if self.device.type != "cuda":
             return bool(torch.isnan(self.train_loss).item())
         if self._loss_evt is not None and self._loss_evt.query():
+            if int(self._err_host[0]) != 0:
+                self._device_error(int(self._err_host[0]))
             return bool(math.isnan(float(self._loss_host[0])))
         return False
 
     def _snapshot_loss(self):
         if self.device.type == "cuda":
             self._loss_host.copy_(self.train_loss, non_blocking=True)
+            self._err_host.copy_(self._err_word, non_blocking=True)
             self._loss_evt = torch.cuda.Event()
             self._loss_evt.record()
+
+    def check_device_errors(self):
+        """Synchronous read (and clear) of the device error word; raises if it is set."""
+        if self.device.type == "cuda":
+            from ..ops import _ext
+
+            code = _ext.require().read_error_flag(True)
+            if code != 0:
+                self._device_error(code)
+
+    def _device_error(self, code: int):
+        from ..ops._ext import DeviceError
+
+        self._stop = True
+        logging.error(f"device error word {code} set by a kernel; stopping without a checkpoint")
+        raise DeviceError(code)
 
     def optimizer_step(self):
         """Reduce, clip, step, schedule, log the post-step norm and zero the grads."""
@@ -491,6 +522,7 @@ class Trainer:
 
     def validate_and_checkpoint(self):
         self.sync_devices()
+        self.check_device_errors()
         self.logs["train_time"] = time.time() - self.train_time
         self.logs["val_time"], self.logs["val_nsteps"], _ = self.val_one_epoch()
         t0 = time.time()

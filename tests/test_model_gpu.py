@@ -74,6 +74,42 @@ def test_trainer_steps_on_gpu(tmp_path):
     dist.destroy_process_group()
 
 
+def test_trainer_stops_when_device_error_word_is_set(tmp_path):
+    """A kernel whose bounded wait runs out sets the device error word and returns with
+    incomplete outputs; training must stop with DeviceError and write no checkpoint.  The
+    word is set from the host here (no kernel is made to fail)."""
+    import os
+
+    import torch.distributed as dist
+
+    from neural_scaling_weather_b200.ops._ext import DeviceError
+    from neural_scaling_weather_b200.training.trainer import Trainer
+
+    os.environ.setdefault("MASTER_PORT", "29535")
+    cfg = C.compose("default", [
+        f"hydra.run.dir={tmp_path}", "parallelism.backend=nccl", "model.embed_dim=64", "model.depth=2",
+        "model.num_heads=4", "model.window_size=[4,8]", "model.patch_size=2", "data.synthetic.nlat=32",
+        "data.synthetic.nlon=64", "data.synthetic.n_samples=40", "data.levels=[500]", "data.batch_size=2",
+        "optimizer=adamw", "optimizer.max_iterations=4", "train.log_every=2", "train.amp_dtype=bf16",
+        "logging.log_to_wandb=false", "train.seed=1"])
+    t = Trainer(cfg)
+    t.init_exp_dir(t.exp_dir)
+    t.build()
+    ext = _ext.require()
+    assert ext.read_error_flag(True) == 0
+    ext.set_error_flag(1)
+    try:
+        with pytest.raises(DeviceError) as info:
+            t.train()
+        assert info.value.code == 1
+        assert t.iters < 4
+        assert not (tmp_path / "checkpoints" / "ckpt.tar").exists()
+    finally:
+        ext.read_error_flag(True)
+        dist.destroy_process_group()
+    assert ext.read_error_flag(True) == 0
+
+
 def test_trainer_cuda_graph_matches_eager(tmp_path):
     """Micro-batches replayed from a captured CUDA graph (derived weight copies refreshed in
     place after each optimizer step) follow the eager loss and parameter trajectory."""

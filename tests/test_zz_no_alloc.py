@@ -20,6 +20,7 @@ from neural_scaling_weather_b200.ops import _ext  # noqa: E402
 
 MAX_N = 2048
 ERR_TOO_LARGE = 1001
+ERR_BAD_ARG = 1002
 
 
 def _lib():
@@ -75,3 +76,39 @@ def test_noalloc_rejects_sizes_beyond_maximum():
     rc = _call(lib, x, x, w, rstd, dx, dw, 0)
     assert rc == ERR_TOO_LARGE
     assert b"exceeds" in lib.nsw_noalloc_error_string(rc)
+
+
+def test_noalloc_zero_rows_writes_zero_weight_gradient():
+    _, lib = _lib()
+    n = 256
+    x = torch.zeros(0, n, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(n, device="cuda")
+    rstd = torch.ones(1, device="cuda")  # not read; any valid pointer
+    dx = torch.empty(1, n, device="cuda", dtype=torch.bfloat16)
+    dw = torch.full((n,), float("nan"), device="cuda")
+    dy = torch.empty(1, n, device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.nsw_rmsnorm_bwd_noalloc(dy.data_ptr(), dy.data_ptr(), w.data_ptr(), rstd.data_ptr(), dx.data_ptr(),
+                                     dw.data_ptr(), 0, n, 0, stream)
+    assert rc == 0, lib.nsw_noalloc_error_string(rc)
+    torch.cuda.synchronize()
+    assert torch.equal(dw, torch.zeros_like(dw))
+
+
+def test_noalloc_rejects_pointers_not_16_byte_aligned():
+    _, lib = _lib()
+    n, rows = 64, 8
+    buf = torch.randn(rows * n + 8, device="cuda").to(torch.bfloat16)
+    w = torch.ones(n, device="cuda")
+    rstd = torch.ones(rows, device="cuda")
+    dw = torch.empty(n, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    ok = buf.data_ptr()
+    odd = ok + 2  # one bf16 element in: 2-byte aligned only
+    for dy_p, x_p, dx_p in ((odd, ok, ok), (ok, odd, ok), (ok, ok, odd)):
+        dx = torch.empty(rows * n + 8, device="cuda", dtype=torch.bfloat16)
+        rc = lib.nsw_rmsnorm_bwd_noalloc(dy_p, x_p, w.data_ptr(), rstd.data_ptr(),
+                                         dx.data_ptr() + (dx_p - ok), dw.data_ptr(), rows, n, 0, stream)
+        assert rc == ERR_BAD_ARG
+        assert b"aligned" in lib.nsw_noalloc_error_string(rc)
+    torch.cuda.synchronize()
