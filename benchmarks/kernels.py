@@ -121,8 +121,6 @@ def bench_block_gemms(a):
 
 
 def bench_attention(a):
-    from . import window_attention
-
     B, H, W, nh, hd = 1, a.H, a.W, a.heads, 64
     C = nh * hd
     geom = WindowGeometry(window=(9, 18), shift=(4, 9), mask=True, mask_shift=4, row_offset=0, h_global=H)
@@ -135,11 +133,12 @@ def bench_attention(a):
     tokens = B * H * W
     L = 162
     flops = 4.0 * tokens * L * hd * nh  # QK^T and PV
-    impls = [(i, t) for i, t in ((1, "mma.sync"), (2, "tcgen05")) if a.impl in (0, i)]
-    for impl, tag in impls:
+    fimpls = [(i, t) for i, t in ((1, "mma.sync"), (2, "tcgen05"), (3, "tcgen05-ws")) if a.impl in (0, i)]
+    for impl, tag in fimpls:
         ms = timeit(lambda: ext.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, impl), a.iters)
         report(f"window_attn_fwd[{tag}] tokens={tokens} heads={nh}", ms, flops, 2 * tokens * 4 * C)
     dout = torch.randn_like(out)
+    impls = [(i, t) for i, t in ((1, "mma.sync"), (2, "tcgen05")) if a.impl in (0, i)]
     for impl, tag in impls:
         ms = timeit(lambda: ext.window_attn_bwd(qkv.view(-1, 3 * C), qw, kw, out, dout, lse, gi, hd ** -0.5,
                                                 impl), a.iters)
@@ -195,7 +194,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true")
     ap.add_argument("--impl", type=int, default=0,
-                    help="attention: 1 = mma.sync only, 2 = tcgen05 only; block GEMMs: 1 = one CTA per tile, "
+                    help="attention: 1 = mma.sync only, 2 = tcgen05 only, 3 = warp-specialised tcgen05 forward only; block GEMMs: 1 = one CTA per tile, "
                          "2 = CTA pair, 0 = default dispatch")
     a = ap.parse_args()
     if a.kernel in ("gemm", "all"):

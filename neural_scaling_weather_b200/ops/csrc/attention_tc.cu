@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include <algorithm>
 #include <cstring>
+#include <cstdlib>
 
 #include "kernels.h"
 
@@ -1243,6 +1244,539 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FWD_TMEM_COLS));
 }
 
+// ============================================================================ forward, warp-specialised
+// Persistent, one CTA of 16 warps per SM walking a contiguous range of (window, head) items, heads
+// fastest.  Unlike the kernel above (every warp takes every phase of one item, separated by block
+// barriers), each role runs its own loop and the roles hand work to one another through mbarriers,
+// so the elementwise work of one item overlaps the loads, the normalisation and the MMAs of others:
+//   warp 0        producer: the window's tables (token row, window-order index, mask label and the
+//                 per-key additive bias of every smem row) and TMA box loads of an item's q, k and v
+//                 rows into stage (n % 3) of a three-stage ring;
+//   warps 1, 2    MMA issuers (one elected lane each), one per softmax warpgroup:
+//                 S_t = Qhat_t Khat^T (A, B K-major smem) and O_t = P_t V (A = P read from TMEM,
+//                 B = V as an MN-major smem operand);
+//   warps 4-7     QK-RMSNorm of a landed stage's q and k rows in place (one thread per row), and
+//                 the norms of the normalised rows (a bound on the logits, below);
+//   warps 8-11,   softmax + epilogue warpgroups; warpgroup w takes the items with (n & 1) == w and
+//   12-15         owns TMEM columns [256 w, 256 w + 256): S at [0, 176) with P written back as
+//                 packed bf16 pairs over its front (tcgen05.st), O at [192, 256).
+// Each thread owns one query row (its TMEM lane), so the row max and row sum need no cross-warp
+// reduction.  The max is replaced by the Cauchy-Schwarz bound sl2 * |qhat_i| * max_j |khat_j| when
+// that bound is at most 48 (log2 units; P then stays a normal number), which skips one pass over S:
+// softmax and lse do not depend on the shift used, only its overflow safety does.  Query tile 0 is
+// rows [0, 128), tile 1 rows [NK - 128, NK), of which rows >= 128 are computed and stored.  O rows
+// go from registers to their tokens' positions (whole 128-byte rows, 16-byte stores); lse (log2
+// domain, window order) per row.  Every mbarrier wait is bounded and raises a CTA abort flag on
+// expiry (kErrWaitTimeout in the device error word); all roles then leave their loops, wait
+// (bounded) for their own TMA loads and MMAs, and the TMEM is freed.
+constexpr int WS_THREADS = 512;
+constexpr int WS_TMEM_COLS = 512;
+constexpr int WS_STAGES = 3;
+constexpr uint32_t WS_O_COL = 192;
+constexpr float WS_MAX_BOUND = 48.f;
+// wait budget in SM cycles (the SM clock, read without the latency of %globaltimer): 4e9 cycles
+// are 2 to 3 s between the power-capped and the maximum clock
+constexpr unsigned long long kWaitBudgetCycles = 4000000000ull;
+
+struct __align__(1024) SmemWS {
+  unsigned char q[WS_STAGES][ROWBUF];  // K-major SW128 rows, normalised in place
+  unsigned char k[WS_STAGES][ROWBUF];
+  unsigned char v[WS_STAGES][ROWBUF];  // MN-major B operand of O = P V
+  // additive log2-domain bias of key j for a query row of label 0 / 1: 0 for the same label,
+  // -100 log2(e) for the other, -inf for padding keys (j >= L, up to the last 32-key chunk)
+  float kbias[WS_STAGES][2][MAXL + 16];
+  int tok[WS_STAGES][MAXL];          // token row of smem row j
+  short wr[WS_STAGES][MAXL];         // window-order index of smem row j
+  signed char lab[WS_STAGES][MAXL];  // mask label of smem row j (-1: padding)
+  float qn[WS_STAGES][MAXL];         // |qhat| of q row j
+  float kn[WS_STAGES][4];            // max |khat| over each norm warp's k rows
+  int mixed[WS_STAGES];
+  float qwv[HD];
+  float kwv[HD];
+  uint64_t loaded[WS_STAGES];      // rows landed (TMA transaction count)
+  uint64_t normed[WS_STAGES];      // q/k normalised, norms written (4 norm warps)
+  uint64_t stage_free[WS_STAGES];  // MMAs done with the rows (commit) and tables read (4 warps)
+  uint64_t s_full[2];              // warpgroup w: S of the current tile in TMEM (MMA commit)
+  uint64_t p_ready[2];             // warpgroup w: P written to TMEM (4 warps)
+  uint64_t o_full[2];              // warpgroup w: O of the current tile in TMEM (MMA commit)
+  uint64_t o_free[2];              // warpgroup w: O drained from TMEM (4 warps)
+  uint64_t mma_done[2];            // MMA issuer w: every product it issued has completed
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void mb_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mb_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mb_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait of one thread on an mbarrier phase; false on timeout (error recorded, abort raised)
+// or once another role has raised the abort flag.  With abort == nullptr the flag is not watched
+// (clean-up waits) and a timeout records nothing.  Each try_wait carries a suspend-time hint, so a
+// waiting thread sleeps in the barrier unit until the phase completes (or about a millisecond
+// passes) instead of spinning: with fifteen waiting roles per CTA, spinning threads took most of
+// the issue slots from the working warps.
+__device__ __forceinline__ bool ws_wait1(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(a), "r"(parity), "r"(1000000u)
+        : "memory");
+    if (ok) return true;
+    if (abort && *abort) return false;
+    if ((unsigned long long)(clock64() - t0) > kWaitBudgetCycles) {
+      if (abort) {
+        if (err) record_error(err, kErrWaitTimeout);
+        *abort = 1;
+      }
+      return false;
+    }
+  }
+}
+// The same, polled by lane 0 and broadcast, so the warp leaves a loop as one.
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = ws_wait1(bar, parity, err, abort) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// 32 columns of this warp's lane quarter without waiting, and the wait naming the registers (so no
+// use of them is scheduled before it): the next chunk's load is in flight while one is processed.
+__device__ __forceinline__ void ld32_async(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void ld_wait32(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// Tables of window `w`'s smem rows, by one warp; returns whether the window mixes labels.
+__device__ __forceinline__ int ws_table(const AttnGeom& g, int64_t w, int nww, int nwh, int L, int* tok,
+                                        signed char* lab, short* wr, float (*kbias)[MAXL + 16], int lane) {
+  WinPos p;
+  p.wx = (int)(w % nww);
+  p.wy = (int)((w / nww) % nwh);
+  p.b = (int)(w / ((int64_t)nww * nwh));
+  const WinLoad wl = win_load(g, w, nww, nwh);
+  const int lab0 = label(g, p, 0);
+  const float ml2 = -100.f * kLog2e;
+  int mx = 0;
+  for (int j = lane; j < MAXL + 16; j += 32) {
+    const int i = j < L ? win_row(g, wl, j) : 0;
+    const int lb = j < L ? label(g, p, i) : -1;
+    if (j < MAXL) {
+      wr[j] = (short)i;
+      lab[j] = (signed char)lb;
+      tok[j] = j < L ? (int)token(g, p, i) : 0;
+    }
+    kbias[0][j] = lb < 0 ? -INFINITY : (lb != 0 ? ml2 : 0.f);
+    kbias[1][j] = lb < 0 ? -INFINITY : (lb != 1 ? ml2 : 0.f);
+    mx |= (j < L && lb != lab0);
+  }
+  return __any_sync(0xffffffffu, mx);
+}
+
+// P = exp2(s - m) of 32 logits (raw S in v, columns [c, c + 32) of this thread's row) as bf16 pairs
+// into TMEM columns [c/2, c/2 + 16); adds them to the row sum l.
+__device__ __forceinline__ void ws_probs(const uint32_t* v, int c, int mixed, int L, float sl2, float m,
+                                         const float* kb, uint32_t trow, float& l) {
+  uint32_t pk[16];
+  if (!mixed && c + 32 <= L) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float p0 = ex2(fmaf(__uint_as_float(v[2 * i]), sl2, -m));
+      const float p1 = ex2(fmaf(__uint_as_float(v[2 * i + 1]), sl2, -m));
+      l += p0 + p1;
+      pk[i] = pack_bf16(p0, p1);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const float4 b4 = *reinterpret_cast<const float4*>(kb + c + 2 * i);
+      const float p0 = ex2(fmaf(__uint_as_float(v[2 * i]), sl2, b4.x - m));
+      const float p1 = ex2(fmaf(__uint_as_float(v[2 * i + 1]), sl2, b4.y - m));
+      const float p2 = ex2(fmaf(__uint_as_float(v[2 * i + 2]), sl2, b4.z - m));
+      const float p3 = ex2(fmaf(__uint_as_float(v[2 * i + 3]), sl2, b4.w - m));
+      l += (p0 + p1) + (p2 + p3);
+      pk[i] = pack_bf16(p0, p1);
+      pk[i + 1] = pack_bf16(p2, p3);
+    }
+  }
+  st16(trow + (uint32_t)(c >> 1), pk);
+}
+
+// The CTAs walk the windows column-major (window row fastest), so that every CTA's contiguous range
+// holds its share of the bottom window row, whose windows mix mask labels and cost more: in row-
+// major order a few CTAs got only such windows and finished last.  Returns the item index
+// (window * nh + head, the lse layout) of position j of that order.
+__device__ __forceinline__ int64_t ws_item(const AttnGeom& g, int nww, int nwh, int64_t j, int64_t* win, int* h) {
+  const int64_t wq = j / g.nh;
+  *h = (int)(j - wq * g.nh);
+  const int64_t per = (int64_t)nww * nwh;
+  const int64_t b = wq / per, rem = wq - b * per;
+  const int wx = (int)(rem / nwh), wy = (int)(rem - (int64_t)(rem / nwh) * nwh);
+  *win = (b * nwh + wy) * nww + wx;
+  return *win * g.nh + *h;
+}
+
+__global__ void __launch_bounds__(WS_THREADS, 1)
+    fwd_ws_kernel(const __grid_constant__ BoxMaps box_qkv, const float* __restrict__ qw, const float* __restrict__ kw,
+                  __nv_bfloat16* __restrict__ out, float* __restrict__ lse, AttnGeom g, int* err,
+                  long long* __restrict__ stamps) {
+  extern __shared__ unsigned char smem_raw[];
+  SmemWS& S = *reinterpret_cast<SmemWS*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int L = g.T * g.wh * g.ww;
+  const int NK = (L + 15) & ~15;
+  const int ntiles = (L + 127) / 128;
+  const int nww = g.W / g.ww, nwh = g.H / g.wh;
+  const int C = g.nh * HD;
+  const int64_t n_items = (int64_t)g.B * nwh * nww * g.nh;
+  const int64_t i_begin = n_items * blockIdx.x / gridDim.x;
+  const int64_t n_local = n_items * (blockIdx.x + 1) / gridDim.x - i_begin;
+  volatile int* abort = &S.abort;
+  // optional phase timestamps (SM clock) of the first 64 items of the first 16 CTAs; null in
+  // production.  Slot k of item n: stamps[(blockIdx.x * 64 + n) * 16 + k].
+  long long* st = (stamps && blockIdx.x < 16) ? stamps + (int64_t)blockIdx.x * 64 * 16 : nullptr;
+#define WS_STAMP(n_, k_)                                   \
+  do {                                                     \
+    if (st && (n_) < 64) st[(n_) * 16 + (k_)] = clock64(); \
+  } while (0)
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+                 "r"(WS_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < WS_STAGES; ++s) {
+      mb_init(&S.loaded[s], 1);
+      mb_init(&S.normed[s], 4);
+      mb_init(&S.stage_free[s], 5);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mb_init(&S.s_full[w], 1);
+      mb_init(&S.p_ready[w], 4);
+      mb_init(&S.o_full[w], 1);
+      mb_init(&S.o_free[w], 4);
+      mb_init(&S.mma_done[w], 1);
+    }
+    S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // rows [L, 176) of every operand buffer stay zero (the loads write rows < L only)
+  for (int idx = tid; idx < (MAXL - L) * 8; idx += WS_THREADS) {
+    const int r = L + (idx >> 3), c = idx & 7;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int s = 0; s < WS_STAGES; ++s) {
+      *reinterpret_cast<uint4*>(S.q[s] + swz(r, c)) = z;
+      *reinterpret_cast<uint4*>(S.k[s] + swz(r, c)) = z;
+      *reinterpret_cast<uint4*>(S.v[s] + swz(r, c)) = z;
+    }
+  }
+  if (tid < HD) {
+    S.qwv[tid] = qw[tid];
+    S.kwv[tid] = kw[tid];
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    int64_t tab_win[WS_STAGES] = {-1, -1, -1};
+    int64_t issued[WS_STAGES] = {0, 0, 0};
+    for (int64_t n = 0; n < n_local; ++n) {
+      const int s = (int)(n % WS_STAGES);
+      const int64_t use = n / WS_STAGES;
+      if (lane == 0) WS_STAMP(n, 0);
+      if (use > 0 && !ws_wait(&S.stage_free[s], (uint32_t)((use - 1) & 1), err, abort, lane)) break;
+      int64_t win;
+      int h;
+      ws_item(g, nww, nwh, i_begin + n, &win, &h);
+      if (win != tab_win[s]) {
+        const int mx = ws_table(g, win, nww, nwh, L, S.tok[s], S.lab[s], S.wr[s], S.kbias[s], lane);
+        if (lane == 0) S.mixed[s] = mx;
+        tab_win[s] = win;
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) {
+        mb_expect_tx(&S.loaded[s], (uint32_t)(3 * L * ROW_B));
+        const WinLoad wl = win_load(g, win, nww, nwh);
+        load_window(S.q[s], box_qkv, &S.loaded[s], h * HD, wl, g);
+        load_window(S.k[s], box_qkv, &S.loaded[s], C + h * HD, wl, g);
+        load_window(S.v[s], box_qkv, &S.loaded[s], 2 * C + h * HD, wl, g);
+        WS_STAMP(n, 1);
+      }
+      __syncwarp();
+      ++issued[s];
+    }
+    // loads still in flight land before the shared memory is released
+    if (lane == 0)
+      for (int s = 0; s < WS_STAGES; ++s)
+        if (issued[s] > 0) ws_wait1(&S.loaded[s], (uint32_t)((issued[s] - 1) & 1), nullptr, nullptr);
+    __syncwarp();
+  } else if (warp == 1 || warp == 2) {
+    // ---------------------------------------------------------------- MMA issuers
+    const int w = warp - 1;
+    if (lane == 0) {
+      const uint32_t tb = tmem + 256u * (uint32_t)w;
+      const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NK >> 3) << 17) |
+                            ((uint32_t)(128 >> 4) << 24);
+      const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                            ((uint32_t)(128 >> 4) << 24);
+      uint32_t c_s = 0, c_o = 0;
+      bool ok = true;
+      for (int64_t n = w; n < n_local && ok; n += 2) {
+        const int s = (int)(n % WS_STAGES);
+        ok = ws_wait1(&S.normed[s], (uint32_t)((n / WS_STAGES) & 1), err, abort);
+        WS_STAMP(n, 13);
+        for (int t = 0; t < ntiles && ok; ++t) {
+          // S_t overwrites the columns from which the previous O product read P
+          if (c_o > 0) ok = ws_wait1(&S.o_full[w], (c_o - 1) & 1, err, abort);
+          if (!ok) break;
+          fence_after();
+          const int qrow = t == 0 ? 0 : NK - 128;
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks)
+            mma_ss(tb, desc_kmajor(S.q[s] + qrow * ROW_B + ks * 32), desc_kmajor(S.k[s] + ks * 32), id_s, ks > 0);
+          commit(&S.s_full[w]);
+          if (t == 0) WS_STAMP(n, 14);
+          ++c_s;
+          ok = ws_wait1(&S.p_ready[w], (c_s - 1) & 1, err, abort);
+          // the previous O has been drained from its columns
+          if (ok && c_o > 0) ok = ws_wait1(&S.o_free[w], (c_o - 1) & 1, err, abort);
+          if (!ok) break;
+          fence_after();
+          for (int ks = 0; ks < NK / 16; ++ks)
+            mma_ts(tb + WS_O_COL, tb + 8u * (uint32_t)ks, desc_mnmajor(S.v[s] + ks * 16 * ROW_B), id_o, ks > 0);
+          commit(&S.o_full[w]);
+          ++c_o;
+        }
+        WS_STAMP(n, 15);
+        if (ok) commit(&S.stage_free[s]);  // arrives once this item's products have all completed
+      }
+      commit(&S.mma_done[w]);
+      ws_wait1(&S.mma_done[w], 0, nullptr, nullptr);
+    }
+    __syncwarp();
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- QK-RMSNorm
+    const int nt = tid - 128, nw = warp - 4;
+    for (int64_t n = 0; n < n_local; ++n) {
+      const int s = (int)(n % WS_STAGES);
+      if (!ws_wait(&S.loaded[s], (uint32_t)((n / WS_STAGES) & 1), err, abort, lane)) break;
+      if (nt == 0) WS_STAMP(n, 2);
+      float kmax = 0.f;
+      // two threads per row (32 columns each), four partial sums per thread: the squares of x (for
+      // rs) and of x * w (for |qhat| = rs * |x * w|) come from one pass over the row
+      for (int base = 0; base < 4 * L; base += 128) {
+        if (base + (nt & ~31) >= 4 * L) break;  // warp-uniform
+        const int idx = base + nt;
+        const bool act = idx < 4 * L;
+        const int hr = act ? idx >> 1 : 0, half = idx & 1;
+        const bool isq = hr < L;
+        const int r = isq ? hr : hr - L;
+        unsigned char* row = isq ? S.q[s] : S.k[s];
+        const float* wv = (isq ? S.qwv : S.kwv) + 32 * half;
+        float x[4][8];
+        float ss[4] = {0.f, 0.f, 0.f, 0.f}, sw[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(row + swz(r, 4 * half + c)), x[c]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float xw = x[c][i] * wv[8 * c + i];
+            ss[i & 3] = fmaf(x[c][i], x[c][i], ss[i & 3]);
+            sw[i & 3] = fmaf(xw, xw, sw[i & 3]);
+            x[c][i] = xw;
+          }
+        }
+        float ssum = (ss[0] + ss[1]) + (ss[2] + ss[3]);
+        float swsum = (sw[0] + sw[1]) + (sw[2] + sw[3]);
+        ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
+        swsum += __shfl_xor_sync(0xffffffffu, swsum, 1);
+        const float rs = rsqrtf(ssum * (1.f / HD) + FLT_EPSILON);
+        if (act) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[c][i] *= rs;
+            *reinterpret_cast<uint4*>(row + swz(r, 4 * half + c)) = pack8<__nv_bfloat16>(x[c]);
+          }
+          const float nrm = rs * sqrtf(swsum) * 1.01f;  // margin for the bf16 rounding of the operands
+          if (half == 0) {
+            if (isq) S.qn[s][r] = nrm;
+            else kmax = fmaxf(kmax, nrm);
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+      if (lane == 0) S.kn[s][nw] = kmax;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mb_arrive(&S.normed[s]);
+      if (nt == 0) WS_STAMP(n, 3);
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int w = (warp - 8) >> 2;
+    const int lg = warp & 3;
+    const uint32_t tb = tmem + 256u * (uint32_t)w;
+    const uint32_t trow = tb + ((uint32_t)(lg * 32) << 16);
+    const float sl2 = g.scale * kLog2e;
+    uint32_t c_s = 0, c_o = 0;
+    bool ok = true;
+    for (int64_t n = w; n < n_local && ok; n += 2) {
+      const int s = (int)(n % WS_STAGES);
+      int64_t win;
+      int h;
+      const int64_t item = ws_item(g, nww, nwh, i_begin + n, &win, &h);
+      // the stage's tables were written before its loads; visible once its rows are normalised
+      ok = ws_wait(&S.normed[s], (uint32_t)((n / WS_STAGES) & 1), err, abort, lane);
+      if (!ok) break;
+      const bool stamper = lg == 3 && lane == 0;
+      if (stamper) WS_STAMP(n, 4);
+      const int mixed = S.mixed[s];
+      const float kmax = fmaxf(fmaxf(S.kn[s][0], S.kn[s][1]), fmaxf(S.kn[s][2], S.kn[s][3]));
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int qrow = t == 0 ? 0 : NK - 128;
+        const int lo = t * 128;
+        const int r = qrow + lg * 32 + lane;
+        const bool live = r >= lo && r < L;
+        const bool warp_live = qrow + lg * 32 + 31 >= lo && qrow + lg * 32 < L;  // warp-uniform
+        ok = ws_wait(&S.s_full[w], c_s & 1, err, abort, lane);
+        ++c_s;
+        if (!ok) break;
+        if (stamper) WS_STAMP(n, 5 + 4 * t);
+        fence_after();
+        float m = -INFINITY, l = 0.f;
+        if (warp_live) {
+          const int lr = r < L ? S.lab[s][r] : 0;
+          const float* kb = S.kbias[s][lr > 0 ? 1 : 0];
+          const float bound = sl2 * (r < L ? S.qn[s][r] : 0.f) * kmax;
+          if (__all_sync(0xffffffffu, bound <= WS_MAX_BOUND)) {
+            m = bound;
+          } else {
+            // exact row max of the scaled, biased logits (scale > 0: the raw maximum of a chunk
+            // without bias, scaled once at the end)
+            float mraw = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < NK; c += 32) {
+              float v[32];
+              ld32(trow + (uint32_t)c, v);
+              if (!mixed && c + 32 <= L) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, v[i]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                  const float4 b4 = *reinterpret_cast<const float4*>(kb + c + i);
+                  m = fmaxf(m, fmaxf(fmaxf(fmaf(v[i], sl2, b4.x), fmaf(v[i + 1], sl2, b4.y)),
+                                     fmaxf(fmaf(v[i + 2], sl2, b4.z), fmaf(v[i + 3], sl2, b4.w))));
+                }
+              }
+            }
+            m = fmaxf(m, mraw * sl2);
+          }
+          // P = exp2(s - m) as bf16 pairs over the front of S (columns c/2 < c: already read).  The
+          // loop is kept rolled with one TMEM load in flight: unrolled, the four roles' loops no longer
+          // fit the instruction caches (instruction-fetch stalls, 40% slower); with a second register
+          // buffer the softmax warps spill at 128 registers (30% slower).
+#pragma unroll 1
+          for (int c = 0; c < NK; c += 32) {
+            uint32_t v[32];
+            ld32_async(trow + (uint32_t)c, v);
+            ld_wait32(v);
+            ws_probs(v, c, mixed, L, sl2, m, kb, trow, l);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mb_arrive(&S.p_ready[w]);
+        if (stamper) WS_STAMP(n, 6 + 4 * t);
+        // ---- epilogue of tile t: O / rowsum to the token rows; lse per row
+        ok = ws_wait(&S.o_full[w], c_o & 1, err, abort, lane);
+        ++c_o;
+        if (!ok) break;
+        if (stamper) WS_STAMP(n, 7 + 4 * t);
+        fence_after();
+        if (warp_live) {
+          const float il = 1.f / l;
+          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)S.tok[s][live ? r : 0] * g.out_stride + (int64_t)h * HD);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float o[32];
+            ld32(trow + WS_O_COL + 32u * hf, o);
+            if (live) {
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float f8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) f8[i] = o[8 * c + i] * il;
+                dst[4 * hf + c] = pack8<__nv_bfloat16>(f8);
+              }
+            }
+          }
+          if (live) lse[item * L + S.wr[s][r]] = m + __log2f(l);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mb_arrive(&S.o_free[w]);  // the next O product may start
+        if (stamper) WS_STAMP(n, 8 + 4 * t);
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mb_arrive(&S.stage_free[s]);  // this warp is done with the stage's tables
+    }
+    __syncwarp();
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(WS_TMEM_COLS));
+#undef WS_STAMP
+}
+
 }  // namespace attn_tc
 
 bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype) {
@@ -1328,6 +1862,26 @@ cudaError_t window_attn_bwd_tc(const void* qkv, const float* qw, const float* kw
                                              (const __nv_bfloat16*)dout, lse,
                                              (__nv_bfloat16*)dqkv, dqw_part, dkw_part, g, device_error_flag(),
                                              stamps);
+  return cudaGetLastError();
+}
+
+cudaError_t window_attn_fwd_ws(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
+                               const AttnGeom& g, cudaStream_t s, long long* stamps) {
+  if (!(g.scale > 0.f)) return cudaErrorInvalidValue;  // the row max is taken on unscaled logits
+  const size_t smem = sizeof(attn_tc::SmemWS) + 1024;
+  auto k = attn_tc::fwd_ws_kernel;
+  NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int dev = 0, sms = 0;
+  NSW_CUDA_CHECK(cudaGetDevice(&dev));
+  NSW_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t n_tok = (int64_t)g.B * g.T * g.H * g.W;
+  if (n_tok >= (1LL << 31) - 1) return cudaErrorInvalidValue;
+  attn_tc::BoxMaps b_qkv;
+  if (!window_box_maps(&b_qkv, qkv, g, g.qkv_stride)) return cudaErrorInvalidValue;
+  const int64_t items = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww) * g.nh;
+  const int grid = (int)std::min<int64_t>(items, sms);
+  k<<<grid, attn_tc::WS_THREADS, smem, s>>>(b_qkv, qw, kw, (__nv_bfloat16*)out, lse, g, device_error_flag(),
+                                            stamps);
   return cudaGetLastError();
 }
 

@@ -403,7 +403,7 @@ nsw::AttnGeom make_geom(const std::vector<int64_t>& gi, double scale) {
 }
 
 std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vector<int64_t> gi, double scale,
-                                    int64_t impl) {
+                                    int64_t impl, c10::optional<Tensor> stamps) {
   need_cuda(qkv, "qkv");
   auto g = make_geom(gi, scale);
   const int64_t tokens = (int64_t)g.B * g.T * g.H * g.W;
@@ -412,11 +412,18 @@ std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vecto
   const int L = g.T * g.wh * g.ww;
   const int64_t nwin = (int64_t)g.B * (g.H / g.wh) * (g.W / g.ww);
   auto lse = torch::empty({nwin * g.nh * L}, qkv.options().dtype(at::kFloat));
-  // impl: 0 = default (mma.sync: 0.44 ms against 0.66 ms for the persistent tcgen05 kernel at the
-  // production shape), 1 = mma.sync, 2 = tcgen05/TMEM
+  // impl: 0 = default (the warp-specialised tcgen05 kernel where it applies, else mma.sync),
+  // 1 = mma.sync, 2 = persistent tcgen05 (every warp in every phase), 3 = warp-specialised tcgen05.
+  // Measured at 64800 tokens x 16 heads: 0.37 / 0.44 / 0.66 ms for impl 3 / 1 / 2.
   const bool tc_ok = nsw::window_attn_fwd_tc_supported(g, dt_code(qkv));
   TORCH_CHECK(impl != 2 || tc_ok, "window_attn_fwd: tcgen05 path needs bf16, head_dim 64, window <= 176 tokens");
-  if (tc_ok && impl == 2)
+  TORCH_CHECK(impl != 3 || tc_ok, "window_attn_fwd: tcgen05 path needs bf16, head_dim 64, window <= 176 tokens");
+  if (tc_ok && (impl == 3 || impl == 0))
+    check(nsw::window_attn_fwd_ws(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
+                                  lse.data_ptr<float>(), g, stream(),
+                                  stamps ? reinterpret_cast<long long*>(stamps->data_ptr<int64_t>()) : nullptr),
+          "window_attn_fwd_ws");
+  else if (tc_ok && impl == 2)
     check(nsw::window_attn_fwd_tc(qkv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), out.data_ptr(),
                                   lse.data_ptr<float>(), g, stream()),
           "window_attn_fwd_tc");
@@ -490,7 +497,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("segment_sumsq", &segment_sumsq);
   m.def("window_attn_fwd", &window_attn_fwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("geom"),
-        py::arg("scale"), py::arg("impl") = 0);
+        py::arg("scale"), py::arg("impl") = 0, py::arg("stamps") = py::none());
   m.def("window_attn_bwd", &window_attn_bwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("out"),
         py::arg("dout"), py::arg("lse"), py::arg("geom"), py::arg("scale"), py::arg("impl") = 0,
         py::arg("stamps") = py::none());

@@ -73,6 +73,9 @@ cudaError_t window_attn_fwd(const void* qkv, const float* qw, const float* kw, v
 bool window_attn_fwd_tc_supported(const AttnGeom& g, int dtype);
 cudaError_t window_attn_fwd_tc(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
                                const AttnGeom& g, cudaStream_t s);
+// warp-specialised tcgen05 forward (same contract and support as window_attn_fwd_tc)
+cudaError_t window_attn_fwd_ws(const void* qkv, const float* qw, const float* kw, void* out, float* lse,
+                               const AttnGeom& g, cudaStream_t s, long long* stamps = nullptr);
 // RMSNorm, one warp per row with the row in registers (n <= 2048); rmsnorm_fwd/bwd use the TMA
 // version below where it applies and these otherwise
 cudaError_t rmsnorm_fwd_rows(const void* x, const float* w, void* y, float* rstd, int64_t rows, int n,

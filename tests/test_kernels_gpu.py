@@ -336,13 +336,14 @@ def test_window_attention_tcgen05_forward(case, _ext_loaded):
     qw = 1 + 0.1 * torch.randn(hd, device=DEV)
     kw = 1 + 0.1 * torch.randn(hd, device=DEV)
     gi = [B, T, H, W, nh, hd, win[0], win[1], shift[0], shift[1], int(mask), shift[0], 0, H]
-    out_tc, lse_tc = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 2)
     out_mma, lse_mma = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, 1)
-    assert _ext_loaded.read_error_flag(True) == 0
     ref = reference.window_attention(qkv.float(), qw, kw, nh, hd, geom, hd ** -0.5)
-    assert rel(out_tc.view_as(ref), ref) < 2e-2
-    assert rel(out_tc, out_mma) < 1e-2
-    assert torch.allclose(lse_tc, lse_mma, atol=2e-2, rtol=1e-3)
+    for impl in (2, 3):  # persistent tcgen05; warp-specialised tcgen05
+        out_tc, lse_tc = _ext_loaded.window_attn_fwd(qkv.view(-1, 3 * C), qw, kw, gi, hd ** -0.5, impl)
+        assert _ext_loaded.read_error_flag(True) == 0, impl
+        assert rel(out_tc.view_as(ref), ref) < 2e-2, impl
+        assert rel(out_tc, out_mma) < 1e-2, impl
+        assert torch.allclose(lse_tc, lse_mma, atol=2e-2, rtol=1e-3), impl
 
 
 @pytest.mark.parametrize("case", TC_CASES)
