@@ -145,6 +145,24 @@ def bench_attention(a):
         report(f"window_attn_bwd[{tag}] tokens={tokens} heads={nh}", ms, 2.5 * flops, 2 * tokens * 8 * C)
 
 
+def bench_wgrad(a):
+    """Weight-gradient GEMMs of one Swin block (dW = dy^T x, fp32 out) against cuBLAS (torch.mm)."""
+    ext = _ext.require()
+    T, E = a.M, 1024
+    shapes = [("qkv", 3 * E, E), ("proj", E, E), ("fc1", 4 * E, E), ("fc2", E, 4 * E)]
+    for name, m, n in shapes:
+        dy = torch.randn(T, m, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(T, n, device="cuda", dtype=torch.bfloat16)
+        out = torch.zeros(m, n, device="cuda")
+        db = torch.zeros(m, device="cuda")
+        flops = 2.0 * T * m * n
+        ms = timeit(lambda: ext.wgrad(dy, x, out, True, db, True), a.iters)
+        report(f"wgrad[tcgen05 +db] {name} T={T} M={m} N={n} splits={ext.wgrad_plan(m, n, T)}", ms, flops,
+               2 * T * (m + n))
+        ms = timeit(lambda: torch.mm(dy.t(), x, out_dtype=torch.float32), a.iters)
+        report(f"wgrad[cublas] {name} T={T} M={m} N={n}", ms, flops, 2 * T * (m + n))
+
+
 def bench_rmsnorm(a):
     ext = _ext.require()
     x = torch.randn(a.M, a.N, device="cuda", dtype=torch.bfloat16)
@@ -183,7 +201,8 @@ def bench_sse(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "block", "attention", "rmsnorm", "adamw", "sse", "colsum", "all"])
+    ap.add_argument("kernel", choices=["gemm", "block", "attention", "wgrad", "rmsnorm", "adamw", "sse", "colsum",
+                                       "all"])
     ap.add_argument("--M", type=int, default=64800)
     ap.add_argument("--N", type=int, default=3072)
     ap.add_argument("--K", type=int, default=1024)
@@ -209,6 +228,8 @@ def main():
             report(f"col_sum {a.M}x{n}", ms, None, 2 * a.M * n)
     if a.kernel in ("attention", "all"):
         bench_attention(a)
+    if a.kernel in ("wgrad", "all"):
+        bench_wgrad(a)
     if a.kernel in ("rmsnorm", "all"):
         a2 = argparse.Namespace(**vars(a))
         if a.kernel == "all":

@@ -1,3 +1,4 @@
+#include <cstdlib>
 // PyTorch bindings of the sm_100a kernels: argument checks, output allocation and the
 // current CUDA stream; the kernels themselves live in the .cu files (no torch headers).
 #include <ATen/cuda/CUDAContext.h>
@@ -257,6 +258,99 @@ Tensor gelu_bwd(Tensor dy, Tensor u) {
   return du;
 }
 
+// Weight gradient D (+)= dy^T x (fp32 [M, N]) and optionally the bias gradient db (+)= colsum(dy)
+// (fp32 [M]) on the tensor cores.  dy [T, M] and x [T, N] may be column slices (row stride >= width,
+// unit column stride).  `out` / `db` (fp32, contiguous) are written, or accumulated into.
+bool wgrad_supported(const Tensor& dy, const Tensor& x) {
+  if (!dy.is_cuda() || !x.is_cuda() || dy.dim() != 2 || x.dim() != 2 || dy.scalar_type() != x.scalar_type())
+    return false;
+  if (dy.stride(1) != 1 || x.stride(1) != 1 || dy.size(0) != x.size(0)) return false;
+  nsw::WgradArgs a{};
+  a.dy = dy.data_ptr();
+  a.ldy = dy.stride(0);
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.T = dy.size(0);
+  a.M = dy.size(1);
+  a.N = x.size(1);
+  a.D[0] = reinterpret_cast<float*>(16);  // placeholder: only the operands are checked here
+  a.ldd = a.N;
+  a.dtype = dt_code(dy);
+  return nsw::wgrad_tcgen05_supported(a) != 0;
+}
+
+static void check_f32_out(const Tensor& t, int64_t numel, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() == numel &&
+                  (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
+              "wgrad: ", what, " must be a contiguous, 16-byte aligned fp32 tensor of ", numel, " elements");
+}
+
+// dy's M columns form len(outs) equal row segments of dW: segment i (M / len(outs) rows) goes to
+// outs[i] (and its feature sums to dbs[i]).  Returns outs.
+std::vector<Tensor> wgrad_segments(Tensor dy, Tensor x, std::vector<Tensor> outs, bool accumulate,
+                                   c10::optional<std::vector<Tensor>> dbs, bool db_accumulate) {
+  TORCH_CHECK(wgrad_supported(dy, x), "wgrad: unsupported operands (bf16/fp16 [T, M] and [T, N] with unit column "
+                                      "stride, row strides multiples of 8, 16-byte aligned)");
+  const int64_t T = dy.size(0), M = dy.size(1), N = x.size(1);
+  const int nseg = (int)outs.size();
+  TORCH_CHECK(nseg >= 1 && nseg <= 4 && M % nseg == 0, "wgrad: 1 to 4 equal row segments");
+  const int64_t seg = M / nseg;
+  nsw::WgradArgs a{};
+  for (int i = 0; i < nseg; ++i) {
+    check_f32_out(outs[i], seg * N, "out");
+    a.D[i] = outs[i].data_ptr<float>();
+  }
+  if (dbs.has_value()) {
+    TORCH_CHECK((int)dbs->size() == nseg, "wgrad: one db per segment");
+    for (int i = 0; i < nseg; ++i) {
+      check_f32_out((*dbs)[i], seg, "db");
+      a.db[i] = (*dbs)[i].data_ptr<float>();
+    }
+  }
+  a.dy = dy.data_ptr();
+  a.ldy = dy.stride(0);
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.T = T;
+  a.M = M;
+  a.N = N;
+  a.ldd = N;
+  a.seg_rows = seg;
+  a.accumulate = accumulate ? 1 : 0;
+  a.db_accumulate = db_accumulate ? 1 : 0;
+  a.dtype = dt_code(dy);
+  const nsw::WgradPlan plan = nsw::wgrad_plan(M, N, T);
+  Tensor ws;
+  const int64_t wsn = nsw::wgrad_workspace_floats(M, N, plan);
+  if (wsn > 0) {
+    ws = torch::empty({wsn}, dy.options().dtype(at::kFloat));
+    a.ws = ws.data_ptr<float>();
+  }
+  check(nsw::wgrad_tcgen05(a, plan, stream()), "wgrad_tcgen05");
+  return outs;
+}
+
+Tensor wgrad(Tensor dy, Tensor x, c10::optional<Tensor> out, bool accumulate, c10::optional<Tensor> db,
+             bool db_accumulate) {
+  const int64_t M = dy.size(1), N = x.size(1);
+  Tensor D;
+  if (out.has_value() && out->defined()) {
+    D = *out;
+  } else {
+    TORCH_CHECK(!accumulate, "wgrad: accumulate needs out");
+    D = torch::empty({M, N}, dy.options().dtype(at::kFloat));
+  }
+  c10::optional<std::vector<Tensor>> dbs;
+  if (db.has_value() && db->defined()) dbs = std::vector<Tensor>{*db};
+  wgrad_segments(dy, x, {D.view({-1})}, accumulate, dbs, db_accumulate);
+  return D.view({M, N});
+}
+
+std::vector<int64_t> wgrad_plan(int64_t M, int64_t N, int64_t T) {
+  const nsw::WgradPlan p = nsw::wgrad_plan(M, N, T);
+  return {p.splits, p.k1, p.pairs};
+}
+
 Tensor col_sum(Tensor x) {
   need_cuda(x, "x");
   const int n = (int)x.size(-1);
@@ -473,6 +567,12 @@ std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of neural_scaling_weather_b200";
   m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
+  m.def("wgrad_supported", &wgrad_supported, py::arg("dy"), py::arg("x"));
+  m.def("wgrad", &wgrad, py::arg("dy"), py::arg("x"), py::arg("out") = py::none(), py::arg("accumulate") = false,
+        py::arg("db") = py::none(), py::arg("db_accumulate") = false);
+  m.def("wgrad_segments", &wgrad_segments, py::arg("dy"), py::arg("x"), py::arg("outs"), py::arg("accumulate"),
+        py::arg("dbs") = py::none(), py::arg("db_accumulate") = false);
+  m.def("wgrad_plan", &wgrad_plan, py::arg("M"), py::arg("N"), py::arg("T"));
   m.def("error_word", &error_word);
   m.def("set_error_flag", &set_error_flag);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

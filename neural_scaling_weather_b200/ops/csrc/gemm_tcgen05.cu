@@ -1257,6 +1257,503 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// ============================================================================ weight gradient
+// dW[m, n] (+)= sum_t dY[t, m] * X[t, n] and db[m] (+)= sum_t dY[t, m]: the weight (and bias)
+// gradient of a linear layer, whose operands are token-major ([T, M] and [T, N], features
+// contiguous), i.e. MN-major for the MMA.  CTA pair (cta_group::2), 256 x 256 pair tiles, the same
+// warp roles as gemm2_kernel:
+//   both CTAs, warp 0: TMA producer.  A stage of a CTA holds its 128 features of dY and its 128
+//     features of X for 64 tokens, each as two [64 tokens x 64 features] boxes (128-byte swizzle;
+//     the 64-feature blocks are 8 KB apart, the leading byte offset of the MN-major descriptor);
+//   leader, warp 1: issues the MMAs (A and B MN-major in the instruction descriptor) into one TMEM
+//     accumulator of 256 columns; for tiles of the first column block, when db is requested, also
+//     an N = 16 MMA of the same dY stage against a tile of ones (columns 256..271: the feature sums);
+//   both CTAs, warps 2-9: drain their 128 rows.
+// The token range is split S ways (split-K, S chosen on the host so that S x tiles fills the pairs):
+// split-major order, so the pairs running at one time read the same token slab of dY and X from L2.
+// With S > 1 every (tile, split) writes its fp32 partial to a workspace [S][M_pad][N_pad] (and its
+// feature sums to [S][M_pad]) and wgrad_reduce_kernel then sums the S partials in split order
+// (deterministic) into D and db.  (A reduction by the last arriving split inside this kernel kept
+// that pair's single accumulator from being released for microseconds: 25% slower at S = 8.)
+// Bounded mbarrier waits as in the other kernels.
+constexpr int WG_STAGES = 6;
+constexpr int WG_ACC_COLS = 512;  // TMEM of each CTA: [0, 256) dW, [256, 272) feature sums
+
+struct WgradParams {
+  // D (and db) in up to four row segments of seg_rows rows each (the q / k / v weights of one
+  // fused projection are separate gradient buffers): row m goes to D[m / seg_rows] at row m % seg_rows
+  float* D[4];
+  float* db[4];  // all null: no feature sums
+  int64_t seg_rows;
+  int64_t ldd;
+  int accumulate;     // D += result
+  int db_accumulate;  // db += sums
+  int splits;         // partial slots: S of the uniform split, or the remainder pieces of the balanced one
+  int k1;             // 0: uniform split; > 0: balanced (see wg_unit)
+  float* ws;          // partials [splits][M_pad][N_pad], then feature sums [splits][M_pad]
+  int64_t m_pad;      // M rounded up to the pair tile
+  int64_t n_pad;      // N rounded up to the pair tile
+};
+
+// The i-th work unit of pair `pair`: a tile, a k-block range, and where its result goes (slot -1:
+// straight into D; otherwise partial slot `slot`, added into D by wgrad_reduce_kernel).
+//   uniform (k1 == 0): units (split, tile) in split-major order, split s taking k-blocks
+//     [s nkb / S, (s + 1) nkb / S); with S == 1 every unit writes D directly;
+//   balanced (k1 > 0, tiles < pairs): pair t < tiles takes tile t's k-blocks [0, k1) and writes D;
+//     the other pairs share the remainder [k1, nkb) of every tile, cut into `splits` pieces, in
+//     piece-major order.  k1 is chosen on the host so that both kinds of pair finish together, so no
+//     pair idles when there are fewer tiles than pairs, and most of the work still runs with all
+//     pairs at the same k-blocks (reading the same token slab from L2).
+struct WUnit {
+  int64_t tile;
+  int kb0, kb1;
+  int slot;
+};
+__device__ __forceinline__ bool wg_unit(const WgradParams& wp, int64_t tiles, int nkb, int64_t pair, int64_t npairs,
+                                        int64_t i, WUnit& u) {
+  if (wp.k1 == 0) {
+    const int64_t v = pair + i * npairs;
+    if (v >= tiles * wp.splits) return false;
+    const int split = (int)(v / tiles);
+    u.tile = v - (int64_t)split * tiles;
+    u.kb0 = (int)((int64_t)split * nkb / wp.splits);
+    u.kb1 = (int)((int64_t)(split + 1) * nkb / wp.splits);
+    u.slot = wp.splits > 1 ? split : -1;
+    return true;
+  }
+  if (pair < tiles) {
+    if (i > 0) return false;
+    u.tile = pair;
+    u.kb0 = 0;
+    u.kb1 = wp.k1;
+    u.slot = -1;
+    return true;
+  }
+  const int64_t ps = npairs - tiles;
+  const int64_t v = (pair - tiles) + i * ps;
+  if (v >= tiles * wp.splits) return false;
+  const int piece = (int)(v / tiles);
+  const int rem = nkb - wp.k1;
+  u.tile = v - (int64_t)piece * tiles;
+  u.kb0 = wp.k1 + (int)((int64_t)piece * rem / wp.splits);
+  u.kb1 = wp.k1 + (int)((int64_t)(piece + 1) * rem / wp.splits);
+  u.slot = piece;
+  return true;
+}
+
+template <typename T>
+struct SmemW {
+  alignas(1024) T a[WG_STAGES][BM * BK];
+  alignas(1024) T b[WG_STAGES][BM * BK];
+  alignas(1024) T ones[8 * BK];  // this CTA's 8 rows of the N = 16 ones operand (K-major)
+  uint64_t full[WG_STAGES];
+  uint64_t empty[WG_STAGES];
+  uint64_t tmem_full;
+  uint64_t tmem_empty;
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// MN-major, 128-byte swizzle: 64-element rows of one K index, 8-row groups 1024 B apart (SBO), and
+// 64-wide MN blocks `lbo` bytes apart (LBO).
+__device__ __forceinline__ uint64_t smem_desc_mn(const void* p, uint32_t lbo) {
+  const uint32_t a = smem_u32(p);
+  return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// named barrier of the epilogue warps (id 1) that also ANDs a predicate over them, so that a failed
+// wait makes every epilogue warp leave together (none is left at a later barrier)
+__device__ __forceinline__ bool epi_sync_and(bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(out)
+      : "r"(v ? 1u : 0u), "r"(kEpiWarps * 32)
+      : "memory");
+  return out != 0;
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    wgrad2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int64_t M,
+                  int64_t N, int nkb, const __grid_constant__ WgradParams wp, uint32_t idesc, uint32_t idesc_b,
+                  int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto& S = *reinterpret_cast<SmemW<T>*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int64_t m_tiles = (M + BM2 - 1) / BM2;
+  const int64_t n_tiles = (N + BN2 - 1) / BN2;
+  const int64_t tiles = m_tiles * n_tiles;
+  const bool want_db = wp.db[0] != nullptr;
+  volatile int* abort_flag = &S.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WG_STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    mbar_init(&S.tmem_full, 1);
+    mbar_init(&S.tmem_empty, 2 * kEpiWarps);
+    mbar_init(&S.done, 1);
+    S.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  // the ones operand (any layout of all ones is the same tile)
+  {
+    const T one = from_f<T>(1.f);
+    for (int i = threadIdx.x; i < 8 * BK; i += blockDim.x) S.ones[i] = one;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+                 "r"(WG_ACC_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = map_rank(&S.full[0], 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      WUnit un;
+      for (int64_t i = 0; wg_unit(wp, tiles, nkb, pair, npairs, i, un) && !*abort_flag; ++i) {
+        const int64_t tile = un.tile;
+        const int m0 = (int)((tile / n_tiles) * BM2) + (int)rank * BM;
+        const int nb0 = (int)((tile % n_tiles) * BN2) + (int)rank * (BN2 / 2);
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+          if (!mbar_wait(&S.empty[stage], phase ^ 1, abort_flag, err)) break;
+          if (rank == 0) mbar_expect_tx(&S.full[stage], (uint32_t)(2 * 2 * BM * BK * sizeof(T)));
+          const uint32_t fb = full_leader + 8u * stage;
+          tma_load_2d_pair(&S.a[stage][0], &map_a, fb, m0, kb * BK);
+          tma_load_2d_pair(&S.a[stage][64 * BK], &map_a, fb, m0 + 64, kb * BK);
+          tma_load_2d_pair(&S.b[stage][0], &map_b, fb, nb0, kb * BK);
+          tma_load_2d_pair(&S.b[stage][64 * BK], &map_b, fb, nb0 + 64, kb * BK);
+          if (++stage == WG_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      WUnit un;
+      for (int64_t i = 0; wg_unit(wp, tiles, nkb, pair, npairs, i, un) && !*abort_flag; ++i) {
+        const bool sums = want_db && (un.tile % n_tiles) == 0;
+        const int kb0 = un.kb0, kb1 = un.kb1;
+        if (!mbar_wait(&S.tmem_empty, acc_phase ^ 1, abort_flag, err)) break;
+        acc_phase ^= 1;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&S.full[stage], phase, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // (timed against K-major operands in this kernel: the same 0.46 ms at 64800 x 4096 x 1024)
+            const uint64_t da = smem_desc_mn(&S.a[stage][k * 16 * 64], 64 * BK * (uint32_t)sizeof(T));
+            const uint64_t db = smem_desc_mn(&S.b[stage][k * 16 * 64], 64 * BK * (uint32_t)sizeof(T));
+            const uint32_t accf = (kb > kb0 || k > 0) ? 1u : 0u;
+            umma2_f16(tmem_base, da, db, idesc, accf);
+            if (sums) umma2_f16(tmem_base + 256u, da, smem_desc_sw128(&S.ones[k * 16]), idesc_b, accf);
+          }
+          umma2_commit_both(&S.empty[stage]);
+          if (++stage == WG_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma2_commit_both(&S.tmem_full);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;  // columns [128 half, 128 half + 128) of the CTA's 256
+    const uint32_t empty_leader = map_rank(&S.tmem_empty, 0);
+    const bool leader_thread = ew == 0 && lane == 0;
+    uint32_t acc_phase = 0;
+    WUnit un;
+    for (int64_t i = 0; wg_unit(wp, tiles, nkb, pair, npairs, i, un); ++i) {
+      const int64_t tile = un.tile;
+      const bool sums = want_db && (tile % n_tiles) == 0;
+      const int64_t m0 = (tile / n_tiles) * BM2 + (int64_t)rank * BM;
+      const int64_t n0 = (tile % n_tiles) * BN2 + 128 * half;
+      const int64_t row = m0 + q * 32 + lane;
+      const bool row_ok = row < M;
+      const int seg = row_ok ? (int)(row / wp.seg_rows) : 0;
+      const int64_t lrow = row - (int64_t)seg * wp.seg_rows;
+      if (!epi_sync_and(mbar_wait(&S.tmem_full, acc_phase, abort_flag, err))) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16);
+      float sum_v = 0.f;
+      if (un.slot < 0) {
+        // direct: this lane's row, 128 columns, straight to D (and db)
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + (uint32_t)(128 * half + 32 * c), r);
+          const int64_t col = n0 + 32 * c;
+          if (row_ok && col < N) {
+            float* dp = wp.D[seg] + lrow * wp.ldd + col;
+            if (col + 32 <= N && (wp.ldd & 3) == 0) {
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                       __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                if (wp.accumulate) {
+                  const float4 old = reinterpret_cast<const float4*>(dp)[v];
+                  o.x += old.x;
+                  o.y += old.y;
+                  o.z += old.z;
+                  o.w += old.w;
+                }
+                reinterpret_cast<float4*>(dp)[v] = o;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col + j < N) dp[j] = wp.accumulate ? dp[j] + __uint_as_float(r[j]) : __uint_as_float(r[j]);
+            }
+          }
+        }
+        if (sums && half == 0) {
+          uint32_t r[32];
+          tmem_ld32(trow + 256u, r);
+          sum_v = __uint_as_float(r[0]);
+          if (row_ok) {
+            float* bp = wp.db[seg] + lrow;
+            *bp = wp.db_accumulate ? *bp + sum_v : sum_v;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_leader);
+      } else {
+        // split: this CTA's 128 rows of the partial to the workspace (wgrad_reduce_kernel sums them)
+        const int64_t prow_i = m0 + q * 32 + lane;  // < m_pad
+        float* prow = wp.ws + ((int64_t)un.slot * wp.m_pad + prow_i) * wp.n_pad + n0;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + (uint32_t)(128 * half + 32 * c), r);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            __stcg(reinterpret_cast<float4*>(prow + 32 * c) + v,
+                   make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
+                               __uint_as_float(r[4 * v + 3])));
+        }
+        if (sums && half == 0) {
+          uint32_t r[32];
+          tmem_ld32(trow + 256u, r);
+          __stcg(wp.ws + (int64_t)wp.splits * wp.m_pad * wp.n_pad + (int64_t)un.slot * wp.m_pad + prow_i,
+                 __uint_as_float(r[0]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_leader);
+      }
+    }
+  }
+
+  // teardown: both CTAs are past their last unit before the pair's TMEM is released
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(map_rank(&S.done, rank ^ 1u));
+    int never = 0;
+    mbar_wait(&S.done, 0, &never, err);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(WG_ACC_COLS));
+}
+
+// D[m, n] (+)= sum_s ws[s][m][n] in split order; db[m] (+)= sum_s sums[s][m].  One thread per four
+// consecutive columns of a row (scalar at a ragged edge).
+__global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int64_t M, int64_t N,
+                                    const __grid_constant__ WgradParams wp, int accumulate, int db_accumulate) {
+  const int splits = wp.splits;
+  const int64_t m_pad = wp.m_pad, n_pad = wp.n_pad, ldd = wp.ldd;
+  const int64_t n4 = (N + 3) / 4;
+  const int64_t total = M * n4;
+  const int64_t plane = m_pad * n_pad;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n4, c = (i - m * n4) * 4;
+    const int seg = (int)(m / wp.seg_rows);
+    const float* p = ws + m * n_pad + c;
+    float* dp = wp.D[seg] + (m - (int64_t)seg * wp.seg_rows) * ldd + c;
+    if (c + 4 <= N && (ldd & 3) == 0) {
+      float4 acc = __ldcs(reinterpret_cast<const float4*>(p));
+      for (int sp = 1; sp < splits; ++sp) {
+        const float4 x = __ldcs(reinterpret_cast<const float4*>(p + sp * plane));
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+      }
+      if (accumulate) {
+        const float4 old = *reinterpret_cast<const float4*>(dp);
+        acc.x += old.x;
+        acc.y += old.y;
+        acc.z += old.z;
+        acc.w += old.w;
+      }
+      *reinterpret_cast<float4*>(dp) = acc;
+    } else {
+      for (int j = 0; j < 4 && c + j < N; ++j) {
+        float acc = p[j];
+        for (int sp = 1; sp < splits; ++sp) acc += p[sp * plane + j];
+        dp[j] = accumulate ? dp[j] + acc : acc;
+      }
+    }
+  }
+  if (wp.db[0]) {
+    const float* sums = ws + (int64_t)splits * plane;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M; m += (int64_t)gridDim.x * blockDim.x) {
+      float acc = sums[m];
+      for (int sp = 1; sp < splits; ++sp) acc += sums[sp * m_pad + m];
+      const int seg = (int)(m / wp.seg_rows);
+      float* bp = wp.db[seg] + (m - (int64_t)seg * wp.seg_rows);
+      *bp = db_accumulate ? *bp + acc : acc;
+    }
+  }
+}
+
+static int64_t wgrad_units_cost(int64_t tiles, int splits, int nkb, int pairs) {
+  // the busiest pair's k-block steps (about 0.45 us each at the pair's MMA rate), plus, for a split,
+  // the partials (a 256 KB partial per unit written, then read by the reduction: about 0.4 steps per
+  // unit, fitted to 64800-token measurements at S = 1..9) and the reduction launch (about 4 steps)
+  const int64_t units = tiles * splits;
+  const int64_t waves = (units + pairs - 1) / pairs;
+  const int64_t steps = waves * ((nkb + splits - 1) / splits);
+  return steps + (splits > 1 ? (2 * units) / 5 + 4 : 0);
+}
+
+// Balanced schedule for tiles < pairs with the remainder in `s2` pieces: k1 such that a pair of the
+// remainder (ceil(tiles s2 / (pairs - tiles)) pieces of (nkb - k1) / s2 k-blocks) ends with the first
+// part.  Returns k1 (0 if it does not apply) and its cost in k-block steps.
+static int wgrad_balanced(int64_t tiles, int s2, int nkb, int pairs, int64_t* cost) {
+  if (tiles >= pairs || s2 < 1) return 0;
+  const int64_t w2 = (tiles * s2 + (pairs - tiles) - 1) / (pairs - tiles);
+  int k1 = (int)((w2 * nkb + (s2 + w2) - 1) / (s2 + w2));
+  if (k1 >= nkb || k1 < 1) return 0;
+  const int64_t piece = ((int64_t)(nkb - k1) + s2 - 1) / s2;
+  *cost = std::max<int64_t>(k1, w2 * piece) + (2 * tiles * s2) / 5 + 4;
+  return k1;
+}
+
+static int wgrad_pairs(cudaLaunchConfig_t* cfg) {
+  static int max_pairs = 0;
+  if (!max_pairs) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, wgrad2_kernel<__nv_bfloat16>, cfg) != cudaSuccess || n <= 0) n = 1;
+    max_pairs = n;
+  }
+  return max_pairs;
+}
+
+// [T, F] token-major operand as an MN-major TMA source: dims {F, T}, box {64 features, 64 tokens}
+static bool make_map_mn(CUtensorMap* map, const void* ptr, int64_t T, int64_t F, int64_t ld, int dtype) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)F, (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)BK};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+static cudaError_t launch_wgrad(const WgradArgs& a, int pairs_plan, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  if (!make_map_mn(&ma, a.dy, a.T, a.M, a.ldy, a.dtype) || !make_map_mn(&mb, a.x, a.T, a.N, a.ldx, a.dtype))
+    return cudaErrorInvalidValue;
+  const uint32_t fmt = a.dtype == kBF16 ? 1u : 0u;
+  const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 16) |
+                         ((uint32_t)(BN2 >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+  const uint32_t idesc_b = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | ((uint32_t)(16 >> 3) << 17) |
+                           ((uint32_t)(BM2 >> 4) << 24);
+  const size_t smem = sizeof(SmemW<T>) + 1024;
+  auto k = wgrad2_kernel<T>;
+  NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  WgradParams wp;
+  for (int i = 0; i < 4; ++i) {
+    wp.D[i] = a.D[i];
+    wp.db[i] = a.db[i];
+  }
+  wp.seg_rows = a.seg_rows > 0 ? a.seg_rows : a.M;
+  wp.ldd = a.ldd;
+  wp.accumulate = a.accumulate;
+  wp.db_accumulate = a.db_accumulate;
+  wp.splits = a.splits;
+  wp.k1 = a.k1;
+  wp.ws = a.ws;
+  wp.m_pad = (a.M + BM2 - 1) / BM2 * BM2;
+  wp.n_pad = (a.N + BN2 - 1) / BN2 * BN2;
+  const int64_t tiles = ((a.M + BM2 - 1) / BM2) * ((a.N + BN2 - 1) / BN2);
+  const int nkb = (int)((a.T + BK - 1) / BK);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(sm_count() & ~1, 1, 1);
+  int pairs = wgrad_pairs(&cfg);
+  if (a.k1 > 0) {
+    // the balanced schedule was planned for this many pairs
+    if (pairs_plan > pairs || pairs_plan <= tiles) return cudaErrorInvalidValue;
+    pairs = pairs_plan;
+  } else {
+    const int64_t units = tiles * a.splits;
+    if (units < pairs) pairs = (int)units;
+  }
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  NSW_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, ma, mb, a.M, a.N, nkb, wp, idesc, idesc_b, device_error_flag()));
+  NSW_CUDA_CHECK(cudaGetLastError());
+  if (a.splits > 1 || a.k1 > 0) {
+    const int64_t work = a.M * ((a.N + 3) / 4);
+    const int blocks = (int)std::min<int64_t>((work + 255) / 256, 8 * sm_count());
+    // balanced: the direct part already holds D (with the caller's accumulate), the pieces add to it
+    wgrad_reduce_kernel<<<blocks, 256, 0, s>>>(a.ws, a.M, a.N, wp, a.k1 > 0 ? 1 : a.accumulate,
+                                               a.k1 > 0 ? 1 : a.db_accumulate);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace tc
 
 int gemm_tcgen05_supported(const GemmArgs& a) {
@@ -1316,6 +1813,83 @@ cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl) {
   if (rt) return gelu12 ? tc::launch<__half, 256, 3, true, 12>(a, s) : tc::launch<__half, 256, 3, true>(a, s);
   if (gelu12) return tc::launch<__half, 256, 3, false, 12>(a, s);
   return wide ? tc::launch<__half, 256, 4>(a, s) : tc::launch<__half, 128, 6>(a, s);
+}
+
+// ---------------------------------------------------------------------------- weight gradient API
+int wgrad_tcgen05_supported(const WgradArgs& a) {
+  if (a.dtype != kBF16 && a.dtype != kF16) return 0;
+  if (a.T <= 0 || a.M <= 0 || a.N <= 0 || !a.D[0] || a.ldd < a.N) return 0;
+  const int64_t seg = a.seg_rows > 0 ? a.seg_rows : a.M;
+  if ((a.M + seg - 1) / seg > 4) return 0;
+  for (int i = 0; i < (int)((a.M + seg - 1) / seg); ++i)
+    if (!a.D[i] || ((a.db[0] != nullptr) != (a.db[i] != nullptr))) return 0;
+  if (a.ldy % 8 || a.ldx % 8 || a.ldy < a.M || a.ldx < a.N) return 0;  // 16-byte TMA strides
+  if ((reinterpret_cast<uintptr_t>(a.dy) | reinterpret_cast<uintptr_t>(a.x)) & 15) return 0;
+  return tc::get_encode() != nullptr;
+}
+
+WgradPlan wgrad_plan(int64_t M, int64_t N, int64_t T) {
+  const int64_t tiles = ((M + tc::BM2 - 1) / tc::BM2) * ((N + tc::BN2 - 1) / tc::BN2);
+  const int nkb = (int)((T + tc::BK - 1) / tc::BK);
+  int pairs = tc::sm_count() / 2;
+  {
+    const size_t smem = sizeof(tc::SmemW<__nv_bfloat16>) + 1024;
+    if (cudaFuncSetAttribute(tc::wgrad2_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.blockDim = dim3(tc::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cfg.gridDim = dim3(tc::sm_count() & ~1, 1, 1);
+      pairs = tc::wgrad_pairs(&cfg);
+    }
+  }
+  WgradPlan plan;
+  plan.splits = 1;
+  plan.k1 = 0;
+  plan.pairs = pairs;
+  int64_t best_cost = tc::wgrad_units_cost(tiles, 1, nkb, pairs);
+  for (int sp = 2; sp <= 16; ++sp) {
+    if (nkb / sp < 16) break;  // at least 16 k-blocks (1024 tokens) per split
+    const int64_t c = tc::wgrad_units_cost(tiles, sp, nkb, pairs);
+    if (c < best_cost) {
+      best_cost = c;
+      plan.splits = sp;
+    }
+  }
+  for (int s2 = 1; s2 <= 8; ++s2) {
+    int64_t c = 0;
+    const int k1 = tc::wgrad_balanced(tiles, s2, nkb, pairs, &c);
+    if (k1 > 0 && (nkb - k1) / s2 >= 8 && c < best_cost) {
+      best_cost = c;
+      plan.splits = s2;
+      plan.k1 = k1;
+    }
+  }
+  return plan;
+}
+
+int64_t wgrad_workspace_floats(int64_t M, int64_t N, const WgradPlan& plan) {
+  const int splits = plan.splits;
+  if (splits <= 1 && plan.k1 == 0) return 0;
+  const int64_t m_pad = (M + tc::BM2 - 1) / tc::BM2 * tc::BM2, n_pad = (N + tc::BN2 - 1) / tc::BN2 * tc::BN2;
+  return (int64_t)splits * m_pad * (n_pad + 1);
+}
+
+cudaError_t wgrad_tcgen05(const WgradArgs& a_in, const WgradPlan& plan, cudaStream_t s) {
+  if (!wgrad_tcgen05_supported(a_in)) return cudaErrorInvalidValue;
+  WgradArgs a = a_in;
+  a.splits = plan.splits < 1 ? 1 : plan.splits;
+  a.k1 = plan.k1;
+  if ((a.splits > 1 || a.k1 > 0) && !a.ws) return cudaErrorInvalidValue;
+  if (a.dtype == kBF16) return tc::launch_wgrad<__nv_bfloat16>(a, plan.pairs, s);
+  return tc::launch_wgrad<__half>(a, plan.pairs, s);
 }
 
 }  // namespace nsw

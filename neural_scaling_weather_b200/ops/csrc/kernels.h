@@ -125,4 +125,37 @@ struct GemmArgs {
 cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl = 0);
 int gemm_tcgen05_supported(const GemmArgs& a);
 
+// Weight (and bias) gradient of a linear layer on the tensor cores:
+//   D[m, n] (+)= sum_t dy[t, m] * x[t, n]   (fp32),   db[m] (+)= sum_t dy[t, m]   (fp32)
+// dy [T, M] and x [T, N] token-major (features contiguous, leading dimensions ldy / ldx).
+// D and db may be split into up to four row segments of seg_rows rows (separate buffers, e.g. the
+// q / k / v weights of a fused projection); seg_rows = 0 means one segment of M rows.
+struct WgradArgs {
+  const void* dy;
+  int64_t ldy;
+  const void* x;
+  int64_t ldx;
+  int64_t T, M, N;
+  float* D[4];
+  int64_t ldd;
+  int64_t seg_rows;
+  int accumulate;
+  float* db[4];  // db[0] null: no bias gradient
+  int db_accumulate;
+  int dtype;
+  float* ws;   // wgrad_workspace_floats(M, N, plan) floats (none needed when that is 0)
+  int splits;  // set from the plan
+  int k1;      // set from the plan
+};
+// Work schedule: `splits` k-splits (uniform), or with k1 > 0 the balanced schedule (each tile's first
+// k1 k-blocks on a pair of its own, the rest in `splits` pieces on the remaining pairs); `pairs` is
+// the number of CTA pairs it was planned for.
+struct WgradPlan {
+  int splits, k1, pairs;
+};
+WgradPlan wgrad_plan(int64_t M, int64_t N, int64_t T);
+int64_t wgrad_workspace_floats(int64_t M, int64_t N, const WgradPlan& plan);
+int wgrad_tcgen05_supported(const WgradArgs& a);
+cudaError_t wgrad_tcgen05(const WgradArgs& a, const WgradPlan& plan, cudaStream_t s);
+
 }  // namespace nsw

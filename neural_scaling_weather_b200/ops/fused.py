@@ -3,9 +3,11 @@
 Forward GEMMs run on the tcgen05 kernel with their epilogues fused (bias, GELU with the
 pre-activation saved for backward, residual add, broadcast positional-embedding add).
 Backward data-gradient GEMMs also run on the tcgen05 kernel (against a cached
-transposed weight); weight-gradient GEMMs, whose operands are M-major, use cuBLAS with
-fp32 output.  Shapes the tcgen05 kernel cannot take (K or N not a multiple of 8: only
-tiny test models) use cuBLAS plus the fused epilogue kernel.
+transposed weight).  Weight-gradient GEMMs (dW = dy^T x, token-major operands read
+MN-major by TMA) run on the tcgen05 CTA-pair kernel with the bias gradient (the column sums
+of dy) from the same pass, accumulating in fp32 straight into ``param.grad`` where that is
+the optimizer's flat buffer (``gradsink``).  Shapes the tcgen05 kernels cannot take (K or N
+not a multiple of 8: only tiny test models) use cuBLAS plus the fused epilogue kernel.
 """
 
 from __future__ import annotations
@@ -14,6 +16,7 @@ from typing import List, Optional, Sequence
 
 import torch
 
+from . import gradsink
 from . import weights as wcache
 from ._ext import require
 from .geometry import WindowGeometry
@@ -49,8 +52,67 @@ def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, residual=None, res_period:
 
 
 def wgrad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
-    """fp32 ``dy^T @ x`` (cuBLAS; M-major operands)."""
+    """fp32 ``dy^T @ x`` (tcgen05 weight-gradient kernel; cuBLAS for shapes it cannot take)."""
+    ext = require()
+    if ext.wgrad_supported(dy, x):
+        return ext.wgrad(dy, x)
     return torch.mm(dy.t(), x, out_dtype=torch.float32)
+
+
+def weight_grads(dy: torch.Tensor, x: torch.Tensor, ws: Sequence[torch.Tensor], bs: Sequence[torch.Tensor]):
+    """Gradients of weights ``ws`` stacked along the rows of ``dy^T x`` (weight i owns the columns
+    ``[off_i, off_i + rows_i)`` of ``dy``) and of their biases ``bs`` (one per weight, or none).
+
+    dW and db come from one tcgen05 pass (one launch for equally shaped weights, e.g. the q / k / v
+    projections); where ``param.grad`` is the flat fp32 buffer the kernel adds into it and the
+    returned entry is ``None`` (``gradsink``).  Returns (grads_w, grads_b) in the order of ``ws``/``bs``.
+    """
+    ext = require()
+    with_b = len(bs) == len(ws)
+    rows = [w.shape[0] for w in ws]
+    total = sum(rows)
+    dy_all = dy[:, :total]
+    if len(ws) <= 4 and len(set(rows)) == 1 and ext.wgrad_supported(dy_all, x):
+        n, K = rows[0], x.shape[1]
+        tws = [gradsink.target(w) for w in ws]
+        tbs = [gradsink.target(b) for b in bs] if with_b else []
+        acc = any(t is not None for t in tws)
+        outs = [t.view(-1) if t is not None else
+                (torch.zeros if acc else torch.empty)(n * K, dtype=torch.float32, device=dy.device) for t in tws]
+        dbs = None
+        db_acc = False
+        if with_b:
+            db_acc = any(t is not None for t in tbs)
+            dbs = [t if t is not None else (torch.zeros if db_acc else torch.empty)(n, dtype=torch.float32,
+                                                                                   device=dy.device) for t in tbs]
+        ext.wgrad_segments(dy_all, x, outs, acc, dbs, db_acc)
+        gw = [None if t is not None else o.view(w.shape) for t, o, w in zip(tws, outs, ws)]
+        gb: List[Optional[torch.Tensor]] = []
+        if with_b:
+            gb = [None if t is not None else d.to(b.dtype) for t, d, b in zip(tbs, dbs, bs)]
+        for w, t in zip(ws, tws):
+            gradsink.done(w, t is not None)
+        for b, t in zip(bs if with_b else [], tbs):
+            gradsink.done(b, t is not None)
+    else:
+        gw, gb = [], []
+        off = 0
+        for i, w in enumerate(ws):
+            dyi = dy[:, off:off + rows[i]]
+            off += rows[i]
+            gw.append(wgrad(dyi, x).view(w.shape))
+            if with_b:
+                gb.append(ext.col_sum(dyi.contiguous()).to(bs[i].dtype))
+        for p in list(ws) + (list(bs) if with_b else []):
+            gradsink.done(p, False)
+    if not with_b and len(bs):  # one bias over all rows
+        gb = [ext.col_sum(dy.contiguous()).to(bs[0].dtype)]
+        gradsink.done(bs[0], False)
+    return gw, gb
+
+
+def _grad_out(g: Optional[torch.Tensor], p: torch.Tensor) -> Optional[torch.Tensor]:
+    return None if g is None else g.to(p.dtype)
 
 
 # ---------------------------------------------------------------------------- RMSNorm
@@ -138,6 +200,9 @@ class _Linear(torch.autograd.Function):
         y = gemm(x2, W, b, res2, 0, act, pre)
         ctx.save_for_backward(x2, pre)
         ctx.params = ws
+        ctx.bparams = list(bs)
+        if any(ctx.needs_input_grad[5:]):
+            gradsink.use(list(ws) + list(bs))
         ctx.W = W
         ctx.act, ctx.nw, ctx.nb = act, nw, nb
         ctx.shapes = [w.shape for w in ws]
@@ -155,25 +220,16 @@ class _Linear(torch.autograd.Function):
         N = W.shape[0]
         dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
         du = ext.gelu_bwd(dy2, pre) if ctx.act else dy2
-        # bias gradient first: the rows of du written last are still in L2
-        db = ext.col_sum(du) if ctx.nb else None
         dx = None
         if ctx.needs_input_grad[0]:
             Wt = _weight_t(ctx.params, W)
             dx = gemm(du, Wt).view(ctx.x_shape).to(ctx.x_dtype)
-        dW = wgrad(du, x2)
-        grads_w: List[torch.Tensor] = []
-        off = 0
-        for shp in ctx.shapes:
-            n = shp[0]
-            grads_w.append(dW[off:off + n].reshape(shp))
-            off += n
-        grads_b: List[torch.Tensor] = []
-        if ctx.nb:
-            off = 0
-            for n in ctx.bsizes:
-                grads_b.append(db[off:off + n])
-                off += n
+        grads_w: List[Optional[torch.Tensor]] = [None] * ctx.nw
+        grads_b: List[Optional[torch.Tensor]] = [None] * ctx.nb
+        if any(ctx.needs_input_grad[5:]):
+            gw, gb = weight_grads(du, x2, ctx.params, ctx.bparams)
+            grads_w = [None if g is None else g.reshape(shp) for g, shp in zip(gw, ctx.shapes)]
+            grads_b = gb
         dres = dy.to(ctx.res_dtype) if ctx.has_res else None
         return (dx, dres, None, None, None, *grads_w, *grads_b)
 
@@ -224,6 +280,9 @@ class _MLP(torch.autograd.Function):
         y = gemm(h, W2, b2.detach().float(), res2)
         ctx.save_for_backward(x2, u, h)
         ctx.w1, ctx.w2, ctx.W1, ctx.W2 = w1, w2, W1, W2
+        ctx.b1, ctx.b2 = b1, b2
+        if any(ctx.needs_input_grad[2:]):
+            gradsink.use([w1, b1, w2, b2])
         ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
         ctx.res_dtype = residual.dtype if residual is not None else None
         return y.view(*x.shape[:-1], N)
@@ -234,8 +293,7 @@ class _MLP(torch.autograd.Function):
         x2, u, h = ctx.saved_tensors
         N = ctx.W2.shape[0]
         dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
-        db2 = ext.col_sum(dy2)  # before the GEMMs: the rows of dy written last are still in L2
-        dW2 = wgrad(dy2, h)
+        (dW2,), (db2,) = weight_grads(dy2, h, [ctx.w2], [ctx.b2])
         W2t = _weight_t([ctx.w2], ctx.W2)
         if ctx.aux_is_grad:
             if ext.gemm_supported(dy2, W2t, False):
@@ -246,14 +304,13 @@ class _MLP(torch.autograd.Function):
             du = ext.gemm(dy2, W2t, None, u, 0, 2)  # epilogue: * GELU'(u)
         else:
             du = ext.gelu_bwd(gemm(dy2, W2t).contiguous(), u)
-        db1 = ext.col_sum(du)
-        dW1 = wgrad(du, x2)
+        (dW1,), (db1,) = weight_grads(du, x2, [ctx.w1], [ctx.b1])
         dx = None
         if ctx.needs_input_grad[0]:
             W1t = _weight_t([ctx.w1], ctx.W1)
             dx = gemm(du, W1t).view(ctx.x_shape).to(ctx.x_dtype)
         dres = dy.to(ctx.res_dtype) if ctx.res_dtype is not None else None
-        return dx, dres, dW1, db1, dW2, db2
+        return dx, dres, _grad_out(dW1, ctx.w1), db1, _grad_out(dW2, ctx.w2), db2
 
 
 # Which tensor the fc1 forward saves for the backward.  True: GELU'(u), formed from the same
@@ -321,6 +378,9 @@ class _PatchEmbed(torch.autograd.Function):
         y = gemm(cols, W2, b.detach().float() if b is not None else None, res, period)
         ctx.save_for_backward(cols)
         ctx.w_param, ctx.W2 = w, W2
+        ctx.b_param = b
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            gradsink.use([w] + ([b] if b is not None else []))
         ctx.meta = (N, C, H, Wd, p, h, wn, E, x.dtype, add is not None,
                     add.dtype if add is not None else None, period)
         ctx.has_b = b is not None
@@ -332,8 +392,9 @@ class _PatchEmbed(torch.autograd.Function):
         (cols,) = ctx.saved_tensors
         N, C, H, Wd, p, h, wn, E, xdt, has_add, add_dt, period = ctx.meta
         dy2 = dy.reshape(-1, E).to(cols.dtype).contiguous()
-        db = ext.col_sum(dy2) if ctx.has_b else None
-        dW = wgrad(dy2, cols).view(ctx.w_param.shape)
+        gw, gb = weight_grads(dy2, cols, [ctx.w_param], [ctx.b_param] if ctx.has_b else [])
+        dW = None if gw[0] is None else gw[0].view(ctx.w_param.shape).to(ctx.w_param.dtype)
+        db = gb[0] if ctx.has_b else None
         dadd = None
         if has_add:
             dadd = dy2.float().view(-1, period, E).sum(0).view(-1, h, wn, E).to(add_dt)
@@ -363,6 +424,8 @@ class _Head(torch.autograd.Function):
         ctx.save_for_backward(x2)
         ctx.w_param, ctx.W = w, W
         ctx.meta = (B, T, h, wn, E, p, C, x.dtype)
+        if ctx.needs_input_grad[1]:
+            gradsink.use([w])
         return out
 
     @staticmethod
@@ -371,7 +434,8 @@ class _Head(torch.autograd.Function):
         (x2,) = ctx.saved_tensors
         B, T, h, wn, E, p, C, xdt = ctx.meta
         dy2 = ext.patchify(dout.to(x2.dtype).contiguous(), h, wn, p, C)
-        dW = wgrad(dy2, x2)
+        (gw,), _ = weight_grads(dy2, x2, [ctx.w_param], [])
+        dW = _grad_out(gw, ctx.w_param)
         dx = None
         if ctx.needs_input_grad[0]:
             Wt = _weight_t([ctx.w_param], ctx.W)
@@ -440,7 +504,10 @@ class _LinearAllReduce(torch.autograd.Function):
         y = ext.gemm_allreduce(x2, W, bias, res2, bufs.part_ptrs, bufs.flag_ptrs, bufs.rank)
         ctx.save_for_backward(x2)
         ctx.w, ctx.W = w, W
+        ctx.b = b
         ctx.has_b = b is not None
+        if ctx.needs_input_grad[3] or ctx.needs_input_grad[4]:
+            gradsink.use([w] + ([b] if b is not None else []))
         ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
         ctx.res_dtype = residual.dtype if residual is not None else None
         return y.view(*x.shape[:-1], N)
@@ -453,8 +520,9 @@ class _LinearAllReduce(torch.autograd.Function):
         N = W.shape[0]
         dy2 = dy.reshape(-1, N).to(x2.dtype).contiguous()
         dx = gemm(dy2, _weight_t([ctx.w], W)).view(ctx.x_shape).to(ctx.x_dtype) if ctx.needs_input_grad[0] else None
-        db = ext.col_sum(dy2) if ctx.has_b else None
-        dW = wgrad(dy2, x2).reshape(ctx.w.shape)
+        gw, gb = weight_grads(dy2, x2, [ctx.w], [ctx.b] if ctx.has_b else [])
+        dW = None if gw[0] is None else gw[0].reshape(ctx.w.shape).to(ctx.w.dtype)
+        db = gb[0] if ctx.has_b else None
         dres = dy.to(ctx.res_dtype) if ctx.res_dtype is not None else None
         return dx, dres, None, dW, db
 

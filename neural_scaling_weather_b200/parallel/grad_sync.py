@@ -12,7 +12,8 @@ sorts the parameters by that product group, lays their gradients out contiguousl
 the optimizer's flat fp32 gradient buffer (``.grad`` are views, like DDP's
 ``gradient_as_bucket_view``), cuts each group's range into buckets, and launches one
 asynchronous all-reduce per bucket as soon as backward has produced every gradient in it
-(post-accumulate-grad hooks), so communication overlaps the rest of backward.  The
+(post-accumulate-grad hooks, and ``ops.gradsink`` for gradients the weight-gradient kernel
+writes in place), so communication overlaps the rest of backward.  The
 ``1/dp`` factor is applied to the bucket before the sum.  ``no_sync()`` skips the
 reduction on gradient-accumulation micro-batches, as DDP's does.
 """
@@ -97,6 +98,11 @@ class GradReducer:
         if self.enabled:
             for p in space.params:
                 self._hooks.append(p.register_post_accumulate_grad_hook(self._on_grad))
+            # gradients that the weight-gradient kernel adds into .grad in place bypass autograd's
+            # accumulation (and its hooks); the fused layers report them here instead
+            from ..ops import gradsink
+
+            gradsink.register(self._on_grad)
             if broadcast_from_root and comm.get_size("dp") > 1:
                 dist.broadcast(space.data, src=comm.get_root("dp"), group=comm.get_group("dp"))
 
@@ -112,7 +118,9 @@ class GradReducer:
     def _on_grad(self, p):
         if not self._sync:
             return
-        b = self._param_bucket[id(p)]
+        b = self._param_bucket.get(id(p))
+        if b is None or not any(q is p for q in b.params):  # another model's parameter
+            return
         b.pending -= 1
         if b.pending == 0:
             self._launch(b)

@@ -389,3 +389,69 @@ def test_rms_norm_with_skip_gradients():
     assert rel(y, yr) < 1e-2
     assert rel(x.grad, xr.grad) < 2e-2
     assert rel(w.grad, wr.grad) < 2e-2
+
+
+# --------------------------------------------------------------------------- weight-gradient GEMM
+WGRAD_CASES = [
+    # T, M, N, col_offset (dy a column slice at this offset of a wider tensor), with bias
+    (777, 200, 136, 0, True),       # ragged everywhere, one split
+    (4099, 1024, 1024, 0, True),    # split-K with the last-arriver reduction
+    (8192, 1024, 1024, 1024, True),  # dy a column slice (row stride 3072)
+    (6000, 4096, 264, 0, False),    # ragged N, many m tiles
+]
+
+
+@pytest.mark.parametrize("case", WGRAD_CASES)
+def test_wgrad_matches_fp32(case, _ext_loaded):
+    """dW = dy^T x and db = colsum(dy) on the tcgen05 kernel (MN-major TMA operands, CTA pair,
+    split-K) against fp32 PyTorch; accumulation into a sentinel-guarded output, deterministic reruns."""
+    T, M, N, off, with_bias = case
+    torch.manual_seed(11)
+    width = off + M + (1024 if off else 0)
+    dy_full = torch.randn(T, width, device=DEV).bfloat16()
+    dy = dy_full[:, off:off + M]
+    x = torch.randn(T, N, device=DEV).bfloat16()
+    ref = dy.float().t() @ x.float()
+    ref_b = dy.float().sum(0)
+    pad = 1024
+    buf = torch.full((M * N + 2 * pad,), 12345.0, device=DEV)
+    out = buf[pad:pad + M * N]
+    old = torch.randn(M * N, device=DEV)
+    out.copy_(old)
+    db = torch.randn(M, device=DEV) if with_bias else None
+    db_old = db.clone() if with_bias else None
+    _ext_loaded.wgrad(dy, x, out, True, db, True)
+    torch.cuda.synchronize()
+    assert _ext_loaded.read_error_flag(True) == 0
+    assert torch.all(buf[:pad] == 12345.0) and torch.all(buf[pad + M * N:] == 12345.0)
+    assert rel(out.view(M, N) - old.view(M, N), ref) < 3e-3
+    if with_bias:
+        assert rel(db - db_old, ref_b) < 3e-3
+    # written (not accumulated), twice: bit-identical
+    d1 = _ext_loaded.wgrad(dy, x)
+    d2 = _ext_loaded.wgrad(dy, x)
+    assert rel(d1, ref) < 3e-3
+    assert torch.equal(d1, d2)
+    assert _ext_loaded.read_error_flag(True) == 0
+
+
+def test_wgrad_segments_balanced_schedule(_ext_loaded):
+    """Three equal row segments (a fused q/k/v projection) written to separate buffers in one launch,
+    on shapes whose plan is the balanced schedule (tiles < CTA pairs) and the uniform split."""
+    torch.manual_seed(12)
+    for T, seg, N in ((64800, 1024, 1024), (20000, 512, 768)):
+        dy = torch.randn(T, 3 * seg, device=DEV).bfloat16()
+        x = torch.randn(T, N, device=DEV).bfloat16()
+        ref = dy.float().t() @ x.float()
+        ref_b = dy.float().sum(0)
+        outs = [torch.randn(seg * N, device=DEV) for _ in range(3)]
+        olds = [o.clone() for o in outs]
+        dbs = [torch.randn(seg, device=DEV) for _ in range(3)]
+        db_olds = [d.clone() for d in dbs]
+        _ext_loaded.wgrad_segments(dy, x, outs, True, dbs, True)
+        torch.cuda.synchronize()
+        for i in range(3):
+            assert rel((outs[i] - olds[i]).view(seg, N), ref[i * seg:(i + 1) * seg]) < 3e-3, (T, i)
+            assert rel(dbs[i] - db_olds[i], ref_b[i * seg:(i + 1) * seg]) < 3e-3, (T, i)
+        print(T, seg, N, _ext_loaded.wgrad_plan(3 * seg, N, T))
+    assert _ext_loaded.read_error_flag(True) == 0

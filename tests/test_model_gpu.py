@@ -198,3 +198,50 @@ def test_inference_bf16_matches_fp32_on_gpu(tmp_path):
     assert (b["acc"] - a["acc"]).abs().max().item() < 2e-2
     assert b["ms_per_step"] is not None and b["ms_per_step"] > 0
     assert _ext.require().read_error_flag(True) == 0
+
+
+@pytest.mark.parametrize("nrs", [1, 2])
+def test_weight_grads_written_in_place_match_returned_grads(nrs):
+    """With the optimizer's flat fp32 gradient buffer as .grad, the weight-gradient kernel adds dW / db
+    into it in place (no autograd accumulation); the result equals the gradients autograd receives
+    when .grad starts unset, and the in-place hook (the data-parallel reducer's trigger) runs once per
+    parameter even when a rollout applies the model twice."""
+    from neural_scaling_weather_b200.ops import gradsink
+    from neural_scaling_weather_b200.training.optimizer import FlatParamSpace
+
+    torch.manual_seed(0)
+    H, W, Cc = 32, 64, 5
+    md = create_dummy_metadata(H, W, Cc)
+    cfg = _cfg(embed=128, heads=2, nrs=nrs)
+    a = get_model(cfg, md).cuda()
+    b = get_model(cfg, md).cuda()
+    b.load_state_dict(a.state_dict())
+    space = FlatParamSpace([p for p in b.parameters()])
+
+    class Counter:
+        def __init__(self):
+            self.n = {}
+
+        def hit(self, p):
+            self.n[id(p)] = self.n.get(id(p), 0) + 1
+
+    cnt = Counter()
+    gradsink.register(cnt.hit)
+    x = torch.randn(2, 1, Cc + 3, H, W, device="cuda")
+    y = torch.randn(2, nrs, Cc, H, W, device="cuda")
+    for m in (a, b):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = m(x)
+        ((out.float() - y) ** 2).mean().backward()
+    torch.cuda.synchronize()
+    gradsink.unregister(cnt.hit)
+    ga = dict(a.named_parameters())
+    n_in_place = 0
+    for name, p in b.named_parameters():
+        assert p.grad is not None and p.grad.data_ptr() >= space.grad.data_ptr(), name
+        assert rel(p.grad, ga[name].grad) < 1e-4, name
+        if id(p) in cnt.n:
+            assert cnt.n[id(p)] == 1, name
+            n_in_place += 1
+    assert n_in_place >= 8  # the linear / MLP / patch-embed / head weights and biases
+    assert _ext.require().read_error_flag(True) == 0
