@@ -296,7 +296,7 @@ def kernel_breakdown(fn, path):
     """Per-kernel device time of one call of ``fn`` (profiler run; for analysis only)."""
     from torch.profiler import ProfilerActivity, profile
 
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
         fn()
         torch.cuda.synchronize()
     agg = {}
@@ -319,6 +319,14 @@ def kernel_breakdown(fn, path):
         f.write(f"total device time of one step: {total / 1000:.1f} ms\n")
         for name, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
             f.write(f"{t / 1000:10.2f} ms {100 * t / total:5.1f}% {c:6d}x  {name[:110]}\n")
+        # PyTorch operators that launched device work (attribution of the library kernels above)
+        f.write("\noperators by self device time:\n")
+        try:
+            f.write(prof.key_averages(group_by_input_shape=True).table(sort_by="self_device_time_total",
+                                                                        row_limit=25, max_name_column_width=40,
+                                                                        max_shapes_column_width=80))
+        except Exception as e:  # pragma: no cover
+            f.write(f"(unavailable: {e})\n")
 
 
 # ----------------------------------------------------------------------------- reference arm

@@ -103,7 +103,9 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, doub
                          fused_add ? add->data_ptr() : nullptr),
         "rmsnorm_bwd");
   if (add && !fused_add) dx.add_(*add);
-  return {dx, part.sum(0)};
+  auto dw = torch::empty({(int64_t)n}, x.options().dtype(at::kFloat));
+  check(nsw::sum_rows(part.data_ptr<float>(), 1, parts, n, dw.data_ptr<float>(), stream()), "sum_rows");
+  return {dx, dw};
 }
 
 // ------------------------------------------------------------------------------ GEMM + all-reduce
@@ -558,7 +560,8 @@ std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out
                                dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp, kp, g, dt_code(qkv),
                                stream()),
           "window_attn_bwd");
-  auto sums = part.sum(1);
+  auto sums = torch::empty({2, (int64_t)g.hd}, qkv.options().dtype(at::kFloat));
+  check(nsw::sum_rows(part.data_ptr<float>(), 2, rows, g.hd, sums.data_ptr<float>(), stream()), "sum_rows");
   return {dqkv, sums[0], sums[1]};
 }
 

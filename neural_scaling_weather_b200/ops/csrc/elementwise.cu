@@ -357,6 +357,35 @@ __global__ void col_sum_final_kernel(const float* __restrict__ partial, float* _
   }
 }
 
+// out[b, c] = sum_r part[b, r, c] (deterministic: a fixed split of the rows over 8 thread rows, then
+// the 8 partial sums in order).  Block (32 columns x 8 row groups) per 32 columns of one batch.
+// Used for the per-CTA weight-gradient partial rows of the norm and attention kernels.
+__global__ void sum_rows_kernel(const float* __restrict__ part, int64_t rows, int64_t n, float* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int64_t b = blockIdx.y;
+  const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  const int ry = threadIdx.y;
+  float acc = 0.f;
+  if (c < n) {
+    const float* p = part + b * rows * n + c;
+    for (int64_t r = ry; r < rows; r += 8) acc += p[r * n];
+  }
+  red[ry][threadIdx.x] = acc;
+  __syncthreads();
+  if (ry == 0 && c < n) {
+    float t = red[0][threadIdx.x];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) t += red[k][threadIdx.x];
+    out[b * n + c] = t;
+  }
+}
+
+cudaError_t sum_rows(const float* part, int64_t batches, int64_t rows, int64_t n, float* out, cudaStream_t s) {
+  if (batches <= 0 || n <= 0) return cudaSuccess;
+  sum_rows_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)batches), dim3(32, 8), 0, s>>>(part, rows, n, out);
+  return cudaGetLastError();
+}
+
 cudaError_t col_sum(const void* x, float* out, float* partial, int partial_rows, int64_t rows, int n,
                     int dtype, cudaStream_t s) {
   if (n % 8 == 0 && dtype != kF32) {

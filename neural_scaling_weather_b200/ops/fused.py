@@ -397,7 +397,10 @@ class _PatchEmbed(torch.autograd.Function):
         db = gb[0] if ctx.has_b else None
         dadd = None
         if has_add:
-            dadd = dy2.float().view(-1, period, E).sum(0).view(-1, h, wn, E).to(add_dt)
+            if dy2.shape[0] == period:  # one image per positional-embedding period: no reduction
+                dadd = dy2.view(-1, h, wn, E).to(add_dt)
+            else:
+                dadd = dy2.float().view(-1, period, E).sum(0).view(-1, h, wn, E).to(add_dt)
         dx = None
         if ctx.needs_input_grad[0]:
             Wt = _weight_t([ctx.w_param], ctx.W2)
