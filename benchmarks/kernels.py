@@ -163,6 +163,29 @@ def bench_wgrad(a):
         report(f"wgrad[cublas] {name} T={T} M={m} N={n}", ms, flops, 2 * T * (m + n))
 
 
+def bench_amse(a):
+    """AMSE loss forward + backward on 70 x 720 x 1440 fields (device SHT: rFFT, fp32 Legendre kernels)."""
+    import numpy as np
+
+    from neural_scaling_weather_b200.losses import AMSELoss
+
+    H, W, C = 720, 1440, 70
+    lat = np.linspace(90, -90, H + 1)[:-1]
+    lon = np.arange(W) * 360.0 / W
+    loss_fn = AMSELoss(latitudes=lat, longitudes=lon, sp_shapes=[[H], [W]])
+    x = torch.randn(1, 1, C, H, W, device="cuda", requires_grad=True)
+    y = torch.randn(1, 1, C, H, W, device="cuda")
+
+    def step():
+        loss_fn(x, y).backward()
+
+    ms = timeit(step, a.iters)
+    # Legendre contraction FLOPs (triangular, forward for x and y, adjoint for x) plus the rFFTs
+    L, M, N = H, W // 2 + 1, 2 * C
+    flops = 3 * 2.0 * sum(L - m for m in range(min(M, L))) * H * N
+    report(f"amse fwd+bwd {C}x{H}x{W}", ms, flops, 4 * 3 * C * H * W)
+
+
 def bench_rmsnorm(a):
     ext = _ext.require()
     x = torch.randn(a.M, a.N, device="cuda", dtype=torch.bfloat16)
@@ -201,8 +224,8 @@ def bench_sse(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "block", "attention", "wgrad", "rmsnorm", "adamw", "sse", "colsum",
-                                       "all"])
+    ap.add_argument("kernel", choices=["gemm", "block", "attention", "wgrad", "amse", "rmsnorm", "adamw", "sse",
+                                       "colsum", "all"])
     ap.add_argument("--M", type=int, default=64800)
     ap.add_argument("--N", type=int, default=3072)
     ap.add_argument("--K", type=int, default=1024)
@@ -230,6 +253,8 @@ def main():
         bench_attention(a)
     if a.kernel in ("wgrad", "all"):
         bench_wgrad(a)
+    if a.kernel in ("amse", "all"):
+        bench_amse(a)
     if a.kernel in ("rmsnorm", "all"):
         a2 = argparse.Namespace(**vars(a))
         if a.kernel == "all":

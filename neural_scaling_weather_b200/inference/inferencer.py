@@ -35,7 +35,7 @@ from ..parallel import comm
 from ..parallel.mappings import allgather_forward_split_backward
 from ..training.trainer import experiment_dir
 from ..utils.checkpoint_io import verified_load
-from ..utils.sht import RealSHT, power_spectrum
+from ..utils.sht import DistributedRealSHT, power_spectrum_distributed
 
 
 class Inferencer:
@@ -107,7 +107,9 @@ class Inferencer:
         self.acc = torch.zeros(len(self.ics), self.n_channels, nl, device=self.device)
         self.spectra = {lt: torch.zeros(len(self.ics), 2, self.n_channels, self.n_lat, device=self.device)
                         for lt in self.spectra_times_in_hours}
-        self.sht = RealSHT(self.n_lat, self.n_lon).to(self.device) if self.spectra_times_in_hours else None
+        # spectra from the distributed SHT: no rank gathers the globe
+        self.sht = (DistributedRealSHT(self.n_lat, self.n_lon, md["sp_shapes"][0], md["sp_shapes"][1])
+                    if self.spectra_times_in_hours else None)
         self.model = get_model(cfg, domain_metadata=md).to(self.device)
         comm.all_model_groups_exist(self.model)
         self.preprocessor = get_preprocessor(cfg, self.test_dataset).to(self.device)
@@ -162,10 +164,8 @@ class Inferencer:
                     self.rmse[self.ic_count, :, i] = self.weighted_rmse(pred, targ)[0]
                     self.acc[self.ic_count, :, i] = anomaly_correlation(gen, tgt, self.area_w)[0, 0]
                     if lead in self.spectra_times_in_hours:
-                        pg = self.all_gather_helper(pred)
-                        tg = self.all_gather_helper(targ)
-                        self.spectra[lead][self.ic_count, 0] = power_spectrum(pg, self.sht)[0].float()
-                        self.spectra[lead][self.ic_count, 1] = power_spectrum(tg, self.sht)[0].float()
+                        self.spectra[lead][self.ic_count, 0] = power_spectrum_distributed(pred, self.sht)[0].float()
+                        self.spectra[lead][self.ic_count, 1] = power_spectrum_distributed(targ, self.sht)[0].float()
                     window = torch.roll(window, shifts=-1, dims=1)
                     window[:, -1].copy_(gen[:, 0])
                 if self.device.type == "cuda":

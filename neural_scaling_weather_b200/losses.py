@@ -6,7 +6,7 @@ Reference behaviour (``utils/losses.py``):
   ``[nlat_local, 1]`` and optional channel weights (GraphCast surface weights; pressure
   levels weighted ``0.001 * level``; normalised to mean 1), summed, all-reduced over
   ``sp1-sp2`` together with the pixel count, divided by ``pixels_global * B * T * C``;
-* ``AMSELoss`` (``:143-228``): gathers both fields to the full globe, runs a float64 SHT
+* ``AMSELoss`` (``:143-228``): the same loss on a distributed SHT (no full-globe gather; see the class);
   and sums over degrees ``(|x|_l - |y|_l)^2 + 2 max(|x|_l^2, |y|_l^2) (1 - coh_l)`` with the
   m-sums weighting m >= 1 twice; mean over the leading dims;
 * ``WeightedRMSE`` / ``WeightedMSE`` (``:230-305``) per (b, t, c), sp-reduced.
@@ -33,7 +33,7 @@ from .parallel.mappings import (
     allreduce_forward_identity_backward,
 )
 from .utils.profiler import profile_range
-from .utils.sht import RealSHT
+from .utils.sht import DistributedRealSHT
 
 GRAPHCAST_SFC = {"t2m": 1.0, "u10m": 0.1, "v10m": 0.1, "msl": 0.1, "tcwv": 0.1, "sp": 0.1}
 
@@ -122,6 +122,18 @@ def global_pixel_count(h: int, w: int, device) -> float:
 
 
 class AMSELoss(nn.Module):
+    """Spectral AMSE (reference ``utils/losses.py:143-228``, eq. 6 of its paper): per degree l,
+    ``(|x|_l - |y|_l)^2 + 2 max(|x|_l^2, |y|_l^2) (1 - coh_l)`` with ``|x|_l^2 = sum_m w_m |c_lm|^2``
+    and the coherence ``coh_l = sum_m w_m Re(c^x_lm conj c^y_lm) / (|x|_l |y|_l)``, summed over l and
+    averaged over the remaining dimensions.
+
+    The reference gathers both fields to the full globe on every rank and runs a float64 SHT there.
+    Here the transform is :class:`DistributedRealSHT`: no rank gathers the globe, each ``sp2`` rank
+    computes its own orders m, and the per-degree sums over m are added over ``sp2``; the loss is the
+    same on every rank.  CPU: float64 throughout; CUDA: the SHT in float32 (device kernels), the sums
+    over m in float64.
+    """
+
     @classmethod
     def instantiate_from_cfg(cls, cfg, latitudes, longitudes, sp_shapes):
         return cls(latitudes=latitudes, longitudes=longitudes, sp_shapes=sp_shapes,
@@ -132,28 +144,25 @@ class AMSELoss(nn.Module):
         self.latitudes, self.longitudes = latitudes, longitudes
         self.sp_shapes = sp_shapes
         self.loss_type = loss_type
-        self.sht = RealSHT(len(latitudes), len(longitudes))
-
-    def _gather(self, x):
-        x = allgather_forward_split_backward(x, -1, self.sp_shapes[1], "sp2")
-        return allgather_forward_split_backward(x, -2, self.sp_shapes[0], "sp1")
+        lat_shapes, lon_shapes = (sp_shapes if sp_shapes is not None else ([len(latitudes)], [len(longitudes)]))
+        self.sht = DistributedRealSHT(len(latitudes), len(longitudes), lat_shapes, lon_shapes)
 
     def forward(self, x, y):
-        xg = self._gather(x).to(torch.float64)
-        yg = self._gather(y).to(torch.float64)
         with torch.autocast(x.device.type, enabled=False):
-            xc = self.sht(xg)
-            yc = self.sht(yg)
-        xs = xc.real ** 2 + xc.imag ** 2
-        ys = yc.real ** 2 + yc.imag ** 2
-        xy = xc.real * yc.real + xc.imag * yc.imag
-        xn2 = xs[..., 0] + 2 * xs[..., 1:].sum(-1)
-        yn2 = ys[..., 0] + 2 * ys[..., 1:].sum(-1)
-        coh = xy[..., 0] + 2 * xy[..., 1:].sum(-1)
-        xn, yn = torch.sqrt(xn2), torch.sqrt(yn2)
-        coh = coh / (xn * yn)
-        loss = (xn - yn) ** 2 + 2 * torch.maximum(xn2, yn2) * (1 - coh)
-        return loss.sum(-1).mean()
+            cx = self.sht(x)
+            cy = self.sht(y)
+            wm = self.sht.order_weights(cx.device, torch.float64)
+            xs = (cx[..., 0] ** 2 + cx[..., 1] ** 2).double()
+            ys = (cy[..., 0] ** 2 + cy[..., 1] ** 2).double()
+            xy = (cx[..., 0] * cy[..., 0] + cx[..., 1] * cy[..., 1]).double()
+            sums = torch.stack([(xs * wm).sum(-1), (ys * wm).sum(-1), (xy * wm).sum(-1)])
+            if self.sht.sp2 > 1:
+                sums = allreduce_forward_identity_backward(sums, "sp2")
+            xn2, yn2, coh = sums[0], sums[1], sums[2]
+            xn, yn = torch.sqrt(xn2), torch.sqrt(yn2)
+            coh = coh / (xn * yn)
+            loss = (xn - yn) ** 2 + 2 * torch.maximum(xn2, yn2) * (1 - coh)
+            return loss.sum(-1).mean()
 
 
 class WeightedRMSE(nn.Module):

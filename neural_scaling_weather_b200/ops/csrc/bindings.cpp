@@ -353,6 +353,56 @@ std::vector<int64_t> wgrad_plan(int64_t M, int64_t N, int64_t T) {
   return {p.splits, p.k1, p.pairs};
 }
 
+// ------------------------------------------------------------------------------ SHT (Legendre part)
+// x, w: float64 [K] (this rank's colatitude nodes and quadrature weights); orders m0 .. m0 + m_count - 1;
+// returns (P packed float32 [rows, K], row_off int64 [m_count]).
+std::vector<Tensor> legendre_table(Tensor x, Tensor w, int64_t m0, int64_t m_count, int64_t L, bool csphase) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kDouble && w.scalar_type() == at::kDouble &&
+                  x.is_contiguous() && w.is_contiguous() && x.numel() == w.numel(),
+              "legendre_table: x, w float64 CUDA vectors of equal length");
+  const int64_t K = x.numel();
+  std::vector<int64_t> off(m_count);
+  int64_t rows = 0;
+  for (int64_t i = 0; i < m_count; ++i) {
+    off[i] = rows;
+    rows += std::max<int64_t>(0, L - (m0 + i));
+  }
+  auto row_off = torch::from_blob(off.data(), {m_count}, torch::kInt64).to(x.device());
+  auto P = torch::zeros({std::max<int64_t>(rows, 1), K}, x.options().dtype(at::kFloat));
+  check(nsw::legendre_table(x.data_ptr<double>(), w.data_ptr<double>(), (int)m0, (int)m_count, (int)L, (int)K,
+                            row_off.data_ptr<int64_t>(), P.data_ptr<float>(), csphase ? 1 : 0, stream()),
+        "legendre_table");
+  return {P, row_off};
+}
+
+// F float32 [m_count, K, N] -> C float32 [m_count, L, N]
+Tensor legendre_fwd(Tensor P, Tensor row_off, Tensor F, int64_t m0, int64_t L) {
+  need_cuda(P, "P");
+  need_cuda(F, "F");
+  TORCH_CHECK(F.dim() == 3 && F.scalar_type() == at::kFloat, "legendre_fwd: F float32 [m, K, N]");
+  const int64_t mc = F.size(0), K = F.size(1), N = F.size(2);
+  TORCH_CHECK(row_off.numel() == mc && P.size(1) == K, "legendre_fwd: table shape");
+  auto C = torch::empty({mc, L, N}, F.options());
+  check(nsw::legendre_fwd(P.data_ptr<float>(), row_off.data_ptr<int64_t>(), F.data_ptr<float>(), C.data_ptr<float>(),
+                          (int)m0, (int)mc, (int)L, (int)K, (int)N, stream()),
+        "legendre_fwd");
+  return C;
+}
+
+// dC float32 [m_count, L, N] -> dF float32 [m_count, K, N]
+Tensor legendre_bwd(Tensor P, Tensor row_off, Tensor dC, int64_t m0, int64_t K) {
+  need_cuda(P, "P");
+  need_cuda(dC, "dC");
+  TORCH_CHECK(dC.dim() == 3 && dC.scalar_type() == at::kFloat, "legendre_bwd: dC float32 [m, L, N]");
+  const int64_t mc = dC.size(0), L = dC.size(1), N = dC.size(2);
+  TORCH_CHECK(row_off.numel() == mc && P.size(1) == K, "legendre_bwd: table shape");
+  auto dF = torch::empty({mc, K, N}, dC.options());
+  check(nsw::legendre_bwd(P.data_ptr<float>(), row_off.data_ptr<int64_t>(), dC.data_ptr<float>(),
+                          dF.data_ptr<float>(), (int)m0, (int)mc, (int)L, (int)K, (int)N, stream()),
+        "legendre_bwd");
+  return dF;
+}
+
 Tensor col_sum(Tensor x) {
   need_cuda(x, "x");
   const int n = (int)x.size(-1);
@@ -571,6 +621,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of neural_scaling_weather_b200";
   m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
   m.def("wgrad_supported", &wgrad_supported, py::arg("dy"), py::arg("x"));
+  m.def("legendre_table", &legendre_table);
+  m.def("legendre_fwd", &legendre_fwd);
+  m.def("legendre_bwd", &legendre_bwd);
   m.def("wgrad", &wgrad, py::arg("dy"), py::arg("x"), py::arg("out") = py::none(), py::arg("accumulate") = false,
         py::arg("db") = py::none(), py::arg("db_accumulate") = false);
   m.def("wgrad_segments", &wgrad_segments, py::arg("dy"), py::arg("x"), py::arg("outs"), py::arg("accumulate"),

@@ -160,4 +160,14 @@ int64_t wgrad_workspace_floats(int64_t M, int64_t N, const WgradPlan& plan);
 int wgrad_tcgen05_supported(const WgradArgs& a);
 cudaError_t wgrad_tcgen05(const WgradArgs& a, const WgradPlan& plan, cudaStream_t s);
 
+// Legendre part of the real SHT (sht.cu): table P[m, l, k] = w_k Pbar_l^m(x_k) for orders
+// m0 .. m0 + m_count - 1 (packed: order index mi's rows l = m .. L-1 start at row row_off[mi]),
+// and the batched contractions C[mi, l, :] = sum_k P F[mi, k, :] / dF[mi, k, :] = sum_l P dC[mi, l, :].
+cudaError_t legendre_table(const double* x, const double* w, int m0, int m_count, int L, int K,
+                           const int64_t* row_off, float* P, int csphase, cudaStream_t s);
+cudaError_t legendre_fwd(const float* P, const int64_t* row_off, const float* F, float* C, int m0, int m_count, int L,
+                         int K, int N, cudaStream_t s);
+cudaError_t legendre_bwd(const float* P, const int64_t* row_off, const float* dC, float* dF, int m0, int m_count, int L,
+                         int K, int N, cudaStream_t s);
+
 }  // namespace nsw

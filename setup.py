@@ -20,6 +20,7 @@ SOURCES = [
     os.path.join(CSRC, "gemm_tcgen05.cu"),
     os.path.join(CSRC, "noalloc_rmsnorm.cu"),
     os.path.join(CSRC, "rmsnorm_tma.cu"),
+    os.path.join(CSRC, "sht.cu"),
 ]
 
 NVCC_FLAGS = [

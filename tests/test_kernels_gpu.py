@@ -455,3 +455,45 @@ def test_wgrad_segments_balanced_schedule(_ext_loaded):
             assert rel(dbs[i] - db_olds[i], ref_b[i * seg:(i + 1) * seg]) < 3e-3, (T, i)
         print(T, seg, N, _ext_loaded.wgrad_plan(3 * seg, N, T))
     assert _ext_loaded.read_error_flag(True) == 0
+
+
+# --------------------------------------------------------------------------- SHT / AMSE on the device
+def test_legendre_table_matches_recurrence_oracle(_ext_loaded):
+    import numpy as np
+
+    from neural_scaling_weather_b200.utils.sht import _clenshaw_curtis_fast, legendre_orthonormal
+
+    nlat, m0, mc = 48, 3, 20
+    x, w = _clenshaw_curtis_fast(nlat)
+    P, row_off = _ext_loaded.legendre_table(torch.from_numpy(x).to(DEV), torch.from_numpy(w).to(DEV), m0, mc, nlat,
+                                            True)
+    ref = legendre_orthonormal(m0 + mc, nlat, x) * w[None, None, :]
+    P, row_off = P.cpu().double(), row_off.cpu()
+    for i in range(mc):
+        m = m0 + i
+        rows = P[row_off[i]:row_off[i] + (nlat - m)]
+        assert torch.allclose(rows, torch.from_numpy(ref[m, m:]), rtol=1e-5, atol=1e-7), m
+
+
+@pytest.mark.parametrize("H,W", [(64, 128), (45, 90)])
+def test_amse_cuda_fp32_matches_fp64_oracle(H, W, _ext_loaded):
+    """AMSE through the device SHT (fp32 Legendre kernels, fp64 sums over m) against the float64 CPU
+    oracle: loss within 1e-5 and gradient within 1e-4 relative (the fp32 mode's tested bound)."""
+    import numpy as np
+
+    from neural_scaling_weather_b200.losses import AMSELoss
+
+    lat = np.linspace(90, -90, H + 1)[:-1]
+    lon = np.arange(W) * 360.0 / W
+    torch.manual_seed(3)
+    x = torch.randn(2, 1, 4, H, W, dtype=torch.float64)
+    y = x + 0.3 * torch.randn_like(x)
+    xc = x.clone().requires_grad_()
+    ref = AMSELoss(latitudes=lat, longitudes=lon, sp_shapes=[[H], [W]])(xc, y)
+    ref.backward()
+    xg = x.float().to(DEV).requires_grad_()
+    out = AMSELoss(latitudes=lat, longitudes=lon, sp_shapes=[[H], [W]])(xg, y.float().to(DEV))
+    out.backward()
+    assert abs(out.item() - ref.item()) <= 1e-5 * abs(ref.item()), (out.item(), ref.item())
+    assert rel(xg.grad.cpu().double(), xc.grad) < 1e-4
+    assert _ext_loaded.read_error_flag(True) == 0

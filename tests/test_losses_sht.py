@@ -88,3 +88,96 @@ def test_weighted_loss_manual():
     x, y = torch.randn(1, 1, 2, 4, 5), torch.randn(1, 1, 2, 4, 5)
     v = WeightedLoss(area_weighting=True, weights=aw)(x, y)
     assert v.item() == pytest.approx((((x - y) ** 2) * aw).mean().item(), rel=1e-6)
+
+
+# --------------------------------------------------------------------------- distributed SHT / AMSE
+def test_distributed_sht_on_one_rank_matches_realsht():
+    from neural_scaling_weather_b200.utils.sht import DistributedRealSHT
+
+    torch.manual_seed(1)
+    x = torch.randn(2, 3, 17, 32, dtype=torch.float64)
+    ref = RealSHT(17, 32)(x)
+    c = DistributedRealSHT(17, 32)(x)
+    assert c.shape == (2, 3, 17, 17, 2)
+    assert torch.allclose(c[..., 0], ref.real, atol=1e-12) and torch.allclose(c[..., 1], ref.imag, atol=1e-12)
+
+
+def test_amse_gradient_matches_finite_differences():
+    lat = np.linspace(90, -90, 9)[:-1]
+    lon = np.arange(16) * 360 / 16
+    loss = AMSELoss(latitudes=lat, longitudes=lon, sp_shapes=[[8], [16]], loss_type="amse")
+    torch.manual_seed(2)
+    x = torch.randn(1, 1, 2, 8, 16, dtype=torch.float64, requires_grad=True)
+    y = torch.randn(1, 1, 2, 8, 16, dtype=torch.float64)
+    assert torch.autograd.gradcheck(lambda a: loss(a, y), (x,), eps=1e-6, atol=1e-6, rtol=1e-4)
+
+
+def _amse_worker(rank, world, dp, sp1, sp2):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from neural_scaling_weather_b200.losses import AMSELoss
+    from neural_scaling_weather_b200.parallel import comm
+    from neural_scaling_weather_b200.parallel.helpers import compute_split_shapes, offsets
+
+    comm.init_model_parallel_info(tp=1, sp1=sp1, sp2=sp2, dp=dp)
+    B, T, C, H, W = 4, 2, 3, 16, 32
+    g = torch.Generator().manual_seed(0)
+    pred = torch.randn(B, T, C, H, W, dtype=torch.float64, generator=g)
+    targ = pred + 0.5 * torch.randn(B, T, C, H, W, dtype=torch.float64, generator=g)
+    lat = np.linspace(90, -90, H + 1)[:-1]
+    lon = np.arange(W) * 360.0 / W
+    # single-rank oracle (no sharded shapes: no collectives)
+    p = pred.clone().requires_grad_()
+    ref = AMSELoss(latitudes=lat, longitudes=lon, sp_shapes=[[H], [W]])(p, targ)
+    ref.backward()
+    # sharded: batch over dp, latitudes over sp1, longitudes over sp2
+    hs, ws = compute_split_shapes(H, sp1), compute_split_shapes(W, sp2)
+    r1, r2, rd = comm.get_rank("sp1"), comm.get_rank("sp2"), comm.get_rank("dp")
+    h0, w0, b0 = offsets(hs)[r1], offsets(ws)[r2], rd * (B // dp)
+    sl = (slice(b0, b0 + B // dp), slice(None), slice(None), slice(h0, h0 + hs[r1]), slice(w0, w0 + ws[r2]))
+    pl = pred[sl].clone().requires_grad_()
+    loss = AMSELoss(latitudes=lat, longitudes=lon, sp_shapes=[hs, ws])(pl, targ[sl])
+    loss.backward()
+    v = loss.detach().clone()
+    if dp > 1:
+        dist.all_reduce(v, group=comm.get_group("dp"))
+        v /= dp
+    assert abs(v.item() - ref.item()) <= 1e-10 * abs(ref.item()), (v.item(), ref.item())
+    # the local loss is a mean over the local batch: its gradient is dp times the global one
+    assert torch.allclose(pl.grad / dp, p.grad[sl], rtol=1e-9, atol=1e-14)
+
+
+@pytest.mark.parametrize("dp,sp1,sp2", [(1, 2, 1), (1, 1, 2), (2, 2, 1), (1, 2, 2)])
+def test_amse_sharded_matches_single_rank(dp, sp1, sp2):
+    """As the reference's tests/test_losses.py: AMSE value and gradient with the batch split over dp
+    and the grid over sp1 x sp2 equal the single-rank result (here without any full-globe gather)."""
+    from tests.dist_utils import run
+
+    run(_amse_worker, dp * sp1 * sp2, dp, sp1, sp2)
+
+
+def _spectrum_worker(rank, world, sp1, sp2):
+    import numpy as np
+    import torch
+
+    from neural_scaling_weather_b200.parallel import comm
+    from neural_scaling_weather_b200.parallel.helpers import compute_split_shapes, offsets
+    from neural_scaling_weather_b200.utils.sht import DistributedRealSHT, power_spectrum, power_spectrum_distributed
+
+    comm.init_model_parallel_info(tp=1, sp1=sp1, sp2=sp2, dp=1)
+    H, W = 12, 24
+    x = torch.randn(2, 3, H, W, dtype=torch.float64, generator=torch.Generator().manual_seed(5))
+    ref = power_spectrum(x)
+    hs, ws = compute_split_shapes(H, sp1), compute_split_shapes(W, sp2)
+    r1, r2 = comm.get_rank("sp1"), comm.get_rank("sp2")
+    xl = x[..., offsets(hs)[r1]:offsets(hs)[r1] + hs[r1], offsets(ws)[r2]:offsets(ws)[r2] + ws[r2]]
+    p = power_spectrum_distributed(xl, DistributedRealSHT(H, W, hs, ws))
+    assert torch.allclose(p, ref, rtol=1e-10, atol=1e-14)
+
+
+def test_power_spectrum_sharded_matches_single_rank():
+    from tests.dist_utils import run
+
+    run(_spectrum_worker, 4, 2, 2)
