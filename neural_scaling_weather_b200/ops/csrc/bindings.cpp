@@ -353,6 +353,59 @@ std::vector<int64_t> wgrad_plan(int64_t M, int64_t N, int64_t T) {
   return {p.splits, p.k1, p.pairs};
 }
 
+// ------------------------------------------------------------------------------ data-parallel fused path
+static nsw::DpPeers dp_peers(const std::vector<int64_t>& grad, const std::vector<int64_t>& data,
+                             const std::vector<int64_t>& shadow, const std::vector<int64_t>& flags, int64_t rank,
+                             int64_t slots) {
+  const int world = (int)grad.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && (int)data.size() == world && (int)flags.size() == world &&
+                  (shadow.empty() || (int)shadow.size() == world) && rank >= 0 && rank < world,
+              "dp: 1..8 ranks with one pointer each");
+  nsw::DpPeers pr{};
+  for (int r = 0; r < world; ++r) {
+    pr.grad[r] = reinterpret_cast<float*>(grad[r]);
+    pr.data[r] = reinterpret_cast<float*>(data[r]);
+    pr.shadow[r] = shadow.empty() ? nullptr : reinterpret_cast<void*>(shadow[r]);
+    pr.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+    TORCH_CHECK((grad[r] & 15) == 0 && (data[r] & 15) == 0 && (shadow.empty() || (shadow[r] & 7) == 0),
+                "dp: buffers must be 16-byte aligned");
+  }
+  pr.world = world;
+  pr.rank = (int)rank;
+  pr.slots = (int)slots;
+  return pr;
+}
+
+void dp_reduce(std::vector<int64_t> grad, std::vector<int64_t> data, std::vector<int64_t> shadow,
+               std::vector<int64_t> flags, int64_t rank, int64_t slots, int64_t slot, int64_t epoch, int64_t lo,
+               int64_t hi, double scale) {
+  const auto pr = dp_peers(grad, data, shadow, flags, rank, slots);
+  check(nsw::dp_reduce(pr, (int)slot, (uint32_t)epoch, lo, hi, (float)scale, stream()), "dp_reduce");
+}
+
+void dp_adamw(std::vector<int64_t> grad, std::vector<int64_t> data, std::vector<int64_t> shadow,
+              std::vector<int64_t> flags, int64_t rank, int64_t slots, Tensor rlo, Tensor rhi, Tensor rstart,
+              int64_t total4, Tensor m, Tensor v, int64_t shadow_dtype, Tensor gscale, Tensor skip, double lr,
+              double b1, double b2, double eps, double wd, double bc1, double bc2, bool decoupled) {
+  const auto pr = dp_peers(grad, data, shadow, flags, rank, slots);
+  TORCH_CHECK(rlo.scalar_type() == at::kLong && rhi.scalar_type() == at::kLong && rstart.scalar_type() == at::kLong &&
+                  rlo.is_cuda() && rlo.numel() == rhi.numel() && rlo.numel() == rstart.numel(),
+              "dp_adamw: int64 CUDA range tables");
+  need_cuda(m, "m");
+  need_cuda(v, "v");
+  check(nsw::dp_adamw(pr, rlo.data_ptr<int64_t>(), rhi.data_ptr<int64_t>(), rstart.data_ptr<int64_t>(),
+                      (int)rlo.numel(), total4, m.data_ptr<float>(), v.data_ptr<float>(), (int)shadow_dtype,
+                      gscale.data_ptr<float>(), skip.data_ptr<int>(), (float)lr, (float)b1, (float)b2, (float)eps,
+                      (float)wd, (float)bc1, (float)bc2, decoupled, stream()),
+        "dp_adamw");
+}
+
+void dp_barrier(std::vector<int64_t> grad, std::vector<int64_t> data, std::vector<int64_t> shadow,
+                std::vector<int64_t> flags, int64_t rank, int64_t slots, int64_t slot, int64_t epoch) {
+  const auto pr = dp_peers(grad, data, shadow, flags, rank, slots);
+  check(nsw::dp_barrier(pr, (int)slot, (uint32_t)epoch, stream()), "dp_barrier");
+}
+
 // ------------------------------------------------------------------------------ SHT (Legendre part)
 // x, w: float64 [K] (this rank's colatitude nodes and quadrature weights); orders m0 .. m0 + m_count - 1;
 // returns (P packed float32 [rows, K], row_off int64 [m_count]).
@@ -622,6 +675,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_error_flag", &read_error_flag, py::arg("clear") = true);
   m.def("wgrad_supported", &wgrad_supported, py::arg("dy"), py::arg("x"));
   m.def("legendre_table", &legendre_table);
+  m.def("dp_reduce", &dp_reduce);
+  m.def("dp_adamw", &dp_adamw);
+  m.def("dp_barrier", &dp_barrier);
   m.def("legendre_fwd", &legendre_fwd);
   m.def("legendre_bwd", &legendre_bwd);
   m.def("wgrad", &wgrad, py::arg("dy"), py::arg("x"), py::arg("out") = py::none(), py::arg("accumulate") = false,

@@ -160,6 +160,25 @@ int64_t wgrad_workspace_floats(int64_t M, int64_t N, const WgradPlan& plan);
 int wgrad_tcgen05_supported(const WgradArgs& a);
 cudaError_t wgrad_tcgen05(const WgradArgs& a, const WgradPlan& plan, cudaStream_t s);
 
+// Data-parallel reduction / sharded AdamW over peer memory (dp_fused.cu).  Every rank's buffers:
+// grad / data fp32 flat buffers, shadow 16-bit (or null), flags uint32 [kDpFlagBase + world * slots]
+// (flag word of (rank r, slot) at kDpFlagBase + r * slots + slot in every rank's array).
+constexpr int kDpFlagBase = 16;
+struct DpPeers {
+  float* grad[8];
+  float* data[8];
+  void* shadow[8];
+  uint32_t* flags[8];
+  int world, rank, slots;
+};
+cudaError_t dp_reduce(const DpPeers& pr, int slot, uint32_t epoch, int64_t lo, int64_t hi, float scale,
+                      cudaStream_t s);
+cudaError_t dp_adamw(const DpPeers& pr, const int64_t* rlo, const int64_t* rhi, const int64_t* rstart, int nranges,
+                     int64_t total4, float* m, float* v, int shadow_dtype, const float* gscale, const int* skip,
+                     float lr, float b1, float b2, float eps, float wd, float bc1, float bc2, bool decoupled,
+                     cudaStream_t s);
+cudaError_t dp_barrier(const DpPeers& pr, int slot, uint32_t epoch, cudaStream_t s);
+
 // Legendre part of the real SHT (sht.cu): table P[m, l, k] = w_k Pbar_l^m(x_k) for orders
 // m0 .. m0 + m_count - 1 (packed: order index mi's rows l = m .. L-1 start at row row_off[mi]),
 // and the batched contractions C[mi, l, :] = sum_k P F[mi, k, :] / dF[mi, k, :] = sum_l P dC[mi, l, :].

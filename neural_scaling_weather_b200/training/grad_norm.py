@@ -21,8 +21,12 @@ from ..parallel import comm
 
 
 class ShardedNorm:
-    def __init__(self, space):
+    """``owned``: with the data-parallel sharded step, the element ranges this rank owns; the gradient
+    norm is then summed over those only and all-reduced over dp (every gradient is owned once)."""
+
+    def __init__(self, space, owned=None):
         self.space = space
+        self.owned = owned
         classes: Dict[Tuple[str, ...], int] = {}
         seg_lo, seg_hi, seg_cls = [], [], []
         for i, p in enumerate(space.params):
@@ -46,11 +50,30 @@ class ShardedNorm:
         self.block_lo = torch.tensor(blo, dtype=torch.int64, device=dev)
         self.block_hi = torch.tensor(bhi, dtype=torch.int64, device=dev)
         self.block_cls = torch.tensor(bcls, dtype=torch.int32, device=dev)
+        if owned is not None:
+            self._owned_blocks = self._blocks_over(owned)
 
-    def _class_sums(self, buf: torch.Tensor) -> torch.Tensor:
+    def _blocks_over(self, ranges):
+        """Kernel blocks (lo, hi, class) of the parameter segments restricted to ``ranges``."""
+        blo, bhi, bcls = [], [], []
+        chunk = 1 << 16
+        for lo, hi, c in zip(self._lo, self._hi, self._cls):
+            for a, b in ranges:
+                s, e = max(lo, a), min(hi, b)
+                for x in range(s, e, chunk):
+                    blo.append(x)
+                    bhi.append(min(e, x + chunk))
+                    bcls.append(c)
+        dev = self.space.data.device
+        if not blo:  # nothing owned: one empty block
+            blo, bhi, bcls = [0], [0], [0]
+        return (torch.tensor(blo, dtype=torch.int64, device=dev), torch.tensor(bhi, dtype=torch.int64, device=dev),
+                torch.tensor(bcls, dtype=torch.int32, device=dev))
+
+    def _class_sums(self, buf: torch.Tensor, owned: bool = False) -> torch.Tensor:
         if buf.is_cuda:
-            return _ext.require().segment_sumsq(buf, self.block_lo, self.block_hi, self.block_cls,
-                                                len(self.classes))
+            lo, hi, cls = self._owned_blocks if owned else (self.block_lo, self.block_hi, self.block_cls)
+            return _ext.require().segment_sumsq(buf, lo, hi, cls, len(self.classes))
         out = torch.zeros(len(self.classes), dtype=torch.float32)
         for lo, hi, c in zip(self._lo, self._hi, self._cls):
             out[c] += buf[lo:hi].float().square().sum()
@@ -59,7 +82,10 @@ class ShardedNorm:
     def norm(self, which: str = "grad") -> torch.Tensor:
         """Global L2 norm (device scalar tensor, shape [1])."""
         buf = self.space.grad if which == "grad" else self.space.data
-        sums = self._class_sums(buf)
+        owned = which == "grad" and self.owned is not None and buf.is_cuda
+        sums = self._class_sums(buf, owned)
+        if owned:  # each gradient element is owned by one dp rank
+            dist.all_reduce(sums, group=comm.get_group("dp"))
         total = torch.zeros(1, dtype=torch.float32, device=buf.device)
         for c, groups in enumerate(self.classes):
             s = sums[c:c + 1].clone()

@@ -50,6 +50,16 @@ class FlatParamSpace:
         # segment table for the norm kernel: one class id per element range
         self.class_ids: Optional[torch.Tensor] = None
 
+    def rebind(self, data: torch.Tensor, grad: torch.Tensor, shadow: Optional[torch.Tensor]):
+        """Use these flat buffers (same size; contents already copied) and re-point every
+        parameter's ``.data`` / ``.grad`` at them (e.g. buffers in symmetric memory)."""
+        self.data, self.grad = data, grad
+        if shadow is not None:
+            self.shadow = shadow
+        for p, o in zip(self.params, self.offsets):
+            p.data = self.data[o:o + p.numel()].view(p.shape)
+            p.grad = self.grad[o:o + p.numel()].view(p.shape)
+
     def view(self, buf: torch.Tensor, i: int) -> torch.Tensor:
         p = self.params[i]
         o = self.offsets[i]
@@ -88,6 +98,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self.step_count = 0
         self.grad_scale: Optional[torch.Tensor] = None  # device scalar multiplying grads
         self.found_inf: Optional[torch.Tensor] = None  # device flag (skip step if nonzero)
+        self.dp = None  # FusedDPReducer when the data-parallel step is sharded (enable_dp_sharding)
         self._space_index = {id(p): j for j, p in enumerate(self.space.params)}
         self._publish_shadow()
 
@@ -99,6 +110,31 @@ class FusedAdamW(torch.optim.Optimizer):
 
         for i, p in enumerate(self.space.params):
             wcache.register_shadow(p, self.space.view(self.space.shadow, i))
+
+    def enable_dp_sharding(self, reducer):
+        """Step only this rank's owned slices (``dp_adamw``: the update stores the new parameters into
+        every rank's buffers) and keep the moments zero outside them."""
+        self.dp = reducer
+        dev = self.space.data.device
+        lo = [a for a, _ in reducer.owned]
+        hi = [b for _, b in reducer.owned]
+        starts, acc = [], 0
+        for a, b in reducer.owned:
+            starts.append(acc)
+            acc += (b - a) // 4
+        self._rlo = torch.tensor(lo, dtype=torch.int64, device=dev)
+        self._rhi = torch.tensor(hi, dtype=torch.int64, device=dev)
+        self._rstart = torch.tensor(starts, dtype=torch.int64, device=dev)
+        self._total4 = acc
+        self._zero_unowned()
+        self._publish_shadow()
+
+    def _zero_unowned(self):
+        keep = torch.zeros(self.space.numel, dtype=torch.bool, device=self.space.data.device)
+        for a, b in self.dp.owned:
+            keep[a:b] = True
+        self.exp_avg.masked_fill_(~keep, 0.0)
+        self.exp_avg_sq.masked_fill_(~keep, 0.0)
 
     def zero_grad(self, set_to_none: bool = False):
         self.space.zero_grad()
@@ -114,7 +150,16 @@ class FusedAdamW(torch.optim.Optimizer):
         bc1 = 1.0 - b1 ** t
         bc2 = 1.0 - b2 ** t
         sp = self.space
-        if sp.data.is_cuda:
+        if sp.data.is_cuda and self.dp is not None:
+            ext = _ext.require()
+            scale = self.grad_scale if self.grad_scale is not None else torch.ones(1, device=sp.data.device)
+            skip = self.found_inf if self.found_inf is not None else torch.zeros(1, device=sp.data.device, dtype=torch.int32)
+            shadow_code = 1 if (sp.shadow is not None and sp.shadow.dtype == torch.float16) else 0
+            ext.dp_adamw(*self.dp.peers(), self._rlo, self._rhi, self._rstart, self._total4, self.exp_avg,
+                         self.exp_avg_sq, shadow_code, scale, skip, float(lr), float(b1), float(b2), float(eps),
+                         float(wd), float(bc1), float(bc2), bool(decoupled))
+            self.dp.barrier_after_step()
+        elif sp.data.is_cuda:
             ext = _ext.require()
             scale = self.grad_scale if self.grad_scale is not None else torch.ones(1, device=sp.data.device)
             skip = self.found_inf if self.found_inf is not None else torch.zeros(1, device=sp.data.device, dtype=torch.int32)
@@ -144,16 +189,28 @@ class FusedAdamW(torch.optim.Optimizer):
 
     # --------------------------------------------------------------- state
     def state_dict(self):
+        """torch.optim.AdamW layout.  With the data-parallel sharded step every rank holds the moments of
+        its owned slices only (zero elsewhere): they are summed over dp first, so every rank must call
+        this (the trainer builds the checkpoint dictionary on every rank)."""
         g = dict(self.param_groups[0])
         g["params"] = list(range(len(self._given)))
         state = {}
+        exp_avg, exp_avg_sq = self.exp_avg, self.exp_avg_sq
+        if self.dp is not None and self.step_count > 0:
+            import torch.distributed as dist
+
+            from ..parallel import comm
+
+            exp_avg, exp_avg_sq = exp_avg.clone(), exp_avg_sq.clone()
+            dist.all_reduce(exp_avg, group=comm.get_group("dp"))
+            dist.all_reduce(exp_avg_sq, group=comm.get_group("dp"))
         if self.step_count > 0:
             for i, p in enumerate(self._given):
                 j = self._space_index[id(p)]
                 state[i] = {
                     "step": torch.tensor(float(self.step_count)),
-                    "exp_avg": self.space.view(self.exp_avg, j).detach().clone(),
-                    "exp_avg_sq": self.space.view(self.exp_avg_sq, j).detach().clone(),
+                    "exp_avg": self.space.view(exp_avg, j).detach().clone(),
+                    "exp_avg_sq": self.space.view(exp_avg_sq, j).detach().clone(),
                 }
         return {"state": state, "param_groups": [g]}
 
@@ -169,6 +226,8 @@ class FusedAdamW(torch.optim.Optimizer):
             self.space.view(self.exp_avg_sq, j).copy_(st["exp_avg_sq"])
             steps.append(float(st["step"]))
         self.step_count = int(max(steps)) if steps else 0
+        if self.dp is not None:
+            self._zero_unowned()
 
 
 def set_optimizer(cfg, net, shadow_dtype: Optional[torch.dtype] = None,

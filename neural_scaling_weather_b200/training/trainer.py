@@ -208,11 +208,26 @@ class Trainer:
 
         params = [p for p in model.parameters() if p.requires_grad]
         self.space = FlatParamSpace(order_params(params), shadow_dtype=shadow)
-        reducer = GradReducer(self.space) if dist.is_initialized() else None
+        reducer = None
+        if dist.is_initialized():
+            from ..parallel import dp_fused
+
+            fp16_scaler = self.amp_enabled and self.amp_dtype == torch.float16
+            ok, why = dp_fused.available(self.space, cfg.optimizer.optimizer, fp16_scaler)
+            if ok:
+                reducer = dp_fused.FusedDPReducer(self.space)
+            else:
+                reducer = GradReducer(self.space)
+                if self.log_to_screen and comm.get_size("dp") > 1:
+                    logging.info(f"data-parallel reduction over NCCL ({why})")
         self.model = DataParallel(model, reducer)
         self.optimizer = set_optimizer(cfg, model, shadow_dtype=shadow, space=self.space)
+        owned = None
+        if getattr(reducer, "sharded", False) and isinstance(self.optimizer, FusedAdamW):
+            self.optimizer.enable_dp_sharding(reducer)
+            owned = reducer.owned
         self.scheduler = set_scheduler(cfg, self.optimizer)
-        self.norms = ShardedNorm(self.space)
+        self.norms = ShardedNorm(self.space, owned=owned)
         self.use_cuda_graphs = bool(cfg.train.get("cuda_graphs", False))
         self._graph, self._graph_calls, self._static, self._static_loss = None, 0, None, None
         self._graph_pool, self._graph_stream = None, None

@@ -21,6 +21,7 @@ SOURCES = [
     os.path.join(CSRC, "noalloc_rmsnorm.cu"),
     os.path.join(CSRC, "rmsnorm_tma.cu"),
     os.path.join(CSRC, "sht.cu"),
+    os.path.join(CSRC, "dp_fused.cu"),
 ]
 
 NVCC_FLAGS = [

@@ -46,3 +46,12 @@ def test_fused_gemm_allreduce_two_gpus():
         pytest.skip("needs 2 GPUs")
     r = _torchrun(2, ["tests/mp_fused_tp_worker.py"])
     assert "FUSED_TP_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_fused_dp_matches_nccl_two_gpus():
+    """Data-parallel gradient reduction over peer memory + sharded AdamW that stores the new parameters
+    into every rank, against the NCCL all-reduce and the full AdamW (parameters, norms, losses, moments)."""
+    if NGPU < 2:
+        pytest.skip("needs 2 GPUs")
+    r = _torchrun(2, ["tests/mp_dp_fused_worker.py"])
+    assert "DP_FUSED_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
