@@ -222,10 +222,27 @@ def bench_sse(a):
     report("weighted_sse_bwd 70x720x1440", ms, None, x.numel() * 8)
 
 
+def bench_patch(a):
+    """Patch embedding im2col / col2im and head unpatchify / patchify at 73 (70) x 720 x 1440, patch 4."""
+    ext = _ext.require()
+    x = torch.randn(1, 73, 720, 1440, device="cuda")
+    ms = timeit(lambda: ext.im2col(x, 4, 0), a.iters)
+    report("im2col fp32->bf16 73x720x1440 p4", ms, None, x.numel() * (4 + 2))
+    cols = ext.im2col(x, 4, 0)
+    ms = timeit(lambda: ext.col2im(cols, 1, 73, 720, 1440, 4, 2), a.iters)
+    report("col2im bf16->fp32 73x720x1440 p4", ms, None, x.numel() * (2 + 4))
+    y2 = torch.randn(180 * 360, 16 * 70, device="cuda", dtype=torch.bfloat16)
+    ms = timeit(lambda: ext.unpatchify(y2, 1, 1, 180, 360, 4, 70), a.iters)
+    report("unpatchify bf16 70x720x1440 p4", ms, None, y2.numel() * 4)
+    out = ext.unpatchify(y2, 1, 1, 180, 360, 4, 70)
+    ms = timeit(lambda: ext.patchify(out, 180, 360, 4, 70), a.iters)
+    report("patchify bf16 70x720x1440 p4", ms, None, y2.numel() * 4)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemm", "block", "attention", "wgrad", "amse", "rmsnorm", "adamw", "sse",
-                                       "colsum", "all"])
+                                       "patch", "colsum", "all"])
     ap.add_argument("--M", type=int, default=64800)
     ap.add_argument("--N", type=int, default=3072)
     ap.add_argument("--K", type=int, default=1024)
@@ -255,6 +272,8 @@ def main():
         bench_wgrad(a)
     if a.kernel in ("amse", "all"):
         bench_amse(a)
+    if a.kernel in ("patch", "all"):
+        bench_patch(a)
     if a.kernel in ("rmsnorm", "all"):
         a2 = argparse.Namespace(**vars(a))
         if a.kernel == "all":

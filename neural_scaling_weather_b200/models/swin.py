@@ -110,8 +110,7 @@ class MLP(nn.Module):
         tp = comm.get_size("tp")
         if tp == 1 and not (self.drop > 0 and self.training):
             return ops.mlp(x, self.fc1.weight, self.bias1.bias, self.fc2.weight, self.bias2.bias, residual)
-        x = identity_forward_allreduce_backward(x, "tp")
-        h = ops.linear(x, self.fc1.weight, self.bias1.bias, activation="gelu")
+        h = ops.linear_colparallel(x, self.fc1.weight, self.bias1.bias, activation="gelu", group="tp")
         if self.drop > 0 and self.training:
             h = F.dropout(h, self.drop, True)
         if tp == 1 and not (self.drop > 0 and self.training):
@@ -176,9 +175,8 @@ class Block(nn.Module):
             geom = self.attention_geometry((0, 0))
         else:
             geom = self.attention_geometry(self.shift_size)
-        x = identity_forward_allreduce_backward(x, "tp")
         w_qkv, b_qkv = attn.qkv_params()
-        qkv = ops.linear(x, w_qkv, b_qkv)
+        qkv = ops.linear_colparallel(x, w_qkv, b_qkv, group="tp")
         o = ops.window_attention(qkv, attn.q_norm.weight, attn.k_norm.weight,
                                  attn.num_heads_local, attn.head_dim, geom, attn.scale)
         tp = comm.get_size("tp")

@@ -103,6 +103,23 @@ def linear_allreduce(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch
     return y if residual is None else y + residual
 
 
+def linear_colparallel(x: torch.Tensor, weight: TensorOrParts, bias: Optional[TensorOrParts] = None,
+                       activation: Optional[str] = None, group: str = "tp") -> torch.Tensor:
+    """Column-parallel linear of a replicated input: ``act(x W_local^T + b_local)``, whose input
+    gradient is all-reduced over ``group`` (the reference's ``copy_to_parallel_region`` followed by
+    the linear).  On CUDA with a symmetric-memory group of 2..8 GPUs the all-reduce runs inside the
+    data-gradient GEMM's epilogue over NVLink; otherwise the NCCL mapping wraps the linear."""
+    from ..parallel import comm, symm
+    from ..parallel.mappings import identity_forward_allreduce_backward
+
+    if comm.get_size(group) > 1 and _use_cuda(x) and symm.available(group):
+        from .fused import linear_cuda
+
+        return linear_cuda(x, weight, bias, None, activation, allreduce_group=group)
+    x = identity_forward_allreduce_backward(x, group)
+    return linear(x, weight, bias, activation=activation)
+
+
 def linear(x: torch.Tensor, weight: TensorOrParts, bias: Optional[TensorOrParts] = None,
            residual: Optional[torch.Tensor] = None, activation: Optional[str] = None):
     """``act(x W^T + b) + residual``; ``weight``/``bias`` may be lists concatenated on N."""

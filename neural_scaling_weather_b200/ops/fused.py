@@ -179,8 +179,13 @@ def rms_norm_cuda(x, w, eps=None):
 
 # ---------------------------------------------------------------------------- Linear
 class _Linear(torch.autograd.Function):
+    """``act(x W^T + b) + residual`` with W / b possibly concatenated parts.  With ``ctx.group`` set
+    (a column-parallel linear whose input is replicated over that group) the data gradient is
+    all-reduced over the group inside the dgrad GEMM's epilogue (peer loads over NVLink), which is
+    the reference's ``copy_to_parallel_region`` backward (``distributed/mappings.py:24-46``)."""
+
     @staticmethod
-    def forward(ctx, x, residual, act, nw, nb, *params):
+    def forward(ctx, x, residual, act, nw, nb, group, *params):
         ws, bs = params[:nw], params[nw:nw + nb]
         dt = _cdtype(x)
         K = x.shape[-1]
@@ -201,7 +206,8 @@ class _Linear(torch.autograd.Function):
         ctx.save_for_backward(x2, pre)
         ctx.params = ws
         ctx.bparams = list(bs)
-        if any(ctx.needs_input_grad[5:]):
+        ctx.group = group
+        if any(ctx.needs_input_grad[6:]):
             gradsink.use(list(ws) + list(bs))
         ctx.W = W
         ctx.act, ctx.nw, ctx.nb = act, nw, nb
@@ -223,15 +229,22 @@ class _Linear(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[0]:
             Wt = _weight_t(ctx.params, W)
-            dx = gemm(du, Wt).view(ctx.x_shape).to(ctx.x_dtype)
+            if ctx.group is not None:
+                from ..parallel import symm
+
+                bufs = symm.allreduce_buffers(ctx.group, du.shape[0], Wt.shape[0], du.dtype, du.device)
+                dx = ext.gemm_allreduce(du.contiguous(), Wt, None, None, bufs.part_ptrs, bufs.flag_ptrs, bufs.rank)
+            else:
+                dx = gemm(du, Wt)
+            dx = dx.view(ctx.x_shape).to(ctx.x_dtype)
         grads_w: List[Optional[torch.Tensor]] = [None] * ctx.nw
         grads_b: List[Optional[torch.Tensor]] = [None] * ctx.nb
-        if any(ctx.needs_input_grad[5:]):
+        if any(ctx.needs_input_grad[6:]):
             gw, gb = weight_grads(du, x2, ctx.params, ctx.bparams)
             grads_w = [None if g is None else g.reshape(shp) for g, shp in zip(gw, ctx.shapes)]
             grads_b = gb
         dres = dy.to(ctx.res_dtype) if ctx.has_res else None
-        return (dx, dres, None, None, None, *grads_w, *grads_b)
+        return (dx, dres, None, None, None, None, *grads_w, *grads_b)
 
 
 def _as_list(t):
@@ -242,11 +255,11 @@ def _as_list(t):
     return list(t)
 
 
-def linear_cuda(x, weight, bias=None, residual=None, activation=None):
+def linear_cuda(x, weight, bias=None, residual=None, activation=None, allreduce_group=None):
     ws = _as_list(weight)
     bs = _as_list(bias)
     act = {None: 0, "gelu": 1}[activation]
-    return _Linear.apply(x, residual, act, len(ws), len(bs), *ws, *bs)
+    return _Linear.apply(x, residual, act, len(ws), len(bs), allreduce_group, *ws, *bs)
 
 
 # ---------------------------------------------------------------------------- MLP

@@ -85,6 +85,25 @@ def main():
         if rel(xg.grad, dx_ref) > 2e-2 or rel(w.grad, dw_ref) > 2e-2 or rel(b.grad, dy.sum(0)) > 2e-2:
             print(f"[rank {rank}] backward mismatch {rel(xg.grad, dx_ref)} {rel(w.grad, dw_ref)}", flush=True)
             ok = False
+        # column-parallel linear of a replicated input: the data-gradient all-reduce runs in the
+        # dgrad GEMM's epilogue; against the NCCL composition
+        xr = torch.randn(M, N, device=dev, generator=gs).bfloat16()  # replicated input (K_in = N)
+        wc = torch.nn.Parameter(0.05 * torch.randn(K, N, device=dev, generator=g))  # local column shard
+        bc = torch.nn.Parameter(torch.randn(K, device=dev, generator=g))
+        dyc = torch.randn(M, K, device=dev, generator=g)
+        x1 = xr.detach().float().requires_grad_()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            yc = ops.linear_colparallel(x1, wc, bc, activation="gelu", group="tp")
+        (yc.float() * dyc).sum().backward()
+        x2 = xr.detach().float().requires_grad_()
+        from neural_scaling_weather_b200.parallel.mappings import identity_forward_allreduce_backward
+
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            yr = ops.linear(identity_forward_allreduce_backward(x2, "tp"), wc, bc, activation="gelu")
+        (yr.float() * dyc).sum().backward()
+        if rel(yc, yr) > 1e-3 or rel(x1.grad, x2.grad) > 1e-2:
+            print(f"[rank {rank}] colparallel mismatch {rel(yc, yr)} {rel(x1.grad, x2.grad)}", flush=True)
+            ok = False
     if _ext.require().read_error_flag(True) != 0:
         print(f"[rank {rank}] device error flag set", flush=True)
         ok = False
