@@ -12,6 +12,7 @@ not a multiple of 8: only tiny test models) use cuBLAS plus the fused epilogue k
 
 from __future__ import annotations
 
+import os
 from typing import List, Optional, Sequence
 
 import torch
@@ -344,13 +345,17 @@ def _geom_ints(B, T, H, W, nh, hd, g: WindowGeometry):
             int(g.mask_shift), int(g.row_offset), int(g.h_global if g.h_global else H)]
 
 
+# forward kernel choice (0: default = warp-specialised tcgen05; 1: mma.sync; 2: persistent tcgen05)
+ATTN_FWD_IMPL = int(os.environ.get("NSW_ATTN_FWD_IMPL", "0"))
+
+
 class _WindowAttn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, qw, kw, gi, scale):
         ext = require()
         qkv2 = qkv.contiguous()
         out, lse = ext.window_attn_fwd(qkv2, qw.detach().float().contiguous(),
-                                       kw.detach().float().contiguous(), gi, scale)
+                                       kw.detach().float().contiguous(), gi, scale, ATTN_FWD_IMPL)
         ctx.save_for_backward(qkv2, qw, kw, out, lse)
         ctx.gi, ctx.scale = gi, scale
         return out

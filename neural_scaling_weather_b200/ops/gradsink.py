@@ -4,14 +4,16 @@ The fused linear layers compute dW (and db) on the tensor cores with fp32 accumu
 (``ext.wgrad``).  When a parameter's ``.grad`` is an fp32 contiguous tensor (the optimizer's flat
 gradient buffer keeps every ``.grad`` as such a view), the kernel adds into it directly and the
 autograd function returns ``None`` for that input: no separate gradient tensor, no autograd
-accumulation kernel.  Autograd's post-accumulate-grad hooks do not fire for such a parameter, so
-the data-parallel reducer registers its hook here as well.  A parameter used by several forward
+accumulation kernel.  Autograd's post-accumulate-grad hook of such a parameter still fires (with
+no gradient), after all of its uses; the data-parallel reducer registers its hook here as well and
+counts each parameter once per backward, whichever notice comes first.  A parameter used by several forward
 calls before one backward (a multi-step rollout applies the model several times) is reported once,
 after the last of its backward calls has written its share, as autograd would have done.
 """
 
 from __future__ import annotations
 
+import os
 import weakref
 from typing import Callable, List, Optional
 
@@ -32,9 +34,13 @@ def unregister(cb: Callable[[torch.nn.Parameter], None]) -> None:
     _callbacks[:] = [r for r in _callbacks if r() is not None and r() != cb]
 
 
+_IN_PLACE = os.environ.get("NSW_WGRAD_INPLACE", "1") != "0"
+
+
 def target(p: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
-    """``p.grad`` if the kernel may accumulate into it in place (fp32, contiguous, 16-byte aligned)."""
-    if p is None or not isinstance(p, torch.nn.Parameter) or not p.requires_grad:
+    """``p.grad`` if the kernel may accumulate into it in place (fp32, contiguous, 16-byte aligned).
+    ``NSW_WGRAD_INPLACE=0`` returns every gradient through autograd instead."""
+    if not _IN_PLACE or p is None or not isinstance(p, torch.nn.Parameter) or not p.requires_grad:
         return None
     g = p.grad
     if g is None or g.dtype != torch.float32 or not g.is_contiguous() or g.data_ptr() % 16 != 0:

@@ -27,6 +27,7 @@ multicast touches peer memory.  ``NSW_FUSED_DP=1`` selects this path (default: t
 
 from __future__ import annotations
 
+import importlib
 import os
 from typing import Dict, List, Tuple
 
@@ -34,7 +35,6 @@ import torch
 import torch.distributed as dist
 
 from . import comm
-from .grad_sync import reduction_group_name
 
 FLAG_BASE = 16  # kDpFlagBase of the kernels
 
@@ -54,10 +54,11 @@ def available(space, optimizer_name: str, fp16_scaler: bool) -> Tuple[bool, str]
         return False, "needs all ranks on one node"
     if dist.get_backend(comm.get_group("dp")) != "nccl":
         return False, "needs the NCCL backend"
-    if any(reduction_group_name(p) != "dp" for p in space.params):
+    # with tp = sp1 = sp2 = 1 every product reduction group of a parameter is the dp group
+    if any(comm.get_size(g) != 1 for g in ("tp", "sp1", "sp2")):
         return False, "parameters reduced over other groups"
     try:
-        import torch.distributed._symmetric_memory  # noqa: F401
+        importlib.import_module("torch.distributed._symmetric_memory")
     except ImportError:
         return False, "symmetric memory unavailable"
     return True, ""
@@ -136,6 +137,7 @@ class FusedDPReducer:
         if space.shadow is not None:
             space.refresh_shadow()
         self.stream = torch.cuda.Stream(device=dev)
+        self._seen = set()
         self.epoch = 0
         self._open = False
         self._sync = True
@@ -173,6 +175,12 @@ class FusedDPReducer:
         b = self._param_bucket.get(id(p))
         if b is None or not any(q is p for q in b.params):  # another model's parameter
             return
+        # a parameter is counted once per backward: autograd's post-accumulate hook also fires
+        # (with no gradient) for a parameter whose gradient the kernel wrote in place and reported
+        # through ops.gradsink
+        if id(p) in self._seen:
+            return
+        self._seen.add(id(p))
         b.pending -= 1
         if b.pending == 0:
             self._launch(b)
@@ -196,10 +204,12 @@ class FusedDPReducer:
         torch.cuda.current_stream(self.space.data.device).wait_stream(self.stream)
         for b in self.buckets:
             b.pending = len(b.params)
+        self._seen.clear()
 
     def reset(self):
         for b in self.buckets:
             b.pending = len(b.params)
+        self._seen.clear()
 
     # ------------------------------------------------------------------ optimizer side
     def barrier_after_step(self):

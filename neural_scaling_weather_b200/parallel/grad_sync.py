@@ -94,6 +94,7 @@ class GradReducer:
             self._param_bucket[id(p)] = cur
         for b in self.buckets:
             b.pending = len(b.params)
+        self._seen = set()
         self._hooks = []
         if self.enabled:
             for p in space.params:
@@ -121,6 +122,12 @@ class GradReducer:
         b = self._param_bucket.get(id(p))
         if b is None or not any(q is p for q in b.params):  # another model's parameter
             return
+        # a parameter is counted once per backward: autograd's post-accumulate hook also fires
+        # (with no gradient) for a parameter whose gradient the kernel wrote in place and reported
+        # through ops.gradsink
+        if id(p) in self._seen:
+            return
+        self._seen.add(id(p))
         b.pending -= 1
         if b.pending == 0:
             self._launch(b)
@@ -149,8 +156,10 @@ class GradReducer:
                 b.handle.wait()
                 b.handle = None
             b.pending = len(b.params)
+        self._seen.clear()
 
     def reset(self):
         for b in self.buckets:
             b.pending = len(b.params)
             b.handle = None
+        self._seen.clear()
