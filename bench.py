@@ -37,6 +37,18 @@ N_CH = 70
 N_INV = 3
 GLOBAL_BATCH = 16
 
+# the benchmark configurations (model, parallel layout, batch, loss, training rollout steps); "dp" is
+# the headline one, the others are the hybrid, large-model and autoregressive-inference setups
+CONFIGS = {
+    "dp": dict(model=MODEL, tp=1, sp1=1, sp2=1, global_batch=16, loss="mse", rollout=1, name="swin-p4-e1024-d16"),
+    "hybrid": dict(model=MODEL, tp=2, sp1=1, sp2=2, global_batch=8, loss="mse", rollout=1,
+                   name="swin-p4-e1024-d16"),
+    "large": dict(model=dict(embed_dim=2048, depth=24, num_heads=32, patch_size=4, window_size=[9, 18], mlp_ratio=4),
+                  tp=4, sp1=1, sp2=2, global_batch=4, loss="amse", rollout=2, name="swin-p4-e2048-d24"),
+    "rollout": dict(model=MODEL, tp=2, sp1=1, sp2=2, global_batch=16, loss="mse", rollout=1,
+                    name="swin-p4-e1024-d16"),
+}
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -44,13 +56,43 @@ def parse():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
-    ap.add_argument("--depth", type=int, default=MODEL["depth"])
+    ap.add_argument("--config", default="dp", choices=sorted(CONFIGS),
+                    help="dp: pure data parallel (headline); hybrid: sp2=2 x tp=2 x dp, global batch 8; large: "
+                         "e2048-d24 with tp=4 x sp2=2, AMSE loss, 2 rollout steps, global batch 4; rollout: "
+                         "40-step bf16 inference from 16 initial conditions with sp2=2 x tp=2 x dp")
+    ap.add_argument("--global-batch", type=int, default=None)
+    ap.add_argument("--depth", type=int, default=None)
+    ap.add_argument("--tp", type=int, default=None)
+    ap.add_argument("--sp1", type=int, default=None)
+    ap.add_argument("--sp2", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-rollout", action="store_true")
     ap.add_argument("--breakdown", default=None,
                     help="write a per-kernel device-time table of one step to this file (not timed)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    c = CONFIGS[args.config]
+    args.model = dict(c["model"])
+    if args.depth is not None:
+        args.model["depth"] = args.depth
+    args.depth = args.model["depth"]
+    args.global_batch = args.global_batch or c["global_batch"]
+    for k in ("tp", "sp1", "sp2"):
+        if getattr(args, k) is None:
+            setattr(args, k, c[k])
+    args.loss, args.rollout, args.model_name = c["loss"], c["rollout"], c["name"]
+    return args
+
+
+def layout(args, world):
+    mp = args.tp * args.sp1 * args.sp2
+    if world % mp:
+        raise SystemExit(f"--config {args.config}: {world} GPUs do not divide into tp={args.tp} x sp1={args.sp1} "
+                         f"x sp2={args.sp2}")
+    dp = world // mp
+    if mp == 1:
+        return dp, f"dp{dp}"
+    parts = [f"{k}={getattr(args, k)}" for k in ("sp1", "sp2", "tp") if getattr(args, k) > 1] + [f"dp={dp}"]
+    return dp, " x ".join(parts)
 
 
 # ----------------------------------------------------------------------------- infra
@@ -134,17 +176,19 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 # ----------------------------------------------------------------------------- data
-def make_batches(n, device, pinned=False):
-    """n synthetic micro-batches (1, 2, 73, 720, 1440) fp32: inputs + target time step."""
+def make_batches(n, device, pinned=False, rollout=1):
+    """n synthetic micro-batches (1, 1 + rollout, 70, H, W) fp32: inputs + target time steps, where
+    (H, W) is this rank's spatial shard of 720 x 1440 once the process groups exist."""
     from neural_scaling_weather_b200.data.synthetic import SyntheticERA5
 
     ds = SyntheticERA5(mode="train", nlat=NLAT, nlon=NLON, sfc_vars=["u10m", "v10m", "t2m", "tcwv", "msl"],
                        pl_vars=["u", "v", "z", "t", "q"],
                        levels=[50, 100, 150, 200, 250, 300, 400, 500, 600, 700, 850, 925, 1000],
-                       n_times=200, dt_scale=6, model_patch_size=4, invariants=["lsm", "orog", "coslat"])
+                       n_times=200, dt_scale=6, model_patch_size=4, invariants=["lsm", "orog", "coslat"],
+                       num_rollout_steps=rollout)
     out = []
     for i in range(n):
-        x = ds.generate(ds.window_hours(7 * i), device=device)  # (2, 70, 720, 1440)
+        x = ds.generate(ds.window_hours(7 * i), device=device)  # (1 + rollout, 70, H, W)
         out.append(x.unsqueeze(0))
     inv = torch.from_numpy(ds.invar).to(device)
     if pinned:
@@ -161,19 +205,21 @@ def native(args, rank, world, local):
     overrides = [
         f"hydra.run.dir=/tmp/nsw_bench_{os.getpid()}", "parallelism.backend=nccl", "optimizer=adamw",
         "optimizer.lr=5e-4", "optimizer.scheduler=null", "train.clip_grad_norm=1.0", "train.amp_dtype=bf16",
-        "train.enable_amp=true", "loss=mse", "loss.area_weights=true", "logging.log_to_wandb=false",
+        "train.enable_amp=true", f"loss={args.loss}", "loss.area_weights=true", "logging.log_to_wandb=false",
         "logging.log_to_screen=false", "train.save_checkpoint=false",
-        f"model.embed_dim={MODEL['embed_dim']}", f"model.depth={args.depth}",
-        f"model.num_heads={MODEL['num_heads']}", f"model.patch_size={MODEL['patch_size']}",
+        f"model.embed_dim={args.model['embed_dim']}", f"model.depth={args.depth}",
+        f"model.num_heads={args.model['num_heads']}", f"model.patch_size={args.model['patch_size']}",
         "model.window_size=[9,18]", f"data.batch_size={args.global_batch}",
         "data.synthetic.n_samples=200", "train.seed=0", "train.cuda_graphs=true",
+        f"parallelism.tp={args.tp}", f"parallelism.sp1={args.sp1}", f"parallelism.sp2={args.sp2}",
+        f"train.num_rollout_steps={args.rollout}",
     ]
     cfg = C.compose("default", overrides)
     tr = Trainer(cfg)
     tr.init_exp_dir(tr.exp_dir)
     tr.build()
     accum = tr.gradient_accum_steps
-    _, batches, _ = make_batches(2, "cuda")
+    _, batches, _ = make_batches(2, "cuda", rollout=args.rollout)
     dev_batches = batches
 
     def step(src):
@@ -191,8 +237,8 @@ def native(args, rank, world, local):
 
     # launch count (one extra step under the profiler, outside the timed region)
     launches = count_launches(lambda: step(dev_batches))
-    if args.breakdown and rank == 0:
-        kernel_breakdown(lambda: step(dev_batches), args.breakdown)
+    if args.breakdown:  # every rank profiles (model-parallel steps need all ranks); rank 0 writes
+        kernel_breakdown(lambda: step(dev_batches), args.breakdown if rank == 0 else None)
 
     sampler = ClockSampler(gpus=list(range(world)) if world > 1 else [torch.cuda.current_device()])
     if rank == 0:
@@ -216,7 +262,7 @@ def native(args, rank, world, local):
     if not args.no_e2e:
         from neural_scaling_weather_b200.data import device_prefetch
 
-        _, host_batches, _ = make_batches(2, "cuda", pinned=True)
+        _, host_batches, _ = make_batches(2, "cuda", pinned=True, rollout=args.rollout)
         dev = torch.device("cuda", torch.cuda.current_device())
 
         def run_steps(n):
@@ -247,8 +293,8 @@ def native(args, rank, world, local):
                        "micro-batch ahead on a copy stream) + loss.item() each step"}
 
     rollout_ms = None
-    if not args.no_rollout and rank == 0:
-        rollout_ms = rollout_latency(tr, dev_batches[0])
+    if not args.no_rollout:  # every rank runs the forward (model-parallel layouts need all of them)
+        rollout_ms = max_over_ranks(rollout_latency(tr, dev_batches[0]), world)
     err = _ext.require().read_error_flag(True)
     return ms, clocks, e2e, launches, rollout_ms, err
 
@@ -270,7 +316,65 @@ def rollout_latency(tr, batch, n=5):
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
     model.train()
-    return statistics.median(ts)
+    return statistics.median(ts) / max(1, int(tr.cfg.train.num_rollout_steps))  # the forward rolls out nrs steps
+
+
+def inference_bench(args, rank, world, local):
+    """Autoregressive bf16 inference through ``Inferencer`` (the ``inference.py`` path): 16 initial
+    conditions 12 h apart, each rolled out 40 x 6 h with latitude-weighted RMSE / ACC per lead and
+    spectra at 6/24/120/240 h; random-init weights.  Returns the median device-timed ms per model step
+    (max over ranks), the wall seconds of the whole loop and channel-0 scores at 24 h and 240 h."""
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.inference.inferencer import Inferencer
+
+    overrides = [
+        f"hydra.run.dir=/tmp/nsw_bench_inf_{os.getpid()}", "parallelism.backend=nccl",
+        "logging.log_to_wandb=false", "logging.log_to_screen=false",
+        f"model.embed_dim={args.model['embed_dim']}", f"model.depth={args.depth}",
+        f"model.num_heads={args.model['num_heads']}", f"model.patch_size={args.model['patch_size']}",
+        "model.window_size=[9,18]", "train.num_rollout_steps=1", "train.seed=0",
+        f"parallelism.tp={args.tp}", f"parallelism.sp1={args.sp1}", f"parallelism.sp2={args.sp2}",
+        "inference.start_date=2020-01-01T00", "inference.end_date=2020-01-08T12",
+        "inference.time_horizon_in_hours=240", "inference.precision=bf16",
+        "inference.checkpoint=/tmp/nsw_bench_no_checkpoint.tar", "inference.checkpoint_hyperparams=null",
+        "inference.run_benchmark=true",
+        # random-init weights diverge within a few steps: keep every IC in the scores instead of dropping
+        # the "unstable" ones (the default threshold drops all of them)
+        "inference.unstable_rmse_threshold=1e30",
+    ]
+    cfg = C.compose("default", overrides)
+    inf = Inferencer(cfg)
+    inf.init_exp_dir(inf.exp_dir)
+    torch.manual_seed(0)
+    inf.build()
+    # warm-up: one initial condition's first steps, outside the recorded timings
+    keep, leads = inf.ics, inf.lead_times
+    inf.ics, inf.lead_times = keep[:1], leads[:3]
+    inf.inference()
+    inf.ics, inf.lead_times, inf.ic_count, inf.step_ms = keep, leads, 0, []
+    for buf in [inf.rmse, inf.acc] + list(inf.spectra.values()):
+        buf.zero_()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(gpus=list(range(world)) if world > 1 else [torch.cuda.current_device()])
+    if rank == 0:
+        sampler.start()
+    t0 = time.perf_counter()
+    inf.inference()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    out = inf.compute_final_metrics()
+    ms = max_over_ranks(out["ms_per_step"], world)
+    wall = max_over_ranks(wall, world)
+    lt = inf.lead_times
+    scores = {"rmse_ch0_24h": float(out["rmse"][0, lt.index(24)]), "rmse_ch0_240h": float(out["rmse"][0, -1]),
+              "acc_ch0_24h": float(out["acc"][0, lt.index(24)]), "acc_ch0_240h": float(out["acc"][0, -1]),
+              "unstable_ics": int(out["unstable"])}
+    return ms, wall, clocks, scores, inf.total_ic_count, len(lt)
 
 
 def count_launches(fn):
@@ -314,6 +418,8 @@ def kernel_breakdown(fn, path):
             t = ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
             c, tt = agg.get(name, (0, 0.0))
             agg[name] = (c + 1, tt + t)
+    if path is None:
+        return
     total = sum(v[1] for v in agg.values())
     with open(path, "w") as f:
         f.write(f"total device time of one step: {total / 1000:.1f} ms\n")
@@ -462,6 +568,13 @@ def main():
     args = parse()
     if args.impl == "reference":
         rank, world, local = init_dist(args.gpus)
+        if args.config != "dp":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"the reference arm is wired for the dp "
+                                  f"configuration only, not --config {args.config}"}))
+            if dist.is_initialized():
+                dist.destroy_process_group()
+            return
         try:
             res = reference(args, rank, world, local)
         except Exception as e:  # noqa: BLE001
@@ -488,6 +601,24 @@ def main():
         return
 
     rank, world, local = init_dist(args.gpus)
+    dp, par = layout(args, world)
+    if args.config == "rollout":
+        ms, wall, clocks, scores, n_ic, n_lead = inference_bench(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps({
+                "metric": "ms per autoregressive rollout step (device-timed median, max over ranks)", "value": ms,
+                "unit": "ms/step", "n_gpus": world, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded advected sinusoids + noise, 70 ch x 720 x 1440), random-init weights",
+                "config": {"model": args.model_name, "parallelism": par, "initial_conditions": n_ic,
+                           "steps_per_ic": n_lead, "step_hours": 6, "depth": args.depth,
+                           "path": "Inferencer.inference (inference.py): rollout + RMSE/ACC + spectra per lead"},
+                "wall_s_all_ics": wall, "scores": scores, "clocks": clocks,
+            }))
+        if dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     ms, clocks, e2e, launches, rollout_ms, err = native(args, rank, world, local)
     if rank == 0:
         per_step_launch = launches[0] if isinstance(launches, tuple) else None
@@ -496,8 +627,9 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded advected sinusoids + noise, 70 ch x 720 x 1440), random-init weights",
-            "config": {"model": "swin-p4-e1024-d16", "global_batch": args.global_batch, "seq_len": 64800,
-                       "parallelism": f"dp{world}", "micro_batch": 1, "optimizer": "adamw lr 5e-4 clip 1.0",
+            "config": {"model": args.model_name, "global_batch": args.global_batch, "seq_len": 64800,
+                       "parallelism": par, "micro_batch": 1, "optimizer": "adamw lr 5e-4 clip 1.0",
+                       "loss": args.loss, "train_rollout_steps": args.rollout, "bench_config": args.config,
                        "l2": "inputs (300 MB fp32 per sample) larger than L2; no extra flush",
                        "depth": args.depth},
             "clocks": clocks,

@@ -406,6 +406,72 @@ void dp_barrier(std::vector<int64_t> grad, std::vector<int64_t> data, std::vecto
   check(nsw::dp_barrier(pr, (int)slot, (uint32_t)epoch, stream()), "dp_barrier");
 }
 
+// ------------------------------------------------------------------------------ sharded roll (halo)
+// x, out: contiguous (..., H_l, W_l, C) CUDA tensors of this rank's shard; C * element size a multiple of
+// 16 bytes.  geom = [n1, n2, sh, sw, rank]; h_off / w_off: shard offsets (n1 + 1 / n2 + 1 entries);
+// coord1 / coord2: shard of each group rank; band / flags: every group rank's symmetric buffers.
+static nsw::HaloArgs halo_args(const Tensor& x, const Tensor& out, std::vector<int64_t> geom,
+                               std::vector<int64_t> h_off, std::vector<int64_t> w_off, std::vector<int64_t> coord1,
+                               std::vector<int64_t> coord2, std::vector<int64_t> band, std::vector<int64_t> flags) {
+  TORCH_CHECK(geom.size() == 5, "halo_roll: geom = [n1, n2, sh, sw, rank]");
+  nsw::HaloArgs a{};
+  a.n1 = (int)geom[0];
+  a.n2 = (int)geom[1];
+  a.sh = (int)geom[2];
+  a.sw = (int)geom[3];
+  a.rank = (int)geom[4];
+  a.world = (int)band.size();
+  TORCH_CHECK(a.world >= 2 && a.world <= 8 && a.n1 * a.n2 == a.world && (int)flags.size() == a.world &&
+                  (int)coord1.size() == a.world && (int)coord2.size() == a.world &&
+                  (int)h_off.size() == a.n1 + 1 && (int)w_off.size() == a.n2 + 1 && a.rank >= 0 && a.rank < a.world,
+              "halo_roll: inconsistent group description");
+  for (int i = 0; i < 8; ++i) a.grid_rank[i] = -1;
+  for (int r = 0; r < a.world; ++r) {
+    a.band[r] = reinterpret_cast<void*>(band[r]);
+    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+    a.coord1[r] = (int)coord1[r];
+    a.coord2[r] = (int)coord2[r];
+    TORCH_CHECK(a.coord1[r] >= 0 && a.coord1[r] < a.n1 && a.coord2[r] >= 0 && a.coord2[r] < a.n2,
+                "halo_roll: shard coordinate out of range");
+    a.grid_rank[a.coord1[r] * a.n2 + a.coord2[r]] = r;
+  }
+  for (int i = 0; i < a.n1 * a.n2; ++i) TORCH_CHECK(a.grid_rank[i] >= 0, "halo_roll: a shard has no rank");
+  for (int i = 0; i <= a.n1; ++i) a.h_off[i] = (int)h_off[i];
+  for (int j = 0; j <= a.n2; ++j) a.w_off[j] = (int)w_off[j];
+  need_cuda(x, "x");
+  need_cuda(out, "out");
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && x.sizes() == out.sizes() &&
+                  x.scalar_type() == out.scalar_type() && x.dim() >= 3,
+              "halo_roll: x and out contiguous (..., H_l, W_l, C) of one shape and dtype");
+  const int64_t rowb = x.size(-1) * x.element_size();
+  TORCH_CHECK(rowb % 16 == 0, "halo_roll: C * element size must be a multiple of 16 bytes");
+  const int i1 = a.coord1[a.rank], i2 = a.coord2[a.rank];
+  TORCH_CHECK(x.size(-3) == a.h_off[i1 + 1] - a.h_off[i1] && x.size(-2) == a.w_off[i2 + 1] - a.w_off[i2],
+              "halo_roll: x is not this rank's shard");
+  a.x = x.data_ptr();
+  a.out = out.data_ptr();
+  a.row_vec = (int)(rowb / 16);
+  a.bt = (int)(x.numel() / (x.size(-3) * x.size(-2) * x.size(-1)));
+  return a;
+}
+
+int64_t halo_band_bytes(Tensor x, std::vector<int64_t> geom, std::vector<int64_t> h_off, std::vector<int64_t> w_off,
+                        std::vector<int64_t> coord1, std::vector<int64_t> coord2) {
+  // size of the largest band buffer any rank of the group needs (no pointers involved)
+  std::vector<int64_t> fake(coord1.size(), 16);
+  int64_t best = 0;
+  const auto a = halo_args(x, x, geom, h_off, w_off, coord1, coord2, fake, fake);
+  for (int r = 0; r < a.world; ++r) best = std::max(best, nsw::halo_band_bytes(a, r));
+  return best;
+}
+
+void halo_roll(Tensor x, Tensor out, std::vector<int64_t> geom, std::vector<int64_t> h_off,
+               std::vector<int64_t> w_off, std::vector<int64_t> coord1, std::vector<int64_t> coord2,
+               std::vector<int64_t> band, std::vector<int64_t> flags) {
+  const auto a = halo_args(x, out, geom, h_off, w_off, coord1, coord2, band, flags);
+  check(nsw::halo_roll(a, stream()), "halo_roll");
+}
+
 // ------------------------------------------------------------------------------ SHT (Legendre part)
 // x, w: float64 [K] (this rank's colatitude nodes and quadrature weights); orders m0 .. m0 + m_count - 1;
 // returns (P packed float32 [rows, K], row_off int64 [m_count]).
@@ -678,6 +744,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_reduce", &dp_reduce);
   m.def("dp_adamw", &dp_adamw);
   m.def("dp_barrier", &dp_barrier);
+  m.def("halo_band_bytes", &halo_band_bytes);
+  m.def("halo_roll", &halo_roll);
   m.def("legendre_fwd", &legendre_fwd);
   m.def("legendre_bwd", &legendre_bwd);
   m.def("wgrad", &wgrad, py::arg("dy"), py::arg("x"), py::arg("out") = py::none(), py::arg("accumulate") = false,

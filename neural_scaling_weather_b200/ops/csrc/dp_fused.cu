@@ -19,49 +19,19 @@
 // error word when it runs out (4 s) and the kernel returns.
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 namespace nsw {
 namespace {
-
-constexpr unsigned long long kDpWaitNs = 4000000000ull;
-
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ unsigned long long gtime() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// wait (bounded) until *p >= v (wrap-safe); false on timeout (error recorded)
-__device__ bool dp_wait_geq(const uint32_t* p, uint32_t v, int* err) {
-  if ((int)(ld_acquire_sys_u32(p) - v) >= 0) return true;
-  const unsigned long long t0 = gtime();
-  for (uint32_t spin = 0;; ++spin) {
-    if ((int)(ld_acquire_sys_u32(p) - v) >= 0) return true;
-    if ((spin & 63u) == 63u) {
-      __nanosleep(200);
-      if (gtime() - t0 > kDpWaitNs) {
-        record_error(err, kErrWaitTimeout);
-        return false;
-      }
-    }
-  }
-}
 
 // announce (slot, epoch) to every rank, then wait for every rank's announcement of the same slot
 __device__ bool dp_exchange(const DpPeers& pr, int slot, uint32_t epoch, int* err) {
   __threadfence_system();
   for (int r = 0; r < pr.world; ++r)
-    st_release_sys_u32(pr.flags[r] + kDpFlagBase + (int64_t)pr.rank * pr.slots + slot, epoch);
+    peer::st_release(pr.flags[r] + kDpFlagBase + (int64_t)pr.rank * pr.slots + slot, epoch);
   bool ok = true;
   for (int r = 0; r < pr.world && ok; ++r)
-    ok = dp_wait_geq(pr.flags[pr.rank] + kDpFlagBase + (int64_t)r * pr.slots + slot, epoch, err);
+    ok = peer::wait_geq(pr.flags[pr.rank] + kDpFlagBase + (int64_t)r * pr.slots + slot, epoch, err);
   return ok;
 }
 

@@ -179,6 +179,26 @@ cudaError_t dp_adamw(const DpPeers& pr, const int64_t* rlo, const int64_t* rhi, 
                      cudaStream_t s);
 cudaError_t dp_barrier(const DpPeers& pr, int slot, uint32_t epoch, cudaStream_t s);
 
+// Cyclic roll of a (B*T, H_l, W_l, C) activation sharded over an n1 x n2 (sp1 x sp2) grid of one node's
+// GPUs (halo_roll.cu): band buffers and flag words in symmetric memory, one entry per group rank.
+// Flag words of each rank: [kHaloEpoch] rolls completed, [kHaloPackCount] / [kHaloDoneCount] block
+// counters, [kHaloReady + r] / [kHaloAck + r] the last epoch rank r published.
+constexpr int kHaloEpoch = 0, kHaloPackCount = 1, kHaloDoneCount = 2, kHaloReady = 16, kHaloAck = 32;
+constexpr int kHaloFlagWords = 48;
+struct HaloArgs {
+  const void* x;
+  void* out;
+  void* band[8];
+  uint32_t* flags[8];
+  int world, rank, n1, n2;
+  int coord1[8], coord2[8];  // (sp1, sp2) shard of each group rank
+  int grid_rank[8];          // group rank holding shard (i, j), at i * n2 + j
+  int h_off[9], w_off[9];    // shard offsets along H (n1 + 1 entries) and W (n2 + 1)
+  int bt, row_vec, sh, sw;   // B*T, 16-byte vectors per row of C elements, shifts along H and W
+};
+int64_t halo_band_bytes(const HaloArgs& a, int shard);
+cudaError_t halo_roll(const HaloArgs& a, cudaStream_t s);
+
 // Legendre part of the real SHT (sht.cu): table P[m, l, k] = w_k Pbar_l^m(x_k) for orders
 // m0 .. m0 + m_count - 1 (packed: order index mi's rows l = m .. L-1 start at row row_off[mi]),
 // and the batched contractions C[mi, l, :] = sum_k P F[mi, k, :] / dF[mi, k, :] = sum_l P dC[mi, l, :].

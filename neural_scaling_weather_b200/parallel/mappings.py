@@ -102,20 +102,27 @@ class _RollFwdReverseRollBwd(torch.autograd.Function):
     def forward(ctx, x, shifts, dims, comm_names, shapes):
         if not (len(shifts) == len(dims) == len(comm_names)):
             raise ValueError("shifts, dims and comm_names must have equal length")
-        shapes = shapes or [None] * len(shifts)
         ctx.args = (shifts, dims, comm_names, shapes)
-        for sh, d, c, s in zip(shifts, dims, comm_names, shapes):
-            if sh != 0:
-                x = _distributed_roll(x, sh, d, c, s)
-        return x
+        return _roll_all(x, shifts, dims, comm_names, shapes)
 
     @staticmethod
     def backward(ctx, g):
         shifts, dims, comm_names, shapes = ctx.args
-        for sh, d, c, s in zip(shifts, dims, comm_names, shapes):
-            if sh != 0:
-                g = _distributed_roll(g, -sh, d, c, s)
-        return g, None, None, None, None
+        return _roll_all(g, tuple(-s for s in shifts), dims, comm_names, shapes), None, None, None, None
+
+
+def _roll_all(x, shifts, dims, comm_names, shapes):
+    """Roll along every (dim, group): one peer-memory kernel for the (H, W) roll over sp1 x sp2 where it
+    applies (``parallel.halo``), else one NCCL exchange per dimension."""
+    from . import halo
+
+    if halo.available(x, shifts, dims, comm_names, shapes):
+        return halo.roll(x, shifts, shapes)
+    shapes = shapes or [None] * len(shifts)
+    for sh, d, c, s in zip(shifts, dims, comm_names, shapes):
+        if sh != 0:
+            x = _distributed_roll(x, sh, d, c, s)
+    return x
 
 
 class _TransposeFwdTransposeBwd(torch.autograd.Function):

@@ -22,6 +22,7 @@ SOURCES = [
     os.path.join(CSRC, "rmsnorm_tma.cu"),
     os.path.join(CSRC, "sht.cu"),
     os.path.join(CSRC, "dp_fused.cu"),
+    os.path.join(CSRC, "halo_roll.cu"),
 ]
 
 NVCC_FLAGS = [

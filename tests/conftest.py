@@ -24,3 +24,6 @@ def _reset_comm():
     from neural_scaling_weather_b200.parallel import symm
 
     symm.reset()
+    from neural_scaling_weather_b200.parallel import halo
+
+    halo.reset()

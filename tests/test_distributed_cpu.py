@@ -272,3 +272,13 @@ def test_epoch_covers_every_sample_once_across_dp_ranks(tmp_path, world):
     """The DALI-epoch check of the reference (``tests/test_dali_es.py``) for the synthetic
     loader: one epoch over all dp ranks emits every sample window exactly once."""
     run(_epoch_coverage_worker, world, str(tmp_path))
+
+
+def test_fused_halo_roll_not_available_on_cpu():
+    """The peer-memory roll is only taken for CUDA tensors in an NCCL sp1 x sp2 group; CPU tensors use the
+    portable exchange."""
+    from neural_scaling_weather_b200.parallel import halo
+
+    x = torch.zeros(1, 1, 8, 8, 16)
+    assert halo.available(x, (-2, -3), (-3, -2), ("sp1", "sp2"), ([8], [8])) is False
+    assert halo._norm(-4, 180) == -4 and halo._norm(176, 180) == -4 and halo._norm(9, 360) == 9

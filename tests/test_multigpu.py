@@ -55,3 +55,15 @@ def test_fused_dp_matches_nccl_two_gpus():
         pytest.skip("needs 2 GPUs")
     r = _torchrun(2, ["tests/mp_dp_fused_worker.py"])
     assert "DP_FUSED_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_fused_halo_roll_matches_torch_roll(n):
+    """Sharded shifted-window roll over peer memory against torch.roll of the gathered field (sp1, sp2 and,
+    on 4 GPUs, 2 x 2 layouts; graph replay; the reverse roll of the backward); prints its timing against the
+    NCCL roll."""
+    if NGPU < n:
+        pytest.skip(f"needs {n} GPUs")
+    r = _torchrun(n, ["tests/mp_halo_worker.py"])
+    print("\n".join(l for l in r.stdout.splitlines() if l.startswith("roll of")))
+    assert "HALO_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
