@@ -84,7 +84,10 @@ std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
 
 // eps >= 0: the kernel recomputes rstd from x with this eps (the forward's value); else it reads rstd
 // add (optional, [rows, n] like x): added to dx in the same pass (skip-connection gradient)
-std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, double eps, c10::optional<Tensor> add) {
+// dw_into (optional, fp32 [n] contiguous): the weight gradient is added into it (the optimizer's gradient
+// buffer) and returned; otherwise a fresh tensor
+std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, double eps, c10::optional<Tensor> add,
+                                c10::optional<Tensor> dw_into) {
   need_cuda(dy, "dy");
   need_cuda(x, "x");
   const int n = (int)x.size(-1);
@@ -103,8 +106,13 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, doub
                          fused_add ? add->data_ptr() : nullptr),
         "rmsnorm_bwd");
   if (add && !fused_add) dx.add_(*add);
-  auto dw = torch::empty({(int64_t)n}, x.options().dtype(at::kFloat));
-  check(nsw::sum_rows(part.data_ptr<float>(), 1, parts, n, dw.data_ptr<float>(), stream()), "sum_rows");
+  if (dw_into)
+    TORCH_CHECK(dw_into->is_cuda() && dw_into->scalar_type() == at::kFloat && dw_into->is_contiguous() &&
+                    dw_into->numel() == n,
+                "rmsnorm_bwd: dw_into must be a contiguous fp32 CUDA tensor of n elements");
+  auto dw = dw_into ? *dw_into : torch::empty({(int64_t)n}, x.options().dtype(at::kFloat));
+  check(nsw::sum_rows(part.data_ptr<float>(), 1, parts, n, dw.data_ptr<float>(), stream(), dw_into.has_value()),
+        "sum_rows");
   return {dx, dw};
 }
 
@@ -701,7 +709,8 @@ std::vector<Tensor> window_attn_fwd(Tensor qkv, Tensor qw, Tensor kw, std::vecto
 
 std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out, Tensor dout, Tensor lse,
                                     std::vector<int64_t> gi, double scale, int64_t impl,
-                                    c10::optional<Tensor> stamps) {
+                                    c10::optional<Tensor> stamps, c10::optional<Tensor> dqw_into,
+                                    c10::optional<Tensor> dkw_into) {
   need_cuda(qkv, "qkv");
   need_cuda(dout, "dout");
   auto g = make_geom(gi, scale);
@@ -729,6 +738,17 @@ std::vector<Tensor> window_attn_bwd(Tensor qkv, Tensor qw, Tensor kw, Tensor out
                                dout.data_ptr(), lse.data_ptr<float>(), dqkv.data_ptr(), qp, kp, g, dt_code(qkv),
                                stream()),
           "window_attn_bwd");
+  // QK-norm weight gradients: added into the given fp32 gradient buffers (both or neither), else fresh
+  if (dqw_into || dkw_into) {
+    TORCH_CHECK(dqw_into && dkw_into, "window_attn_bwd: dqw_into and dkw_into go together");
+    for (const Tensor* t : {&*dqw_into, &*dkw_into})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == g.hd,
+                  "window_attn_bwd: QK-norm gradient buffers must be contiguous fp32 CUDA tensors of head_dim");
+    check(nsw::sum_rows(part.data_ptr<float>(), 2, rows, g.hd, dqw_into->data_ptr<float>(), stream(), true,
+                        dkw_into->data_ptr<float>()),
+          "sum_rows");
+    return {dqkv, *dqw_into, *dkw_into};
+  }
   auto sums = torch::empty({2, (int64_t)g.hd}, qkv.options().dtype(at::kFloat));
   check(nsw::sum_rows(part.data_ptr<float>(), 2, rows, g.hd, sums.data_ptr<float>(), stream()), "sum_rows");
   return {dqkv, sums[0], sums[1]};
@@ -757,7 +777,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_error_flag", &set_error_flag);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
-        py::arg("eps") = -1.0, py::arg("add") = py::none());
+        py::arg("eps") = -1.0, py::arg("add") = py::none(), py::arg("dw_into") = py::none());
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("res_period") = 0, py::arg("act") = 0, py::arg("preact") = py::none(), py::arg("out_f32") = false,
         py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("impl") = 0);
@@ -780,5 +800,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("impl") = 0, py::arg("stamps") = py::none());
   m.def("window_attn_bwd", &window_attn_bwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("out"),
         py::arg("dout"), py::arg("lse"), py::arg("geom"), py::arg("scale"), py::arg("impl") = 0,
-        py::arg("stamps") = py::none());
+        py::arg("stamps") = py::none(), py::arg("dqw_into") = py::none(), py::arg("dkw_into") = py::none());
 }

@@ -360,7 +360,8 @@ __global__ void col_sum_final_kernel(const float* __restrict__ partial, float* _
 // out[b, c] = sum_r part[b, r, c] (deterministic: a fixed split of the rows over 8 thread rows, then
 // the 8 partial sums in order).  Block (32 columns x 8 row groups) per 32 columns of one batch.
 // Used for the per-CTA weight-gradient partial rows of the norm and attention kernels.
-__global__ void sum_rows_kernel(const float* __restrict__ part, int64_t rows, int64_t n, float* __restrict__ out) {
+__global__ void sum_rows_kernel(const float* __restrict__ part, int64_t rows, int64_t n, float* __restrict__ out,
+                                float* __restrict__ out1, int accumulate) {
   __shared__ float red[8][33];
   const int64_t b = blockIdx.y;
   const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
@@ -376,13 +377,16 @@ __global__ void sum_rows_kernel(const float* __restrict__ part, int64_t rows, in
     float t = red[0][threadIdx.x];
 #pragma unroll
     for (int k = 1; k < 8; ++k) t += red[k][threadIdx.x];
-    out[b * n + c] = t;
+    float* o = (b == 1 && out1) ? out1 + c : out + b * n + c;
+    *o = accumulate ? *o + t : t;
   }
 }
 
-cudaError_t sum_rows(const float* part, int64_t batches, int64_t rows, int64_t n, float* out, cudaStream_t s) {
+cudaError_t sum_rows(const float* part, int64_t batches, int64_t rows, int64_t n, float* out, cudaStream_t s,
+                     bool accumulate, float* out1) {
   if (batches <= 0 || n <= 0) return cudaSuccess;
-  sum_rows_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)batches), dim3(32, 8), 0, s>>>(part, rows, n, out);
+  sum_rows_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)batches), dim3(32, 8), 0, s>>>(part, rows, n, out, out1,
+                                                                                          accumulate ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -466,6 +470,38 @@ __global__ void col2im_kernel(const T* __restrict__ dcols, TX* __restrict__ dx, 
   }
 }
 
+// p = 4, fp32 image with W % 4 == 0: one thread per (patch, channel) reads its 4 x 4 pixels as four
+// 16-byte rows (consecutive threads take consecutive patches of one image row, so each of the four
+// reads is coalesced) and writes the 16 values of its K-slice (c * 16 .. c * 16 + 15) as whole
+// 16-byte vectors.
+template <typename T>
+__global__ void im2col_p4_kernel(const float* __restrict__ x, T* __restrict__ cols, int N, int C, int H, int W) {
+  const int h = H / 4, w = W / 4, K = C * 16;
+  const int64_t total = (int64_t)N * h * C * w;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int jj = (int)(i % w);
+    const int64_t t = i / w;
+    const int c = (int)(t % C);
+    const int64_t t2 = t / C;
+    const int ii = (int)(t2 % h);
+    const int64_t n = t2 / h;
+    const float* src = x + ((n * C + c) * H + (int64_t)ii * 4) * W + (int64_t)jj * 4;
+    alignas(16) T vals[16];
+#pragma unroll
+    for (int py = 0; py < 4; ++py) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + (int64_t)py * W));
+      vals[py * 4 + 0] = from_f<T>(v.x);
+      vals[py * 4 + 1] = from_f<T>(v.y);
+      vals[py * 4 + 2] = from_f<T>(v.z);
+      vals[py * 4 + 3] = from_f<T>(v.w);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(cols + ((n * h + ii) * w + jj) * K + c * 16);
+    dst[0] = reinterpret_cast<const uint4*>(vals)[0];
+    dst[1] = reinterpret_cast<const uint4*>(vals)[1];
+  }
+}
+
 template <typename TX>
 static cudaError_t launch_im2col(const TX* x, void* cols, int N, int C, int H, int W, int p,
                                  int dtype, cudaStream_t s) {
@@ -484,6 +520,18 @@ static cudaError_t launch_im2col(const TX* x, void* cols, int N, int C, int H, i
 
 cudaError_t im2col_patch(const void* x, int x_dtype, void* cols, int N, int C, int H, int W, int p,
                          int dtype, cudaStream_t s) {
+  if (x_dtype == kF32 && p == 4 && W % 4 == 0 && H % 4 == 0 && (dtype == kBF16 || dtype == kF16) &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(cols) & 15) == 0) {
+    const int64_t total = (int64_t)N * (H / 4) * C * (W / 4);
+    int64_t blocks = (total + 255) / 256;
+    const int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    if (dtype == kBF16)
+      im2col_p4_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>((const float*)x, (__nv_bfloat16*)cols, N, C, H, W);
+    else
+      im2col_p4_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>((const float*)x, (__half*)cols, N, C, H, W);
+    return cudaGetLastError();
+  }
   if (x_dtype == kF32) return launch_im2col((const float*)x, cols, N, C, H, W, p, dtype, s);
   if (x_dtype == kBF16) return launch_im2col((const __nv_bfloat16*)x, cols, N, C, H, W, p, dtype, s);
   if (x_dtype == kF16) return launch_im2col((const __half*)x, cols, N, C, H, W, p, dtype, s);
@@ -550,8 +598,111 @@ __global__ void patchify_kernel(const T* __restrict__ dout, T* __restrict__ dy2,
   }
 }
 
+// Tiled forms for 16-bit data: one block per (bt, patch row ii, JB consecutive patches).  The JB rows
+// of y2 (JB * K contiguous elements, K = p * p * C) move through shared memory, so both global sides
+// are whole 16-byte vectors: y2 rows are read (unpatchify) or written (patchify) contiguously, and
+// each output image row segment (c, y = ii * p + py, x in [j0 * p, (j0 + nj) * p)) is written (or
+// read) as consecutive vectors.  Shared rows are padded by 8 elements to spread the column reads
+// over the banks.
+constexpr int kPatchJB = 16;
+
+template <typename T>
+__global__ void unpatchify_tiled_kernel(const T* __restrict__ y2, T* __restrict__ out, int h, int w, int p, int C) {
+  extern __shared__ uint4 patch_smem[];
+  T* sm = reinterpret_cast<T*>(patch_smem);
+  const int K = p * p * C, Kp = K + 8;
+  const int nbw = (w + kPatchJB - 1) / kPatchJB;
+  const int jb = (int)(blockIdx.x % nbw);
+  const int64_t r = blockIdx.x / nbw;
+  const int ii = (int)(r % h);
+  const int64_t bt = r / h;
+  const int j0 = jb * kPatchJB, nj = min(kPatchJB, w - j0);
+  const int64_t row0 = (bt * h + ii) * w + j0;
+  const int kv = K / 8;  // 16-byte vectors per row
+  const uint4* src = reinterpret_cast<const uint4*>(y2 + row0 * K);
+  for (int v = threadIdx.x; v < nj * kv; v += blockDim.x) {
+    const int jj = v / kv, k = v - jj * kv;
+    *reinterpret_cast<uint4*>(sm + jj * Kp + k * 8) = src[v];
+  }
+  __syncthreads();
+  const int64_t H = (int64_t)h * p, W = (int64_t)w * p;
+  const int vper = nj * p / 8;  // 16-byte vectors per output row segment
+  for (int t = threadIdx.x; t < C * p * vper; t += blockDim.x) {
+    const int v = t % vper, cp = t / vper, py = cp % p, c = cp / p;
+    alignas(16) T vals[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int x = v * 8 + e, jj = x / p, px = x - jj * p;
+      vals[e] = sm[jj * Kp + (py * p + px) * C + c];
+    }
+    *reinterpret_cast<uint4*>(out + ((bt * C + c) * H + ii * p + py) * W + (int64_t)j0 * p + v * 8) =
+        *reinterpret_cast<const uint4*>(vals);
+  }
+}
+
+template <typename T>
+__global__ void patchify_tiled_kernel(const T* __restrict__ dout, T* __restrict__ dy2, int h, int w, int p, int C) {
+  extern __shared__ uint4 patch_smem[];
+  T* sm = reinterpret_cast<T*>(patch_smem);
+  const int K = p * p * C, Kp = K + 8;
+  const int nbw = (w + kPatchJB - 1) / kPatchJB;
+  const int jb = (int)(blockIdx.x % nbw);
+  const int64_t r = blockIdx.x / nbw;
+  const int ii = (int)(r % h);
+  const int64_t bt = r / h;
+  const int j0 = jb * kPatchJB, nj = min(kPatchJB, w - j0);
+  const int64_t H = (int64_t)h * p, W = (int64_t)w * p;
+  const int vper = nj * p / 8;
+  for (int t = threadIdx.x; t < C * p * vper; t += blockDim.x) {
+    const int v = t % vper, cp = t / vper, py = cp % p, c = cp / p;
+    alignas(16) T vals[8];
+    *reinterpret_cast<uint4*>(vals) = *reinterpret_cast<const uint4*>(
+        dout + ((bt * C + c) * H + ii * p + py) * W + (int64_t)j0 * p + v * 8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int x = v * 8 + e, jj = x / p, px = x - jj * p;
+      sm[jj * Kp + (py * p + px) * C + c] = vals[e];
+    }
+  }
+  __syncthreads();
+  const int kv = K / 8;
+  uint4* dst = reinterpret_cast<uint4*>(dy2 + ((bt * h + ii) * w + j0) * K);
+  for (int v = threadIdx.x; v < nj * kv; v += blockDim.x) {
+    const int jj = v / kv, k = v - jj * kv;
+    dst[v] = *reinterpret_cast<const uint4*>(sm + jj * Kp + k * 8);
+  }
+}
+
+// the tiled forms apply: 16-bit data, whole vectors on both sides
+static bool patch_tiled_ok(int w, int p, int C, int dtype) {
+  if (dtype != kBF16 && dtype != kF16) return false;
+  const int K = p * p * C;
+  if (K % 8 || ((int64_t)w * p) % 8) return false;
+  // every segment of nj * p elements, the last (ragged) one included, is whole vectors
+  if ((kPatchJB * p) % 8 || ((w % kPatchJB) * p) % 8) return false;
+  return (size_t)kPatchJB * (K + 8) * 2 <= 100 * 1024;
+}
+
+template <typename T>
+static cudaError_t launch_patch_tiled(bool unpatch, const void* a, void* b, int BT, int h, int w, int p, int C,
+                                      cudaStream_t s) {
+  const int nbw = (w + kPatchJB - 1) / kPatchJB;
+  const int64_t blocks = (int64_t)BT * h * nbw;
+  const size_t smem = (size_t)kPatchJB * (p * p * C + 8) * sizeof(T);
+  auto kern = unpatch ? unpatchify_tiled_kernel<T> : patchify_tiled_kernel<T>;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  kern<<<(unsigned)blocks, 256, smem, s>>>((const T*)a, (T*)b, h, w, p, C);
+  return cudaGetLastError();
+}
+
 cudaError_t unpatchify(const void* y2, void* out, int BT, int h, int w, int p, int C, int dtype,
                        cudaStream_t s) {
+  if (patch_tiled_ok(w, p, C, dtype))
+    return dtype == kBF16 ? launch_patch_tiled<__nv_bfloat16>(true, y2, out, BT, h, w, p, C, s)
+                          : launch_patch_tiled<__half>(true, y2, out, BT, h, w, p, C, s);
   const int64_t total = (int64_t)BT * C * h * p * w * p;
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 32;
@@ -569,6 +720,9 @@ cudaError_t unpatchify(const void* y2, void* out, int BT, int h, int w, int p, i
 
 cudaError_t patchify(const void* dout, void* dy2, int BT, int h, int w, int p, int C, int dtype,
                      cudaStream_t s) {
+  if (patch_tiled_ok(w, p, C, dtype))
+    return dtype == kBF16 ? launch_patch_tiled<__nv_bfloat16>(false, dout, dy2, BT, h, w, p, C, s)
+                          : launch_patch_tiled<__half>(false, dout, dy2, BT, h, w, p, C, s);
   const int64_t total = (int64_t)BT * C * h * p * w * p;
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 32;

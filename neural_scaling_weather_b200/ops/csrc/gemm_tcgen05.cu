@@ -506,61 +506,69 @@ struct EpiWarp {
     }
   }
 
-  // All-reduce mode, step 2 (all ranks' partials of the tile published): sum them (peer loads),
-  // add bias and residual, store D through the TMA-store staging ring.
-  __device__ __forceinline__ void reduce_store(const EpiParams& ep, T* stg, int64_t row_base, int64_t n0, int half,
-                                               int lane, uint32_t& ring) {
-    const int64_t row = row_base + lane;
-    const bool row_ok = row < ep.M;
+  // All-reduce mode, step 2 (all ranks' partials of the tile published): sum them, add bias and
+  // residual, store D.  The warp's block is rows [row_base, row_base + 32) x columns
+  // [n0 + half * BN/2, n0 + (half + 1) * BN/2); lanes walk it row-contiguously (16 bytes each, a row
+  // half of 128 columns is 16 lanes), so every peer load is part of a whole 256-byte row segment
+  // over NVLink.  Two rows per lane are in flight at once, each with the values of every rank, and
+  // the sum runs in rank order 0 .. W-1 on every rank, so all ranks store identical results.
+  __device__ __forceinline__ void reduce_store(const EpiParams& ep, int64_t row_base, int64_t n0, int half,
+                                               int lane) {
+    constexpr int kLanesPerRow = (BN / 2) * (int)sizeof(T) / 16;  // 16-byte pieces in a row half
+    constexpr int kRowsPerStep = 32 / kLanesPerRow;
+    constexpr int kUnroll = 2;
+    const int64_t col = n0 + half * (BN / 2) + (lane % kLanesPerRow) * 8;
+    const bool col_ok = col < ep.N;
+    float b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = 0.f;
+    if (ep.bias && col_ok) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(ep.bias + col) + 1);
+      b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+    }
 #pragma unroll 1
-    for (int cc = 0; cc < kChunks; ++cc) {
-      const int c = half * kChunks + cc;
-      const int64_t nb = n0 + c * 32;
-      if (nb >= ep.N) continue;  // warp-uniform
-      float f[32];
+    for (int r0 = 0; r0 < 32; r0 += kRowsPerStep * kUnroll) {
+      uint4 v[kUnroll][8];
+      uint4 res[kUnroll];
+      int64_t rows[kUnroll];
+      bool ok[kUnroll];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) f[j] = 0.f;
-      if (row_ok) {
-        for (int q = 0; q < ep.ar_world; ++q) {
-          // start with the next rank so the ranks do not all read rank 0 at once
-          const int r = (ep.ar_rank + 1 + q) % ep.ar_world;
-          const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.ar_part[r]) + row * ep.N + nb);
+      for (int u = 0; u < kUnroll; ++u) {
+        rows[u] = row_base + r0 + u * kRowsPerStep + lane / kLanesPerRow;
+        ok[u] = col_ok && rows[u] < ep.M;
+        const int64_t off = rows[u] * ep.N + col;
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            float x[8];
-            unpack8<T>(src[v], x);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) f[8 * v + i] += x[i];
-          }
-        }
-        if (ep.bias) {
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const float4 b4 = __ldg(reinterpret_cast<const float4*>(ep.bias + nb) + v);
-            f[4 * v] += b4.x;
-            f[4 * v + 1] += b4.y;
-            f[4 * v + 2] += b4.z;
-            f[4 * v + 3] += b4.w;
-          }
-        }
-        if (ep.residual) {
-          const uint4* rp = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
-                                                           (row % ep.res_period) * ep.ldr + nb);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            float x[8];
-            unpack8<T>(__ldg(rp + v), x);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) f[8 * v + i] += x[i];
-          }
-        }
+        for (int r = 0; r < 8; ++r)
+          if (r < ep.ar_world && ok[u]) v[u][r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.ar_part[r]) + off);
+        if (ep.residual && ok[u])
+          res[u] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                       (rows[u] % ep.res_period) * ep.ldr + col));
       }
-      if (ep.tma_out) {
-        stage_store(&ep.map_d, f, stg, lane, (int)nb, (int)row_base, ring);
-      } else if (row_ok) {
-        uint4* dp = reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + row * ep.ldd + nb);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) dp[v] = pack8<T>(&f[8 * v]);
+      for (int u = 0; u < kUnroll; ++u) {
+        if (!ok[u]) continue;
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (r < ep.ar_world) {
+            float x[8];
+            unpack8<T>(v[u][r], x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] += x[i];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] += b[i];
+        if (ep.residual) {
+          float x[8];
+          unpack8<T>(res[u], x);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] += x[i];
+        }
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + rows[u] * ep.ldd + col) = pack8<T>(f);
       }
     }
   }
@@ -751,13 +759,16 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     bool ok = true;
     if (leader) S.epi_stop = 0;
     epi_sync();
+    // Tile t's partial is drained and published, then the previous tile of this CTA is reduced: the
+    // peers have had a whole tile's time to publish their partials of it, so the flag wait rarely
+    // stalls.  Every iteration takes exactly two epilogue barriers and all warps leave on the
+    // leader's decision (S.epi_stop), so no warp is left waiting at a barrier.
+    int64_t prev = -1;
     for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int64_t m0 = (tile / n_tiles) * BM;
       const int64_t n0 = (tile % n_tiles) * BN;
       const int64_t row_base = m0 + q * 32;
       EpiWarp<T, BN> epi;
-      // every epilogue warp takes both named barriers of every tile it enters, and all of them
-      // leave the loop on the leader's decision, so no warp is left waiting at a barrier
       const bool have = mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err);
       if (have) {
         tc_fence_after();
@@ -780,8 +791,9 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           __threadfence_system();
           for (int r = 0; r < ep.ar_world; ++r)
             if (r != ep.ar_rank) st_release_sys(ep.ar_flags[r] + kArFlagBase + ep.ar_rank * ep.ar_tiles + tile, epoch);
-          for (int r = 0; r < ep.ar_world && go; ++r)
-            if (r != ep.ar_rank) go = wait_flag_geq(my_flags + kArFlagBase + r * ep.ar_tiles + tile, epoch, err);
+          if (prev >= 0)
+            for (int r = 0; r < ep.ar_world && go; ++r)
+              if (r != ep.ar_rank) go = wait_flag_geq(my_flags + kArFlagBase + r * ep.ar_tiles + prev, epoch, err);
           if (!go) *abort_flag = 1;
         }
         S.epi_stop = go ? 0 : 1;
@@ -791,9 +803,25 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         ok = false;
         break;
       }
-      epi.reduce_store(ep, stg, row_base, n0, half, lane, ring);
+      if (prev >= 0) epi.reduce_store(ep, (prev / n_tiles) * BM + q * 32, (prev % n_tiles) * BN, half, lane);
+      prev = tile;
     }
-    if (lane == 0) bulk_wait_all();
+    if (ok && prev >= 0) {  // the last tile of this CTA
+      if (leader) {
+        bool go = true;
+        for (int r = 0; r < ep.ar_world && go; ++r)
+          if (r != ep.ar_rank) go = wait_flag_geq(my_flags + kArFlagBase + r * ep.ar_tiles + prev, epoch, err);
+        if (!go) *abort_flag = 1;
+        S.epi_stop = go ? 0 : 1;
+      }
+      epi_sync();
+      if (!*reinterpret_cast<volatile int*>(&S.epi_stop)) {
+        EpiWarp<T, BN> epi;
+        epi.reduce_store(ep, (prev / n_tiles) * BM + q * 32, (prev % n_tiles) * BN, half, lane);
+      }
+    }
+    (void)stg;
+    (void)ring;
     // this CTA has read its peers' partials; before the launch ends, every CTA of every peer has
     // read this rank's partials (the next launch overwrites them)
     epi_sync();
@@ -1492,7 +1520,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int half = ew >> 2;  // columns [128 half, 128 half + 128) of the CTA's 256
     const uint32_t empty_leader = map_rank(&S.tmem_empty, 0);
-    const bool leader_thread = ew == 0 && lane == 0;
     uint32_t acc_phase = 0;
     WUnit un;
     for (int64_t i = 0; wg_unit(wp, tiles, nkb, pair, npairs, i, un); ++i) {

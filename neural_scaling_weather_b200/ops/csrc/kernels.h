@@ -24,8 +24,11 @@ cudaError_t bias_act_residual(const void* acc, int acc_dtype, const float* bias,
                               int act, int dtype, cudaStream_t s);
 cudaError_t gelu_bwd(const void* dy, const void* u, void* du, int64_t n, int dtype, cudaStream_t s);
 // column sums of a [rows, n] matrix in fp32 (deterministic two-pass)
-// out[b, :] = sum over rows of part[b, :, :] (fp32, rows in order)
-cudaError_t sum_rows(const float* part, int64_t batches, int64_t rows, int64_t n, float* out, cudaStream_t s);
+// out_b[:] (+)= sum over rows of part[b, :, :] (fp32, rows in order); out_b = out + b * n, except
+// out_1 = out1 when given (separate destinations, e.g. two parameters' gradients); accumulate adds
+// to the destination instead of overwriting it
+cudaError_t sum_rows(const float* part, int64_t batches, int64_t rows, int64_t n, float* out, cudaStream_t s,
+                     bool accumulate = false, float* out1 = nullptr);
 cudaError_t col_sum(const void* x, float* out, float* partial, int partial_rows, int64_t rows, int n,
                     int dtype, cudaStream_t s);
 

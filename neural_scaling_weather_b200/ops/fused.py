@@ -117,6 +117,15 @@ def _grad_out(g: Optional[torch.Tensor], p: torch.Tensor) -> Optional[torch.Tens
 
 
 # ---------------------------------------------------------------------------- RMSNorm
+def _norm_weight_grad(ctx, w, dw, t):
+    """The norm weight's gradient for autograd: None when the kernel added it into the optimizer's buffer
+    ``t`` (the reducer is told), else the fresh tensor."""
+    if not ctx.needs_input_grad[1]:
+        return None
+    gradsink.done(w, t is not None)
+    return None if t is not None else dw.to(w.dtype)
+
+
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, eps):
@@ -128,6 +137,8 @@ class _RMSNorm(torch.autograd.Function):
         ctx.shape = x.shape
         ctx.in_dtype = x.dtype
         ctx.eps = eps
+        if ctx.needs_input_grad[1]:
+            gradsink.use([w])
         return y.view(x.shape)
 
     @staticmethod
@@ -135,8 +146,9 @@ class _RMSNorm(torch.autograd.Function):
         ext = require()
         x2, w, rstd = ctx.saved_tensors
         dy2 = dy.reshape(x2.shape).to(x2.dtype).contiguous()
-        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd, ctx.eps)
-        return dx.view(ctx.shape).to(ctx.in_dtype), dw.to(w.dtype), None
+        t = gradsink.target(w)
+        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd, ctx.eps, dw_into=t)
+        return dx.view(ctx.shape).to(ctx.in_dtype), _norm_weight_grad(ctx, w, dw, t), None
 
 
 class _RMSNormSkip(torch.autograd.Function):
@@ -154,6 +166,8 @@ class _RMSNormSkip(torch.autograd.Function):
         ctx.shape = x.shape
         ctx.in_dtype = x.dtype
         ctx.eps = eps
+        if ctx.needs_input_grad[1]:
+            gradsink.use([w])
         return y.view(x.shape), x.view_as(x)
 
     @staticmethod
@@ -161,11 +175,14 @@ class _RMSNormSkip(torch.autograd.Function):
         ext = require()
         x2, w, rstd = ctx.saved_tensors
         if dy is None:
+            if ctx.needs_input_grad[1]:
+                gradsink.done(w, False)
             return dskip, None, None
         dy2 = dy.reshape(x2.shape).to(x2.dtype).contiguous()
         add = None if dskip is None else dskip.reshape(x2.shape).to(x2.dtype).contiguous()
-        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd, ctx.eps, add)
-        return dx.view(ctx.shape).to(ctx.in_dtype), dw.to(w.dtype), None
+        t = gradsink.target(w)
+        dx, dw = ext.rmsnorm_bwd(dy2, x2, w.detach().float().contiguous(), rstd, ctx.eps, add, dw_into=t)
+        return dx.view(ctx.shape).to(ctx.in_dtype), _norm_weight_grad(ctx, w, dw, t), None
 
 
 def rms_norm_skip_cuda(x, w, eps=None):
@@ -358,15 +375,26 @@ class _WindowAttn(torch.autograd.Function):
                                        kw.detach().float().contiguous(), gi, scale, ATTN_FWD_IMPL)
         ctx.save_for_backward(qkv2, qw, kw, out, lse)
         ctx.gi, ctx.scale = gi, scale
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            gradsink.use([qw, kw])
         return out
 
     @staticmethod
     def backward(ctx, dout):
         ext = require()
         qkv, qw, kw, out, lse = ctx.saved_tensors
+        # QK-norm weight gradients straight into the optimizer's gradient buffer where possible
+        tq, tk = gradsink.target(qw), gradsink.target(kw)
+        inplace = tq is not None and tk is not None
         dqkv, dqw, dkw = ext.window_attn_bwd(qkv, qw.detach().float().contiguous(),
                                              kw.detach().float().contiguous(), out,
-                                             dout.to(qkv.dtype).contiguous(), lse, ctx.gi, ctx.scale)
+                                             dout.to(qkv.dtype).contiguous(), lse, ctx.gi, ctx.scale,
+                                             dqw_into=tq if inplace else None, dkw_into=tk if inplace else None)
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            gradsink.done(qw, inplace)
+            gradsink.done(kw, inplace)
+        if inplace:
+            return dqkv, None, None, None, None
         return dqkv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None
 
 

@@ -227,6 +227,31 @@ def test_patch_embed_and_head():
     assert rel(hw.grad, hwr.grad) < 3e-2
 
 
+@pytest.mark.parametrize("B,T,h,w,p,C", [(1, 1, 180, 360, 4, 70), (2, 1, 5, 12, 4, 10), (1, 2, 3, 22, 4, 8),
+                                          (1, 1, 4, 7, 2, 6)])
+def test_patch_layout_kernels_exact(B, T, h, w, p, C):
+    """unpatchify / patchify / im2col are pure re-layouts: equal to the PyTorch permutes bit for bit (the
+    tiled shared-memory forms, ragged last tile included, and the per-element fallback)."""
+    from neural_scaling_weather_b200.ops import _ext
+    from neural_scaling_weather_b200.ops.fused import DT
+
+    ext = _ext.require()
+    torch.manual_seed(0)
+    y2 = torch.randn(B * T * h * w, p * p * C, device=DEV).bfloat16()
+    out = ext.unpatchify(y2, B, T, h, w, p, C)
+    ref = y2.view(B, T, h, w, p, p, C).permute(0, 1, 6, 2, 4, 3, 5).reshape(B, T, C, h * p, w * p)
+    assert torch.equal(out, ref)
+    d = torch.randn(B, T, C, h * p, w * p, device=DEV).bfloat16()
+    dy2 = ext.patchify(d, h, w, p, C)
+    refd = d.view(B, T, C, h, p, w, p).permute(0, 1, 3, 5, 4, 6, 2).reshape(B * T * h * w, p * p * C)
+    assert torch.equal(dy2, refd)
+    N = B * T
+    x = torch.randn(N, C, h * p, w * p, device=DEV)
+    cols = ext.im2col(x, p, DT[torch.bfloat16])
+    refc = x.view(N, C, h, p, w, p).permute(0, 2, 4, 1, 3, 5).reshape(N * h * w, C * p * p).bfloat16()
+    assert torch.equal(cols, refc)
+
+
 # --------------------------------------------------------------------------- losses
 def test_weighted_sse():
     torch.manual_seed(0)
