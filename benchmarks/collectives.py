@@ -4,8 +4,10 @@
 (N = 2..8 GPUs of one node).  Shape: a row-parallel projection of the Swin p4-e1024 block
 (64800 tokens, 1024 outputs, 1024 / N inputs per rank) with bias and residual.  Times are CUDA
 events on each rank around several launches, reported as the maximum over ranks; the roofline
-is the slower of the GEMM at the measured bf16 rate and the bytes a rank must pull over NVLink
-(its peers' 16-bit partials, (N - 1) / N of the output) at 770 GB/s per direction.
+is the slower of the GEMM at the measured bf16 rate and the bytes that cross a rank's NVLink in one
+direction (its (N - 1) 16-bit partials pushed to the peers) at 770 GB/s.  By default the launches
+are replayed from one CUDA graph, so the figures are device time without host launch gaps
+(``--graph 0``: eager launches).
 """
 
 from __future__ import annotations
@@ -28,6 +30,7 @@ def main():
     ap.add_argument("--N", type=int, default=1024)
     ap.add_argument("--K", type=int, default=1024, help="full input width (split over the ranks)")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--graph", type=int, default=1, help="1: time the launches replayed from a CUDA graph")
     a = ap.parse_args()
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -54,21 +57,39 @@ def main():
         dist.all_reduce(y, group=comm.get_group("tp"))
         return y + b.detach().bfloat16() + res
 
+    def gemm_only():  # the local GEMM with the same epilogue, no reduction: the compute part alone
+        return ext.gemm(x, wb, b.detach(), res)
+
     out = {}
-    for name, fn in (("fused", fused), ("gemm_then_nccl", baseline)):
+    for name, fn in (("fused", fused), ("gemm_then_nccl", baseline), ("gemm_only", gemm_only)):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
         dist.barrier()
+        run = lambda: [fn() for _ in range(a.iters)]  # noqa: E731
+        if a.graph:  # the launches replay from one CUDA graph: device time, no host launch gaps
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    run()
+            torch.cuda.current_stream().wait_stream(s)
+            g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            run = g.replay
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(a.iters):
-            fn()
+        run()
         e1.record()
         torch.cuda.synchronize()
         ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         out[name] = round(ms.item(), 4)
+        if a.graph:
+            del g
+            torch.cuda.synchronize()
     assert ext.read_error_flag(True) == 0
     flops = 2.0 * M * N * K
     peer_bytes = (world - 1) * M * N * 2
@@ -76,6 +97,7 @@ def main():
     if rank == 0:
         print(json.dumps({"op": "row-parallel linear + all-reduce", "world": world, "M": M, "N": N, "K_per_rank": K,
                           "fused_ms": out["fused"], "gemm_then_nccl_ms": out["gemm_then_nccl"],
+                          "gemm_only_ms": out["gemm_only"], "graph": bool(a.graph),
                           "roofline_ms": round(roof_ms, 4), "fused_of_roofline": round(roof_ms / out["fused"], 3)}))
     symm.reset()
     comm.reset()

@@ -119,9 +119,11 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, doub
 // ------------------------------------------------------------------------------ GEMM + all-reduce
 // D = sum over the ranks of A_r B_r^T (+ bias + residual), the reduction done in the GEMM's
 // epilogue over NVLink peer memory.  part_ptrs / flag_ptrs: every rank's symmetric partial
-// buffer (>= M * N elements of A's dtype) and flag words, in rank order; rank: this rank.
+// buffer (one [M, N] slot per rank: >= W * M * N elements of A's dtype) and flag words, in rank
+// order; rank: this rank.
 Tensor gemm_allreduce(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optional<Tensor> residual,
-                      std::vector<int64_t> part_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank) {
+                      std::vector<int64_t> part_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                      c10::optional<Tensor> stamps) {
   need_cuda(A, "A");
   need_cuda(B, "B");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_allreduce: A [M,K], B [N,K]");
@@ -158,6 +160,11 @@ Tensor gemm_allreduce(Tensor A, Tensor B, c10::optional<Tensor> bias, c10::optio
   for (int r = 0; r < g.ar_world; ++r) {
     g.ar_part[r] = reinterpret_cast<void*>(part_ptrs[r]);
     g.ar_flags[r] = reinterpret_cast<uint32_t*>(flag_ptrs[r]);
+  }
+  if (stamps) {
+    TORCH_CHECK(stamps->is_cuda() && stamps->scalar_type() == at::kLong && stamps->numel() >= 4 * 32 * 8,
+                "gemm_allreduce: stamps must be an int64 CUDA tensor of >= 1024 elements");
+    g.ar_stamps = reinterpret_cast<long long*>(stamps->data_ptr<int64_t>());
   }
   TORCH_CHECK(nsw::gemm_tcgen05_supported(g), "gemm_allreduce: shape/alignment not supported");
   check(nsw::gemm_tcgen05(g, stream(), 1), "gemm_allreduce");
@@ -783,7 +790,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha") = 1.0, py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("impl") = 0);
   m.def("gemm_supported", &gemm_supported);
   m.def("gemm_allreduce", &gemm_allreduce, py::arg("A"), py::arg("B"), py::arg("bias") = py::none(),
-        py::arg("residual") = py::none(), py::arg("part_ptrs"), py::arg("flag_ptrs"), py::arg("rank"));
+        py::arg("residual") = py::none(), py::arg("part_ptrs"), py::arg("flag_ptrs"), py::arg("rank"),
+        py::arg("stamps") = py::none());
   m.def("bias_act_residual", &bias_act_residual);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("col_sum", &col_sum);

@@ -178,6 +178,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -234,10 +238,12 @@ struct EpiParams {
   int accumulate;
   float alpha;
   // Tensor-parallel all-reduce fused into the epilogue (ar_world > 1; 16-bit D, no
-  // pre-activation / GELU): each rank's CTA drains its tile as a 16-bit partial into its own
-  // symmetric buffer ar_part[rank], releases the accumulator, publishes a per-tile ready flag to
-  // every peer, and once all ranks' partials of the tile are published sums them with peer
-  // loads over NVLink before bias / residual / store.  Flags (uint32 words): [0] the epoch of
+  // pre-activation / GELU).  Every rank's symmetric buffer ar_part[r] has one [M, N] slot per rank
+  // (slot s at s * M * N).  Each rank's CTA drains its tile as a 16-bit partial into slot `rank` of
+  // its own buffer, releases the accumulator, pushes the tile with plain stores into slot `rank`
+  // of every peer's buffer (posted NVLink writes: no warp waits on a remote round trip), publishes
+  // a per-tile ready flag to every peer, and, once every peer's flag for the tile is seen, sums the
+  // W slots of its own buffer (local reads only) before bias / residual / store.  Flags (uint32 words): [0] the epoch of
   // the last finished launch, [1] CTAs of this rank that finished (all launches), [2 + r] CTAs
   // of rank r that finished reading this rank's partials (all launches), [kArFlagBase + r * tiles
   // + t] the epoch in which rank r published its partial of tile t.  Epochs increase by one per
@@ -247,6 +253,7 @@ struct EpiParams {
   int64_t ar_tiles;
   void* ar_part[8];
   uint32_t* ar_flags[8];
+  long long* ar_stamps;  // phase timestamps (nullptr: off)
 };
 constexpr int kArFlagBase = 16;
 
@@ -484,12 +491,12 @@ struct EpiWarp {
     ++ring;
   }
 
-  // All-reduce mode, step 1: this warp's part of the accumulator as a 16-bit partial in the
-  // rank's own symmetric buffer (this lane's row, 64 contiguous bytes per 32-column chunk).
+  // All-reduce mode, step 1: this warp's part of the accumulator as a 16-bit partial in slot `rank`
+  // of the rank's own symmetric buffer (this lane's row, 64 contiguous bytes per 32-column chunk).
   __device__ __forceinline__ void drain_partial(const EpiParams& ep, uint32_t t_row, int64_t row_base, int64_t n0,
                                                 int half, int lane) {
     const int64_t row = row_base + lane;
-    T* part = reinterpret_cast<T*>(ep.ar_part[ep.ar_rank]);
+    T* part = reinterpret_cast<T*>(ep.ar_part[ep.ar_rank]) + (int64_t)ep.ar_rank * ep.M * ep.N;
 #pragma unroll
     for (int cc = 0; cc < kChunks; ++cc) {
       const int c = half * kChunks + cc;
@@ -506,19 +513,58 @@ struct EpiWarp {
     }
   }
 
-  // All-reduce mode, step 2 (all ranks' partials of the tile published): sum them, add bias and
-  // residual, store D.  The warp's block is rows [row_base, row_base + 32) x columns
-  // [n0 + half * BN/2, n0 + (half + 1) * BN/2); lanes walk it row-contiguously (16 bytes each, a row
-  // half of 128 columns is 16 lanes), so every peer load is part of a whole 256-byte row segment
-  // over NVLink.  Two rows per lane are in flight at once, each with the values of every rank, and
-  // the sum runs in rank order 0 .. W-1 on every rank, so all ranks store identical results.
+  // All-reduce mode, step 2: copy this warp's block of the partial (rows [row_base, row_base + 32) x
+  // columns [n0 + half * BN/2, n0 + (half + 1) * BN/2), just written to the own slot and still in L2)
+  // into slot `rank` of every peer's buffer.  Lanes walk the block row-contiguously (16 bytes each, a
+  // 128-column row half is 16 lanes), so each warp store is two whole 256-byte row segments over
+  // NVLink; eight rows' loads are in flight per lane before their stores.  The stores are posted
+  // (nothing waits for them here); the caller fences them system-wide before the tile's flag is
+  // published, after other work has given them time to land.
+  __device__ __forceinline__ void push_partial(const EpiParams& ep, int64_t row_base, int64_t n0, int half,
+                                               int lane) {
+    constexpr int kLanesPerRow = (BN / 2) * (int)sizeof(T) / 16;
+    constexpr int kRowsPerStep = 32 / kLanesPerRow;
+    constexpr int kUnroll = 4;
+    const int64_t col = n0 + half * (BN / 2) + (lane % kLanesPerRow) * 8;
+    const int64_t slot = (int64_t)ep.ar_rank * ep.M * ep.N;
+    const T* own = reinterpret_cast<const T*>(ep.ar_part[ep.ar_rank]) + slot;
+#pragma unroll 1
+    for (int r0 = 0; r0 < 32; r0 += kRowsPerStep * kUnroll) {
+      uint4 v[kUnroll];
+      int64_t off[kUnroll];
+      bool ok[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t row = row_base + r0 + u * kRowsPerStep + lane / kLanesPerRow;
+        ok[u] = col < ep.N && row < ep.M;
+        off[u] = row * ep.N + col;
+        if (ok[u]) v[u] = *reinterpret_cast<const uint4*>(own + off[u]);
+      }
+#pragma unroll
+      for (int q = 1; q < 8; ++q) {
+        if (q >= ep.ar_world) break;
+        const int r = (ep.ar_rank + q) % ep.ar_world;
+        T* dst = reinterpret_cast<T*>(ep.ar_part[r]) + slot;
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (ok[u]) *reinterpret_cast<uint4*>(dst + off[u]) = v[u];
+      }
+    }
+  }
+
+  // All-reduce mode, step 3 (every rank's partial of the tile is in this rank's slots): sum the W
+  // slots of the own buffer (local reads, past L1), add bias and residual, store D.  Same block and
+  // lane walk as push_partial; two rows per lane are in flight at once, each with every slot, and the
+  // sum runs in rank order 0 .. W-1 on every rank, so all ranks store identical results.
   __device__ __forceinline__ void reduce_store(const EpiParams& ep, int64_t row_base, int64_t n0, int half,
                                                int lane) {
     constexpr int kLanesPerRow = (BN / 2) * (int)sizeof(T) / 16;  // 16-byte pieces in a row half
     constexpr int kRowsPerStep = 32 / kLanesPerRow;
-    constexpr int kUnroll = 2;
+    constexpr int kUnroll = 4;  // row steps per round: 8 rows of this warp's block per lane group
     const int64_t col = n0 + half * (BN / 2) + (lane % kLanesPerRow) * 8;
     const bool col_ok = col < ep.N;
+    const int64_t slot = ep.M * ep.N;
+    const T* mine = reinterpret_cast<const T*>(ep.ar_part[ep.ar_rank]);
     float b[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) b[i] = 0.f;
@@ -529,46 +575,59 @@ struct EpiWarp {
     }
 #pragma unroll 1
     for (int r0 = 0; r0 < 32; r0 += kRowsPerStep * kUnroll) {
-      uint4 v[kUnroll][8];
-      uint4 res[kUnroll];
-      int64_t rows[kUnroll];
+      int64_t off[kUnroll], rows[kUnroll];
       bool ok[kUnroll];
+      uint4 res[kUnroll], s0[kUnroll], s1[kUnroll];
+      float f[kUnroll][8];
+      // slots 0 and 1 and the residual of kUnroll row steps in flight at once (one round trip for
+      // two ranks); further slots follow one by one.  The sum runs in rank order 0 .. W-1, the same
+      // on every rank.
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        rows[u] = row_base + r0 + u * kRowsPerStep + lane / kLanesPerRow;
-        ok[u] = col_ok && rows[u] < ep.M;
-        const int64_t off = rows[u] * ep.N + col;
+        const int64_t row = row_base + r0 + u * kRowsPerStep + lane / kLanesPerRow;
+        rows[u] = row;
+        ok[u] = col_ok && row < ep.M;
+        off[u] = row * ep.N + col;
+        if (ok[u]) {
+          s0[u] = __ldcg(reinterpret_cast<const uint4*>(mine + off[u]));
+          s1[u] = __ldcg(reinterpret_cast<const uint4*>(mine + slot + off[u]));
+          if (ep.residual)
+            res[u] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
+                                                         (row % ep.res_period) * ep.ldr + col));
+        }
+      }
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
-          if (r < ep.ar_world && ok[u]) v[u][r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.ar_part[r]) + off);
-        if (ep.residual && ok[u])
-          res[u] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ep.residual) +
-                                                       (rows[u] % ep.res_period) * ep.ldr + col));
+      for (int u = 0; u < kUnroll; ++u) {
+        float x[8], y[8];
+        unpack8<T>(s0[u], x);
+        unpack8<T>(s1[u], y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[u][i] = x[i] + y[i];
+      }
+      for (int r = 2; r < ep.ar_world; ++r) {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (ok[u]) s0[u] = __ldcg(reinterpret_cast<const uint4*>(mine + (int64_t)r * slot + off[u]));
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          float x[8];
+          unpack8<T>(s0[u], x);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[u][i] += x[i];
+        }
       }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         if (!ok[u]) continue;
-        float f[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = 0.f;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          if (r < ep.ar_world) {
-            float x[8];
-            unpack8<T>(v[u][r], x);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) f[i] += x[i];
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] += b[i];
+        for (int i = 0; i < 8; ++i) f[u][i] += b[i];
         if (ep.residual) {
           float x[8];
           unpack8<T>(res[u], x);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] += x[i];
+          for (int i = 0; i < 8; ++i) f[u][i] += x[i];
         }
-        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + rows[u] * ep.ldd + col) = pack8<T>(f);
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ep.D) + rows[u] * ep.ldd + col) = pack8<T>(f[u]);
       }
     }
   }
@@ -637,14 +696,19 @@ struct Smem {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t res_full[EW];  // RT: a warp's residual tiles landed
+  uint64_t pushed[2];     // all-reduce: every epilogue warp has pushed the tile (alternate tiles)
+  uint64_t published[2];  // all-reduce: the publisher warp has published that tile's flag
   alignas(1024) T stage[EW][kBufs * 32 * kStageRow];
   uint32_t tmem_base;
   int abort_flag;
   int epi_stop;  // all-reduce epilogue: written by its leader only, read after a named barrier
 };
 
-template <typename T, int BN, int STAGES, bool RT, int EW>
-__global__ void __launch_bounds__(64 + 32 * EW, 1)
+// PUB: the fused tensor-parallel all-reduce form, with one more warp (the publisher, after the
+// epilogue warps) that fences each tile's pushed partials system-wide and publishes its flag, so the
+// epilogue warps never wait for a system-scope fence.
+template <typename T, int BN, int STAGES, bool RT, int EW, bool PUB = false>
+__global__ void __launch_bounds__(64 + 32 * EW + (PUB ? 32 : 0), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 int64_t M, int64_t N, int64_t K, const __grid_constant__ EpiParams ep, uint32_t idesc,
                 int* err) {
@@ -670,6 +734,10 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       mbar_init(&S.tmem_empty[a], EW);
     }
     for (int w = 0; w < EW; ++w) mbar_init(&S.res_full[w], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S.pushed[b], EW);
+      mbar_init(&S.published[b], 1);
+    }
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
@@ -744,7 +812,24 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         }
       }
     }
-  } else if (EW == 8 && ep.ar_world > 1) {
+  } else if (PUB && warp == 2 + EW) {
+    // ------------------------------------------------------------------ publisher (all-reduce)
+    // tile i of this CTA: once every epilogue warp has pushed it (pushed[i & 1], its (i >> 1)-th
+    // phase), one system fence orders those stores (cumulatively, through the mbarrier's release /
+    // acquire) before the tile's ready flag in every peer's flag words
+    if (lane == 0) {
+      uint32_t* my_flags = ep.ar_flags[ep.ar_rank];
+      const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_flags) + 1u;
+      int64_t i = 0;
+      for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+        if (!mbar_wait(&S.pushed[i & 1], (uint32_t)((i >> 1) & 1), abort_flag, err)) break;
+        fence_acq_rel_sys();  // with the relaxed flag store below: a release at system scope
+        for (int r = 0; r < ep.ar_world; ++r)
+          if (r != ep.ar_rank) st_relaxed_sys(ep.ar_flags[r] + kArFlagBase + ep.ar_rank * ep.ar_tiles + tile, epoch);
+        mbar_arrive(&S.published[i & 1]);
+      }
+    }
+  } else if (PUB) {
     // ------------------------------------------------------------------ epilogue + all-reduce
     const int ew = warp - 2;
     const int q = warp & 3;
@@ -759,17 +844,28 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     bool ok = true;
     if (leader) S.epi_stop = 0;
     epi_sync();
-    // Tile t's partial is drained and published, then the previous tile of this CTA is reduced: the
-    // peers have had a whole tile's time to publish their partials of it, so the flag wait rarely
-    // stalls.  Every iteration takes exactly two epilogue barriers and all warps leave on the
-    // leader's decision (S.epi_stop), so no warp is left waiting at a barrier.
+    // Per tile t: drain the accumulator into the own slot, push it into every peer's slot (posted
+    // stores), reduce the previous tile of this CTA (the peers have had a whole tile's time to
+    // deliver it, so the flag wait rarely stalls, and this tile's stores drain over NVLink
+    // meanwhile), fence, publish tile t's flag.  Every iteration takes exactly two epilogue
+    // barriers and all warps leave on the leader's decision (S.epi_stop), so no warp is left
+    // waiting at a barrier.
     int64_t prev = -1;
-    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    int it = 0;
+    // phase stamps (diagnostics): the leader of CTAs 0..3 records eight times per tile
+    long long* stamp = (ep.ar_stamps && blockIdx.x < 4 && leader) ? ep.ar_stamps + (int64_t)blockIdx.x * 32 * 8
+                                                                   : nullptr;
+    auto mark = [&](int phase) {
+      if (stamp && it < 32) stamp[it * 8 + phase] = (long long)globaltimer();
+    };
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int64_t m0 = (tile / n_tiles) * BM;
       const int64_t n0 = (tile % n_tiles) * BN;
       const int64_t row_base = m0 + q * 32;
       EpiWarp<T, BN> epi;
+      mark(0);
       const bool have = mbar_wait(&S.tmem_full[acc], acc_phase, abort_flag, err);
+      mark(1);
       if (have) {
         tc_fence_after();
         epi.drain_partial(ep, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row_base, n0, half,
@@ -784,26 +880,36 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         acc = 0;
         acc_phase ^= 1;
       }
-      epi_sync();  // the whole tile's partial is written
+      mark(2);
+      if (have) epi.push_partial(ep, row_base, n0, half, lane);  // posted stores, not yet fenced
+      mark(3);
+      // the previous tile: once every peer's partial of it has arrived, reduce it (while this
+      // tile's pushed stores drain over NVLink)
       if (leader) {
         bool go = !*abort_flag;
-        if (go) {
-          __threadfence_system();
-          for (int r = 0; r < ep.ar_world; ++r)
-            if (r != ep.ar_rank) st_release_sys(ep.ar_flags[r] + kArFlagBase + ep.ar_rank * ep.ar_tiles + tile, epoch);
-          if (prev >= 0)
-            for (int r = 0; r < ep.ar_world && go; ++r)
-              if (r != ep.ar_rank) go = wait_flag_geq(my_flags + kArFlagBase + r * ep.ar_tiles + prev, epoch, err);
-          if (!go) *abort_flag = 1;
-        }
+        if (go && prev >= 0)
+          for (int r = 0; r < ep.ar_world && go; ++r)
+            if (r != ep.ar_rank) go = wait_flag_geq(my_flags + kArFlagBase + r * ep.ar_tiles + prev, epoch, err);
+        if (!go) *abort_flag = 1;
         S.epi_stop = go ? 0 : 1;
       }
       epi_sync();
+      mark(4);
       if (*reinterpret_cast<volatile int*>(&S.epi_stop)) {
         ok = false;
         break;
       }
       if (prev >= 0) epi.reduce_store(ep, (prev / n_tiles) * BM + q * 32, (prev % n_tiles) * BN, half, lane);
+      mark(5);
+      // hand this tile's pushes to the publisher warp (its fence and flag); the barrier it reuses two
+      // tiles later must have been consumed first (never waits in practice)
+      __syncwarp();
+      if (lane == 0 && have) {
+        bool fine = it < 2 || mbar_wait(&S.published[it & 1], (uint32_t)(((it >> 1) - 1) & 1), abort_flag, err);
+        if (fine) mbar_arrive(&S.pushed[it & 1]);
+      }
+      mark(6);
+      mark(7);
       prev = tile;
     }
     if (ok && prev >= 0) {  // the last tile of this CTA
@@ -1197,6 +1303,7 @@ static EpiParams epi_params(const GemmArgs& a) {
     ep.ar_part[r] = r < a.ar_world ? a.ar_part[r] : nullptr;
     ep.ar_flags[r] = r < a.ar_world ? a.ar_flags[r] : nullptr;
   }
+  ep.ar_stamps = a.ar_stamps;
   return ep;
 }
 
@@ -1239,8 +1346,9 @@ static cudaError_t launch2(const GemmArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <typename T, int BN, int STAGES, bool RT = false, int EW = 8>
+template <typename T, int BN, int STAGES, bool RT = false, int EW = 8, bool PUB = false>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
+  if (PUB != (a.ar_world > 1)) return cudaErrorInvalidValue;  // the all-reduce form and only it
   CUtensorMap ma, mb;
   if (!make_map(&ma, a.A, a.M, a.K, a.lda, BM, a.dtype)) return cudaErrorInvalidValue;
   if (!make_map(&mb, a.B, a.N, a.K, a.ldb, BN, a.dtype)) return cudaErrorInvalidValue;
@@ -1252,10 +1360,10 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t s) {
   const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                          ((uint32_t)(BM >> 4) << 24);
   const size_t smem = sizeof(Smem<T, BN, STAGES, RT, EW>) + 1024;
-  auto k = gemm_kernel<T, BN, STAGES, RT, EW>;
+  auto k = gemm_kernel<T, BN, STAGES, RT, EW, PUB>;
   NSW_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-  const int threads = 64 + 32 * EW;
+  const int threads = 64 + 32 * EW + (PUB ? 32 : 0);
   static int resident = 0;  // co-resident CTAs of this kernel on the whole device
   if (!resident) {
     int per_sm = 0;
@@ -1830,6 +1938,12 @@ cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl) {
   // 64800 x 4096 x 1024 (0.538 against 0.548 ms for GELU, 0.614 against 0.581 ms for GELU' with
   // the TMA residual), so eight is the default
   const bool gelu12 = impl == 4 && wide && !pair && a.ar_world <= 1 && (a.act == 1 || a.act == 2);
+  if (a.ar_world > 1) {  // the fused all-reduce form (publisher warp)
+    if (a.dtype == kBF16)
+      return wide ? tc::launch<__nv_bfloat16, 256, 4, false, 8, true>(a, s)
+                  : tc::launch<__nv_bfloat16, 128, 6, false, 8, true>(a, s);
+    return wide ? tc::launch<__half, 256, 4, false, 8, true>(a, s) : tc::launch<__half, 128, 6, false, 8, true>(a, s);
+  }
   if (a.dtype == kBF16) {
     if (pair) return tc::launch2<__nv_bfloat16, 6>(a, s);
     if (rt) return gelu12 ? tc::launch<__nv_bfloat16, 256, 3, true, 12>(a, s) : tc::launch<__nv_bfloat16, 256, 3, true>(a, s);

@@ -121,11 +121,15 @@ struct GemmArgs {
   float alpha;
   int accumulate;       // D += result (fp32 output only)
   // tensor-parallel all-reduce fused into the epilogue (ar_world > 1): ar_part[r] / ar_flags[r]
-  // are rank r's symmetric partial buffer ([M, N] in dtype) and flag words (peer pointers)
+  // are rank r's symmetric partial buffer (ar_world slots of [M, N] in dtype, slot s receiving
+  // rank s's partial) and flag words (peer pointers)
   int ar_world;
   int ar_rank;
   void* ar_part[8];
   uint32_t* ar_flags[8];
+  // optional (nullptr: off): %globaltimer stamps of the fused all-reduce epilogue's phases, eight per
+  // tile for the first 32 tiles of CTAs 0..3, at [(cta * 32 + i) * 8 + phase]
+  long long* ar_stamps;
 };
 cudaError_t gemm_tcgen05(const GemmArgs& a, cudaStream_t s, int impl = 0);
 int gemm_tcgen05_supported(const GemmArgs& a);

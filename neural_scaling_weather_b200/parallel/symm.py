@@ -61,8 +61,8 @@ def disable(group_name: str, why: str) -> None:
 
 
 def allreduce_buffers(group_name: str, m: int, n: int, dtype: torch.dtype, device: torch.device) -> ARBuffers:
-    """Partial buffer ([m * n] of ``dtype``) and zeroed flag words for a fused all-reduce of an
-    [m, n] output over ``group_name``; a collective on first use of a shape (all ranks call it
+    """Partial buffer (one [m, n] slot of ``dtype`` per rank: slot s receives rank s's partial) and
+    zeroed flag words for a fused all-reduce of an [m, n] output over ``group_name``; a collective on first use of a shape (all ranks call it
     in the same order)."""
     key = (group_name, m, n, dtype, device.index)
     hit = _BUFS.get(key)
@@ -73,7 +73,7 @@ def allreduce_buffers(group_name: str, m: int, n: int, dtype: torch.dtype, devic
     group = comm.get_group(group_name)
     world = comm.get_size(group_name)
     tiles = math.ceil(m / 128) * math.ceil(n / 128)  # upper bound over the kernel's tile widths
-    part = symm.empty(m * n, dtype=dtype, device=device)
+    part = symm.empty(world * m * n, dtype=dtype, device=device)  # one [m, n] slot per rank
     flags = symm.empty(FLAG_BASE + world * tiles, dtype=torch.int32, device=device)
     flags.zero_()
     hp = symm.rendezvous(part, group)
