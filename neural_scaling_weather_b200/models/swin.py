@@ -4,7 +4,7 @@ Architecture and parameter layout follow the reference (``models/swin.py:36-323`
 ``models/swin_helpers.py:80-459``, ``models/mlp.py:14-95``):
 
 * patch embedding (``Conv2d`` k = s = p) plus a coordinate positional embedding (a second
-  patch projection of the (x, y, z, t) coordinate field, recomputed every forward) or a
+  patch projection of the (x, y, z, t) coordinate field, on CUDA computed once per weight version) or a
   learned, sp-sharded positional tensor;
 * ``depth`` blocks of RMSNorm -> shifted-window multi-head attention with QK-RMSNorm
   -> residual -> RMSNorm -> GELU MLP -> residual; shift 0 on even blocks and half the
@@ -287,6 +287,8 @@ class SwinTransformer(nn.Module):
         t = torch.linspace(0, 1, T).view(T, 1, 1, 1).expand(T, H, W, 1)
         coords = torch.cat([spatial.unsqueeze(0).expand(T, H, W, -1).float(), t], dim=-1)
         self.register_buffer("coords", coords, persistent=False)  # (T, H, W, 4)
+        # the same field channels-first and contiguous: one tensor that the cached projection keys on
+        self.register_buffer("coords_nchw", coords.permute(0, 3, 1, 2).contiguous(), persistent=False)
 
     @staticmethod
     def _init_weights(m):
@@ -304,7 +306,8 @@ class SwinTransformer(nn.Module):
     def prepare_tokens(self, x):
         b, t, c, h, w = x.shape
         if self.coord_pos_embed:
-            pos = self.pos_embed(self.coords.permute(0, 3, 1, 2))  # (T, h', w', E)
+            conv = self.pos_embed.proj.conv
+            pos = ops.coord_pos_embed(self.coords_nchw, conv.weight, conv.bias, self.patch_size)  # (T, h', w', E)
         else:
             pos = self.pos_embed[0]
         tok = self.patch_embed.proj.conv

@@ -161,6 +161,17 @@ def patch_embed(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tens
     return patch_embed_cuda(x, weight, bias, patch_size, add)
 
 
+def coord_pos_embed(coords: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+                    patch_size: int) -> torch.Tensor:
+    """Patch projection of a constant coordinate field (T, 4, H, W) -> (T, h, w, E): on CUDA computed
+    once per weight version and reused by every forward until the next optimizer step."""
+    if not _use_cuda(coords):
+        return reference.patch_embed(coords, weight, bias, patch_size)
+    from .fused import coord_pos_embed_cuda
+
+    return coord_pos_embed_cuda(coords, weight, bias, patch_size)
+
+
 def head_unpatchify(x: torch.Tensor, weight: torch.Tensor, patch_size: int, out_chans: int):
     """(B, T, h, w, E) -> (B, T, C, h*p, w*p)."""
     if not _use_cuda(x):

@@ -13,7 +13,8 @@ not a multiple of 8: only tiny test models) use cuBLAS plus the fused epilogue k
 from __future__ import annotations
 
 import os
-from typing import List, Optional, Sequence
+import weakref
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -457,6 +458,65 @@ class _PatchEmbed(torch.autograd.Function):
 
 def patch_embed_cuda(x, weight, bias, patch_size, add=None):
     return _PatchEmbed.apply(x, weight, bias, add, int(patch_size))
+
+
+# ---------------------------------------------------------------------------- coordinate positional embedding
+# patch columns of constant coordinate fields: key -> (weak reference to the field, its columns)
+_COORD_COLS: Dict[Tuple, Tuple["weakref.ref", torch.Tensor]] = {}
+
+
+def _coord_cols(coords: torch.Tensor, p: int, dt: torch.dtype) -> torch.Tensor:
+    key = (id(coords), coords.data_ptr(), tuple(coords.shape), p, dt)
+    hit = _COORD_COLS.get(key)
+    if hit is not None and hit[0]() is coords:
+        return hit[1]
+    cols = require().im2col(coords.contiguous(), p, DT[dt])
+    for k in [k for k, v in _COORD_COLS.items() if v[0]() is None]:  # fields of models that are gone
+        del _COORD_COLS[k]
+    _COORD_COLS[key] = (weakref.ref(coords), cols)
+    return cols
+
+
+class _CoordPosEmbed(torch.autograd.Function):
+    """The coordinate positional embedding: a patch projection of the model's constant (T, 4, H, W)
+    coordinate field (reference ``models/swin.py:270-284``, which re-runs the projection in every
+    forward).  The field never changes, so its patch columns are built once; the projection depends
+    only on the weights, so it is computed once per weight version (``ops.weights.get_derived``: a
+    cache hit while the parameters' versions are unchanged, rebuilt in place after each optimizer step
+    for captured CUDA graphs) instead of once per micro-batch.  The backward is the projection's
+    weight and bias gradient from the cached columns."""
+
+    @staticmethod
+    def forward(ctx, coords, w, b, p):
+        dt = _cdtype(coords)
+        cols = _coord_cols(coords, p, dt)
+        T, _, H, Wd = coords.shape
+        h, wn, E = H // p, Wd // p, w.shape[0]
+
+        def build():
+            return gemm(cols, wcache.get(w, dt).reshape(E, -1), b.detach().float() if b is not None else None
+                        ).view(T, h, wn, E)
+
+        pos = wcache.get_derived(("coord_pos", p, dt, tuple(coords.shape), coords.data_ptr()),
+                                 [w] + ([b] if b is not None else []), build)
+        ctx.save_for_backward(cols)
+        ctx.w_param, ctx.b_param, ctx.E = w, b, E
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            gradsink.use([w] + ([b] if b is not None else []))
+        return pos.view_as(pos)
+
+    @staticmethod
+    def backward(ctx, dpos):
+        (cols,) = ctx.saved_tensors
+        dy = dpos.reshape(-1, ctx.E).to(cols.dtype).contiguous()
+        gw, gb = weight_grads(dy, cols, [ctx.w_param], [ctx.b_param] if ctx.b_param is not None else [])
+        dW = None if gw[0] is None else gw[0].view(ctx.w_param.shape).to(ctx.w_param.dtype)
+        db = gb[0] if ctx.b_param is not None else None
+        return None, dW, db, None
+
+
+def coord_pos_embed_cuda(coords, weight, bias, patch_size):
+    return _CoordPosEmbed.apply(coords, weight, bias, int(patch_size))
 
 
 # ---------------------------------------------------------------------------- head

@@ -87,6 +87,22 @@ def refresh_derived() -> None:
         _cache.pop(key, None)
 
 
+def get_derived(key: Tuple, params: Sequence[torch.Tensor], build: Callable[[], torch.Tensor]) -> torch.Tensor:
+    """A tensor computed from ``params`` only (``build`` runs without autograd), cached on their
+    versions and rebuilt in place by ``refresh_derived`` after each optimizer step."""
+    ps = list(params)
+    full = ("D",) + tuple(key) + tuple(id(p) for p in ps)
+    t = _lookup(full, ps)
+    if t is not None:
+        return t
+
+    def rebuild():
+        with torch.no_grad():
+            return build()
+
+    return _store(full, ps, rebuild(), rebuild)
+
+
 def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """``param`` in ``dtype`` (a registered shadow, or a version-cached cast)."""
     if param.dtype == dtype:

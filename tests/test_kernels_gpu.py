@@ -252,6 +252,36 @@ def test_patch_layout_kernels_exact(B, T, h, w, p, C):
     assert torch.equal(cols, refc)
 
 
+def test_coord_pos_embed_cached_per_weight_version():
+    """The coordinate positional embedding equals the plain patch projection (values and weight / bias
+    gradients), is served from the cache while the weights are unchanged, and is rebuilt after an
+    in-place weight update (version bump)."""
+    torch.manual_seed(0)
+    T, H, W, p, E = 1, 24, 48, 4, 64
+    coords = torch.randn(T, 4, H, W, device=DEV)
+    w = torch.nn.Parameter(0.05 * torch.randn(E, 4, p, p, device=DEV))
+    b = torch.nn.Parameter(torch.randn(E, device=DEV))
+    wr, br = (torch.nn.Parameter(t.detach().clone()) for t in (w, b))
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        a = ops.coord_pos_embed(coords, w, b, p)
+        r = ops.patch_embed(coords, wr, br, p)
+    assert a.shape == r.shape and rel(a, r) < 1e-2
+    g = torch.randn_like(r.float())
+    a.backward(g.to(a.dtype))
+    r.backward(g.to(r.dtype))
+    assert rel(w.grad, wr.grad) < 2e-2 and rel(b.grad, br.grad) < 2e-2
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        a2 = ops.coord_pos_embed(coords, w, b, p)
+    assert a2.data_ptr() == a.data_ptr()  # cache hit: no recomputation
+    with torch.no_grad():
+        w.add_(0.01)
+        wr.add_(0.01)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        a3 = ops.coord_pos_embed(coords, w, b, p)
+        r3 = ops.patch_embed(coords, wr, br, p)
+    assert rel(a3, r3) < 1e-2 and rel(a3, a) > 1e-3
+
+
 # --------------------------------------------------------------------------- losses
 def test_weighted_sse():
     torch.manual_seed(0)
