@@ -337,7 +337,7 @@ def inference_bench(args, rank, world, local):
         "inference.start_date=2020-01-01T00", "inference.end_date=2020-01-08T12",
         "inference.time_horizon_in_hours=240", "inference.precision=bf16",
         "inference.checkpoint=/tmp/nsw_bench_no_checkpoint.tar", "inference.checkpoint_hyperparams=null",
-        "inference.run_benchmark=true",
+        "inference.random_init=true",
         # random-init weights diverge within a few steps: keep every IC in the scores instead of dropping
         # the "unstable" ones (the default threshold drops all of them)
         "inference.unstable_rmse_threshold=1e30",

@@ -10,6 +10,10 @@ field (``:337-464``); at the end unstable ICs (channel-0 RMSE > 10) are dropped,
 all-reduced over dp and averaged, and ``rmse_{ch}.npy`` / ``spectra_{ch}_{lt}h.npy`` are
 written (``:466-560``).
 
+``inference.run_benchmark`` (``graphcast`` / ``hres``) scores a WeatherBench2 forecast in place of
+the model (``inference/benchmarks.py``); ``inference.random_init`` runs without a checkpoint
+(random-init weights, for benchmarks of the rollout itself).
+
 Additions: a latitude-weighted anomaly correlation (ACC) per channel and lead, the choice
 of compute precision (``inference.precision``: ``fp32`` as in the reference, computed with
 the plain-PyTorch operators on the GPU, or ``bf16`` / ``fp16`` for the fused kernels) and
@@ -36,11 +40,15 @@ from ..parallel.mappings import allgather_forward_split_backward
 from ..training.trainer import experiment_dir
 from ..utils.checkpoint_io import verified_load
 from ..utils.sht import DistributedRealSHT, power_spectrum_distributed
+from . import benchmarks
 
 
 class Inferencer:
-    def __init__(self, cfg):
+    def __init__(self, cfg, bench_source=None):
+        """``bench_source``: a :class:`~.benchmarks.ForecastSource` to score instead of the one
+        ``inference.run_benchmark`` names (for stores already opened, or other providers)."""
         self.cfg = cfg
+        self.bench_source = bench_source
         self.exp_dir = experiment_dir(cfg)
         comm.init(cfg, timeout_s=float(os.environ.get("NSW_PG_TIMEOUT_S", 600)))
         self.world_size = comm.get_world_size()
@@ -67,7 +75,8 @@ class Inferencer:
             if self.log_to_screen:
                 logging.info(f"Loaded trained model's config from {hp}")
         if self.world_rank == 0:
-            if not os.path.isfile(self.checkpoint_file) and not self.cfg.inference.run_benchmark:
+            random_ok = bool(self.cfg.inference.get("random_init", False))
+            if not os.path.isfile(self.checkpoint_file) and not self.cfg.inference.run_benchmark and not random_ok:
                 raise FileNotFoundError(f"Checkpoint file not found at {self.checkpoint_file}")
             os.makedirs(exp_dir, exist_ok=True)
 
@@ -110,13 +119,21 @@ class Inferencer:
         # spectra from the distributed SHT: no rank gathers the globe
         self.sht = (DistributedRealSHT(self.n_lat, self.n_lon, md["sp_shapes"][0], md["sp_shapes"][1])
                     if self.spectra_times_in_hours else None)
+        self.step_ms = []
+        self.run_benchmark = cfg.inference.get("run_benchmark", None)
+        if self.run_benchmark:
+            # a third-party forecast is scored in place of the model (reference
+            # utils/inferencer.py:201-233): no model, no checkpoint
+            if self.bench_source is None:
+                self.bench_source = benchmarks.make_source(cfg.inference)
+            self.model = None
+            return
         self.model = get_model(cfg, domain_metadata=md).to(self.device)
         comm.all_model_groups_exist(self.model)
         self.preprocessor = get_preprocessor(cfg, self.test_dataset).to(self.device)
         if self.checkpoint_file and os.path.isfile(self.checkpoint_file):
             self.restore_checkpoint(self.checkpoint_file)
         self.model.eval()
-        self.step_ms = []
 
     def set_log_channels(self):
         inf = self.cfg.inference
@@ -147,27 +164,38 @@ class Inferencer:
                 past = self.context_window - 1
                 ts = ic - np.timedelta64(past * self.dt_hours, "h") + \
                     np.timedelta64(self.dt_hours, "h") * np.arange(self.context_window)
-                window = self.test_dataset.get_samples(ts, device=self.device).unsqueeze(0).to(self.device)
+                if self.run_benchmark:
+                    lat_sl, lon_sl = self.metadata["sp_slices"]
+                    fc, _ = benchmarks.assemble(self.bench_source, ic, self.lead_times, self.metadata["channels"],
+                                                lat_sl, lon_sl, self.n_lat)
+                    fc = fc.to(self.device)
+                else:
+                    window = self.test_dataset.get_samples(ts, device=self.device).unsqueeze(0).to(self.device)
                 for i, lead in enumerate(self.lead_times):
                     tgt = self.test_dataset.get_samples([ic + np.timedelta64(lead, "h")], device=self.device)
                     tgt = tgt.unsqueeze(0).to(self.device)
-                    inputs = self.preprocessor(window, device=self.device, mode="inference")
-                    if timed:
-                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                        e0.record()
-                    gen = self._forward(inputs)
-                    if timed:
-                        e1.record()
-                        self.step_ms.append((e0, e1))
-                    pred = gen * self.std + self.mean
+                    if self.run_benchmark:  # physical units already; normalised for the ACC
+                        pred = fc[i].unsqueeze(0).unsqueeze(0)
+                        gen = (pred - self.mean) / self.std
+                    else:
+                        inputs = self.preprocessor(window, device=self.device, mode="inference")
+                        if timed:
+                            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            e0.record()
+                        gen = self._forward(inputs)
+                        if timed:
+                            e1.record()
+                            self.step_ms.append((e0, e1))
+                        pred = gen * self.std + self.mean
                     targ = tgt * self.std + self.mean
                     self.rmse[self.ic_count, :, i] = self.weighted_rmse(pred, targ)[0]
                     self.acc[self.ic_count, :, i] = anomaly_correlation(gen, tgt, self.area_w)[0, 0]
                     if lead in self.spectra_times_in_hours:
                         self.spectra[lead][self.ic_count, 0] = power_spectrum_distributed(pred, self.sht)[0].float()
                         self.spectra[lead][self.ic_count, 1] = power_spectrum_distributed(targ, self.sht)[0].float()
-                    window = torch.roll(window, shifts=-1, dims=1)
-                    window[:, -1].copy_(gen[:, 0])
+                    if not self.run_benchmark:
+                        window = torch.roll(window, shifts=-1, dims=1)
+                        window[:, -1].copy_(gen[:, 0])
                 if self.device.type == "cuda":
                     # a kernel whose bounded wait ran out leaves its outputs incomplete: stop
                     # before this initial condition's scores are counted

@@ -181,7 +181,7 @@ def test_inference_bf16_matches_fp32_on_gpu(tmp_path):
     base = ["parallelism.backend=nccl", "model.embed_dim=64", "model.depth=2", "model.num_heads=4",
             "model.window_size=[4,8]", "model.patch_size=2", "data.synthetic.nlat=32", "data.synthetic.nlon=64",
             "data.synthetic.n_samples=40", "data.levels=[500]", "logging.log_to_wandb=false",
-            "inference.run_benchmark=true", f"inference.checkpoint={tmp_path}/no_ckpt.tar",
+            "inference.random_init=true", f"inference.checkpoint={tmp_path}/no_ckpt.tar",
             f"inference.checkpoint_hyperparams={tmp_path}/no_hp.yaml",
             "inference.start_date='2018-01-01T00'", "inference.end_date='2018-01-01T12'",
             "inference.time_horizon_in_hours=12", "inference.spectra_times_in_hours=[]",

@@ -229,3 +229,87 @@ def test_inference_rollout_scores_and_dp_split(tmp_path):
     run(_infer, 2, str(tmp_path / "inf3"), ckpt_dir, cut, "0")
     c = torch.load(cut)
     assert c["unstable"] == 4 and torch.equal(c["rmse"], torch.zeros_like(c["rmse"]))
+
+
+def _bench_infer(rank, world, exp_dir, out_path):
+    import numpy as np
+    import torch
+
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.inference.benchmarks import ForecastSource
+    from neural_scaling_weather_b200.inference.inferencer import Inferencer
+
+    class TruthOnWB2Grid(ForecastSource):
+        """The dataset's own future fields in physical units, laid out like a WeatherBench2 store
+        (south to north, with a south-pole row); 't2m' is missing from it."""
+
+        inf = None
+
+        def fetch(self, ic, leads_h, var, level):
+            name = var if level is None else f"{var}{level}"
+            chans = list(self.inf.metadata["channels"])
+            if name not in chans or name == "t2m":
+                return None
+            ci = chans.index(name)
+            ds = self.inf.test_dataset
+            out = []
+            for h in leads_h:
+                x = ds.get_samples([ic + np.timedelta64(int(h), "h")]).numpy()
+                phys = (x * ds.stds + ds.means)[0, ci]  # model grid, north to south
+                pole = np.full((1, phys.shape[1]), 1e6, dtype=np.float32)  # must be cut
+                out.append(np.concatenate([phys, pole], 0)[::-1])
+            return np.stack(out)
+
+    src = TruthOnWB2Grid()
+    cfg = C.compose("default", BASE + [
+        f"hydra.run.dir={exp_dir}", "inference.run_benchmark=hres", "inference.checkpoint_hyperparams=null",
+        "inference.start_date='2018-01-01T00'", "inference.end_date='2018-01-02T12'",
+        "inference.time_horizon_in_hours=12", "inference.spectra_times_in_hours=[6]",
+        "inference.unstable_rmse_threshold=1e9", "inference.log_sfc=['u10m','t2m']", "inference.log_var=['z']"])
+    inf = Inferencer(cfg, bench_source=src)
+    src.inf = inf
+    out = inf.launch()
+    if rank == 0:
+        torch.save({"rmse": out["rmse"], "acc": out["acc"], "channels": list(inf.metadata["channels"]),
+                    "model": inf.model}, out_path)
+
+
+def test_benchmark_forecast_scored_in_place_of_the_model(tmp_path):
+    """inference.run_benchmark scores a third-party forecast instead of the model: fields matched to the
+    channels by name, flipped from south-north to north-south with the pole row cut, scored against the
+    same targets.  A source that returns the truth scores RMSE 0 and ACC 1 on its channels; the channel it
+    lacks (t2m) stays zero, as in the reference."""
+    out = str(tmp_path / "bench.pt")
+    run(_bench_infer, 1, str(tmp_path / "inf"), out)
+    r = torch.load(out, weights_only=False)
+    assert r["model"] is None
+    chans = r["channels"]
+    t2m = chans.index("t2m")
+    others = [i for i in range(len(chans)) if i != t2m]
+    assert r["rmse"][others].abs().max() < 1e-3
+    assert (r["acc"][others] - 1).abs().max() < 1e-4
+    assert (r["rmse"][t2m] > 1.0).all()
+
+
+def test_benchmark_channel_names_and_grid_layout():
+    """Channel names split into variable and pressure level; the assembled shard is flipped to north-south,
+    cut to the model's rows and sliced to this rank's part of the grid."""
+    import numpy as np
+
+    from neural_scaling_weather_b200.inference.benchmarks import ForecastSource, assemble, split_channel
+
+    assert split_channel("z500") == ("z", 500) and split_channel("u10m") == ("u10m", None)
+    assert split_channel("t2m") == ("t2m", None) and split_channel(b"q850") == ("q", 850)
+
+    class Ramp(ForecastSource):
+        def fetch(self, ic, leads_h, var, level):
+            if var != "u":
+                return None
+            lat = np.arange(5, dtype=np.float32)[:, None] * np.ones((1, 6), np.float32)  # row index, S->N
+            return np.stack([lat + 100 * i for i in range(len(leads_h))])
+
+    fc, found = assemble(Ramp(), None, [6, 12], ["t2m", "u500"], slice(1, 3), slice(2, 5), n_lat=4)
+    assert found == [1] and fc.shape == (2, 2, 2, 3)
+    # model rows (north to south) are source rows 4, 3, 2, 1; this shard takes model rows 1..2 -> 3, 2
+    assert torch.equal(fc[0, 1, :, 0], torch.tensor([3.0, 2.0])) and torch.equal(fc[1, 1, :, 0], torch.tensor([103.0, 102.0]))
+    assert torch.count_nonzero(fc[:, 0]) == 0
