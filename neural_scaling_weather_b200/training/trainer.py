@@ -54,6 +54,7 @@ from ..utils.checkpoint_io import atomic_save, verified_load  # noqa: F401 (atom
 from ..utils.flops import FlopsCalculator
 from ..utils.profiler import init_profiler, profile_range
 from .grad_norm import ShardedNorm
+from .loss_scale import DeviceLossScaler
 from .optimizer import FlatParamSpace, FusedAdamW, set_optimizer, set_scheduler
 
 AMP_DTYPES = {"fp16": torch.float16, "bf16": torch.bfloat16}
@@ -231,8 +232,12 @@ class Trainer:
         self.use_cuda_graphs = bool(cfg.train.get("cuda_graphs", False))
         self._graph, self._graph_calls, self._static, self._static_loss = None, 0, None, None
         self._graph_pool, self._graph_stream = None, None
-        self.gscaler = torch.amp.GradScaler(
-            "cuda", enabled=self.amp_enabled and self.amp_dtype == torch.float16)
+        fp16 = self.amp_enabled and self.amp_dtype == torch.float16
+        if isinstance(self.optimizer, FusedAdamW):
+            # the unscale and inf check ride on the fused step (training/loss_scale.py)
+            self.gscaler = DeviceLossScaler(self.device, enabled=fp16)
+        else:
+            self.gscaler = torch.amp.GradScaler("cuda", enabled=fp16)
         self.loss_func = get_loss(cfg, self.metadata).to(self.device)
         self.weighted_rmse = get_metric("weighted_rmse", self.metadata).to(self.device)
 
@@ -348,17 +353,24 @@ class Trainer:
         if self.model.reducer is not None:
             self.model.reducer.finish()
         opt = self.optimizer
-        if self.gscaler.is_enabled():
+        device_scale = isinstance(self.gscaler, DeviceLossScaler) and self.gscaler.is_enabled()
+        if self.gscaler.is_enabled() and not device_scale:
             self.gscaler.unscale_(opt)
         clip = self.cfg.train.clip_grad_norm
         norm = self.norms.norm("grad")
+        if device_scale:  # norm of the scaled gradients: non-finite <=> some gradient is inf / nan
+            found_inf = (~torch.isfinite(norm)).to(torch.int32)
+            inv = self.gscaler.inv_scale()
+            norm = norm * inv
         coef = ShardedNorm.clip_coef(norm, float(clip)) if clip else torch.ones_like(norm)
         if isinstance(opt, FusedAdamW):
-            opt.grad_scale = coef
-            if self.gscaler.is_enabled():
-                self.gscaler.step(opt)
-                self.gscaler.update()
+            if device_scale:  # unscale and clip in the kernel's one multiply; skip the step on inf / nan
+                opt.grad_scale, opt.found_inf = coef * inv, found_inf
+                opt.step()
+                opt.found_inf = None
+                self.gscaler.update(found_inf)
             else:
+                opt.grad_scale = coef
                 opt.step()
         else:
             for p in self.model.parameters():

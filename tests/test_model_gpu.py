@@ -110,6 +110,57 @@ def test_trainer_stops_when_device_error_word_is_set(tmp_path):
     assert ext.read_error_flag(True) == 0
 
 
+def test_trainer_fp16_loss_scaling_on_the_fused_step(tmp_path):
+    """fp16 training: the gradient norm of the scaled gradients gives the inf check and, divided by the
+    scale, the clip; the fused AdamW kernel unscales and clips in one multiply.  A step whose gradients
+    hold an inf leaves every parameter unchanged and halves the scale; the next finite step updates."""
+    import os
+
+    import torch.distributed as dist
+
+    from neural_scaling_weather_b200.training.loss_scale import DeviceLossScaler
+    from neural_scaling_weather_b200.training.trainer import Trainer
+
+    os.environ.setdefault("MASTER_PORT", "29536")
+    cfg = C.compose("default", [
+        f"hydra.run.dir={tmp_path}", "parallelism.backend=nccl", "model.embed_dim=64", "model.depth=2",
+        "model.num_heads=4", "model.window_size=[4,8]", "model.patch_size=2", "data.synthetic.nlat=32",
+        "data.synthetic.nlon=64", "data.synthetic.n_samples=40", "data.levels=[500]", "data.batch_size=2",
+        "optimizer=adamw", "optimizer.max_iterations=4", "train.amp_dtype=fp16", "train.clip_grad_norm=1.0",
+        "logging.log_to_wandb=false", "train.seed=1"])
+    t = Trainer(cfg)
+    t.init_exp_dir(t.exp_dir)
+    t.build()
+    try:
+        assert isinstance(t.gscaler, DeviceLossScaler) and t.gscaler.is_enabled()
+        batches = iter(t.train_data_loader)
+        b = next(batches).cuda()
+        s0 = float(t.gscaler._scale.item())
+        # a finite step updates the parameters
+        before = t.space.data.clone()
+        t.train_step(b, is_optimizer_step=False)
+        t.train_step(b, is_optimizer_step=True)
+        torch.cuda.synchronize()
+        assert not torch.equal(t.space.data, before) and torch.isfinite(t.space.data).all()
+        assert float(t.gscaler._scale.item()) == s0
+        # an inf in one gradient: the step is skipped and the scale backs off
+        before = t.space.data.clone()
+        t.train_step(b, is_optimizer_step=False)
+        t.space.grad[3] = float("inf")
+        t.train_step(b, is_optimizer_step=True)
+        torch.cuda.synchronize()
+        assert torch.equal(t.space.data, before)
+        assert float(t.gscaler._scale.item()) == s0 * 0.5
+        # and training goes on
+        t.train_step(b, is_optimizer_step=False)
+        t.train_step(b, is_optimizer_step=True)
+        torch.cuda.synchronize()
+        assert not torch.equal(t.space.data, before) and torch.isfinite(t.space.data).all()
+        assert t.gscaler.state_dict()["scale"] == s0 * 0.5
+    finally:
+        dist.destroy_process_group()
+
+
 def test_trainer_cuda_graph_matches_eager(tmp_path):
     """Micro-batches replayed from a captured CUDA graph (derived weight copies refreshed in
     place after each optimizer step) follow the eager loss and parameter trajectory."""

@@ -313,3 +313,27 @@ def test_benchmark_channel_names_and_grid_layout():
     # model rows (north to south) are source rows 4, 3, 2, 1; this shard takes model rows 1..2 -> 3, 2
     assert torch.equal(fc[0, 1, :, 0], torch.tensor([3.0, 2.0])) and torch.equal(fc[1, 1, :, 0], torch.tensor([103.0, 102.0]))
     assert torch.count_nonzero(fc[:, 0]) == 0
+
+
+def test_device_loss_scaler_follows_torch_grad_scaler():
+    """The device-side loss scaler's back-off / growth rule and checkpoint keys match
+    torch.amp.GradScaler on the same sequence of finite and non-finite steps."""
+    from neural_scaling_weather_b200.training.loss_scale import DeviceLossScaler
+
+    kw = dict(init_scale=1024.0, growth_factor=2.0, backoff_factor=0.5, growth_interval=3)
+    ours = DeviceLossScaler("cpu", **kw)
+    ref = torch.amp.GradScaler("cpu", **kw)
+    p = torch.nn.Parameter(torch.ones(4))
+    opt = torch.optim.SGD([p], lr=0.0)
+    for bad in [0, 0, 1, 0, 0, 0, 0, 1, 1, 0, 0, 0, 0, 0, 0, 0]:
+        opt.zero_grad()
+        ref.scale((p * (float("inf") if bad else 1.0)).sum()).backward()
+        ref.step(opt)
+        ref.update()
+        ours.update(torch.tensor([bad], dtype=torch.int32))
+        assert ours.state_dict()["scale"] == ref.get_scale()
+        assert ours.state_dict()["_growth_tracker"] == ref.state_dict()["_growth_tracker"]
+    assert set(ours.state_dict()) == set(ref.state_dict())
+    fresh = DeviceLossScaler("cpu", **kw)
+    fresh.load_state_dict(ref.state_dict())
+    assert fresh.state_dict() == ours.state_dict()
