@@ -577,6 +577,8 @@ class Trainer:
         # model FLOP rate of the whole job over the interval (forward x 3 for the backward)
         interval_flops = fwd * 3 * int(self.cfg.train.num_rollout_steps) * n_mbs * comm.get_size("dp")
         self.logs["tflops_per_sec"] = interval_flops / max(self.logs["train_time"], 1e-9) / 1e12
+        peak = float(self.cfg.train.get("peak_tflops_per_gpu", 2250.0)) * self.world_size
+        self.logs["mfu"] = self.logs["tflops_per_sec"] / peak if peak > 0 else 0.0
         if self.log_to_wandb:
             import wandb
 

@@ -56,8 +56,11 @@ def test_checkpoint_format_and_keys(tmp_path):
     lines = open(tmp_path / "a" / "logs.txt").read().strip().split("\n")
     head = lines[0].split(",")
     for key in ["iter", "train_time", "val_time", "val_nsteps", "flops_consumed", "learning_rate", "wt_norm",
-                "val_loss", "best_val_loss", "best_iter", "train_loss", "grad", "val_rmse_u10m"]:
+                "val_loss", "best_val_loss", "best_iter", "train_loss", "grad", "val_rmse_u10m",
+                "samples_per_sec", "tflops_per_sec", "mfu"]:
         assert key in head, key
+    row = dict(zip(head, lines[-1].split(",")))
+    assert float(row["samples_per_sec"]) > 0 and 0 < float(row["mfu"]) < 1
     # the optimizer state loads into torch.optim.AdamW
     model_params = [torch.zeros_like(v) for k, v in ck["model_state"].items()]
     opt = torch.optim.AdamW([torch.nn.Parameter(p) for p in model_params], lr=1e-3)
