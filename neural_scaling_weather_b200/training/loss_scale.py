@@ -35,7 +35,8 @@ class DeviceLossScaler:
         return self._enabled
 
     def scale(self, loss: torch.Tensor) -> torch.Tensor:
-        return loss * self._scale.to(loss.dtype) if self._enabled else loss
+        # the fp32 scale promotes a 16-bit loss to fp32 (2**16 itself overflows fp16), as GradScaler does
+        return loss * self._scale if self._enabled else loss
 
     def inv_scale(self) -> torch.Tensor:
         """1 / scale as a device tensor [1]."""

@@ -382,7 +382,10 @@ class Trainer:
         if self.scheduler is not None:
             self.scheduler.step()
         with profile_range("grad norm"):
-            self.grad += norm * coef
+            if device_scale:  # a skipped (inf / nan) step adds nothing to the logged norm
+                self.grad += torch.where(found_inf != 0, torch.zeros_like(norm), norm * coef)
+            else:
+                self.grad += norm * coef
         opt.zero_grad(set_to_none=False)
 
     def _micro_batch(self, inputs, targets):
