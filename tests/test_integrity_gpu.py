@@ -132,7 +132,7 @@ def test_bounded_wait_reports_a_peer_that_never_signals():
     a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     b = torch.randn(N, K, device=DEV, dtype=torch.bfloat16)
     tiles = (M // 128) * (N // 256)
-    parts = [torch.zeros(M * N, device=DEV, dtype=torch.bfloat16) for _ in range(2)]
+    parts = [torch.zeros(2 * M * N, device=DEV, dtype=torch.bfloat16) for _ in range(2)]  # a slot per rank
     flags = [torch.zeros(FLAG_BASE + 2 * tiles, device=DEV, dtype=torch.int32) for _ in range(2)]
     ext.gemm_allreduce(a, b, None, None, [p.data_ptr() for p in parts], [f.data_ptr() for f in flags], 0)
     torch.cuda.synchronize()
@@ -141,4 +141,47 @@ def test_bounded_wait_reports_a_peer_that_never_signals():
     d = ext.gemm(a, b, impl=1)
     ref = a.float() @ b.float().t()
     assert ((d.float() - ref).norm() / ref.norm()).item() < 1e-2
+    assert ext.read_error_flag(True) == 0
+
+
+def test_bounded_wait_in_the_halo_roll():
+    """The sharded roll's gather waits for the peer's ready flag with a time budget.  On one GPU with a
+    stand-in peer (its band buffer and flag words are local tensors nothing else writes) the wait runs
+    out: the timeout lands in the device error word, the kernels return and the context stays usable."""
+    ext = _ext.require()
+    ext.read_error_flag(True)
+    H, W, C = 8, 16, 64  # the global grid: 8 x 16 patches split over sp2 = 2
+    x = torch.randn(1, 1, H, W // 2, C, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    geom, h_off, w_off, coord1, coord2 = [1, 2, 0, -3, 0], [0, H], [0, W // 2, W], [0, 0], [0, 1]
+    nb = ext.halo_band_bytes(x, geom, h_off, w_off, coord1, coord2)
+    bands = [torch.zeros(max(nb, 16), device=DEV, dtype=torch.uint8) for _ in range(2)]
+    flags = [torch.zeros(48, device=DEV, dtype=torch.int32) for _ in range(2)]
+    ext.halo_roll(x, out, geom, h_off, w_off, coord1, coord2, [b.data_ptr() for b in bands],
+                  [f.data_ptr() for f in flags])
+    torch.cuda.synchronize()
+    assert ext.read_error_flag(True) == 1  # wait timeout
+    # the locally sourced part of the roll is complete
+    assert torch.equal(out[:, :, :, : W // 2 - 3], x[:, :, :, 3:])
+    y = torch.randn(64, 64, device=DEV)
+    assert torch.allclose(y.sum(0), y.t().sum(1))  # the context still works
+    assert ext.read_error_flag(True) == 0
+
+
+def test_bounded_wait_in_the_data_parallel_reduction():
+    """The peer-memory data-parallel reduction announces a gradient bucket and waits for every rank's
+    announcement with a time budget.  With a stand-in peer that never announces, the kernel gives up,
+    records the timeout and returns; the context stays usable."""
+    ext = _ext.require()
+    ext.read_error_flag(True)
+    n, slots = 1024, 2
+    grads = [torch.randn(n, device=DEV) for _ in range(2)]
+    datas = [torch.zeros(n, device=DEV) for _ in range(2)]
+    flags = [torch.zeros(16 + 2 * slots, device=DEV, dtype=torch.int32) for _ in range(2)]
+    keep = grads[0].clone()
+    ext.dp_reduce([g.data_ptr() for g in grads], [d.data_ptr() for d in datas], [],
+                  [f.data_ptr() for f in flags], 0, slots, 0, 1, 0, n, 0.5)
+    torch.cuda.synchronize()
+    assert ext.read_error_flag(True) == 1
+    assert torch.equal(grads[0], keep)  # nothing was summed
     assert ext.read_error_flag(True) == 0
