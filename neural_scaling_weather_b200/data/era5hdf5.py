@@ -24,8 +24,6 @@ import numpy as np
 import torch
 
 from ..parallel import comm
-from ..parallel.helpers import compute_split_shapes_for_patching
-from ..utils.misc import build_spherical_area_weights, get_local_slice, get_spatial_coords
 from .synthetic import EPOCH0, SyntheticERA5
 
 

@@ -29,7 +29,7 @@ Sampling semantics follow ``utils/dataloaders/era5hdf5_dali.py`` of the referenc
 from __future__ import annotations
 
 import math
-from typing import Iterator, List, Optional
+from typing import Iterator, List
 
 import numpy as np
 import torch

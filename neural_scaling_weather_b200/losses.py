@@ -28,10 +28,7 @@ import torch.nn as nn
 
 from . import ops
 from .parallel import comm
-from .parallel.mappings import (
-    allgather_forward_split_backward,
-    allreduce_forward_identity_backward,
-)
+from .parallel.mappings import allreduce_forward_identity_backward
 from .utils.profiler import profile_range
 from .utils.sht import DistributedRealSHT
 

@@ -26,7 +26,7 @@ The B200 design departs from the reference's data flow, not its math:
 from __future__ import annotations
 
 import math
-from typing import Optional, Sequence, Tuple
+from typing import Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -35,10 +35,7 @@ import torch.nn.functional as F
 from .. import ops
 from ..parallel import comm
 from ..parallel.helpers import offsets
-from ..parallel.mappings import (
-    identity_forward_allreduce_backward,
-    roll_forward_reverseroll_backward,
-)
+from ..parallel.mappings import roll_forward_reverseroll_backward
 from ..utils.checkpoint_io import verified_load
 from ..utils.profiler import profile
 from .layers import (

@@ -11,7 +11,7 @@ for the fused optimizer to read.
 
 from __future__ import annotations
 
-from typing import Dict, List, Tuple
+from typing import Dict, Tuple
 
 import torch
 import torch.distributed as dist
