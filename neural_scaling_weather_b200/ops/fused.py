@@ -470,7 +470,7 @@ def _coord_cols(coords: torch.Tensor, p: int, dt: torch.dtype) -> torch.Tensor:
     hit = _COORD_COLS.get(key)
     if hit is not None and hit[0]() is coords:
         return hit[1]
-    cols = require().im2col(coords.contiguous(), p, DT[dt])
+    cols = wcache.normal_tensor(lambda: require().im2col(coords.contiguous(), p, DT[dt]))
     for k in [k for k, v in _COORD_COLS.items() if v[0]() is None]:  # fields of models that are gone
         del _COORD_COLS[k]
     _COORD_COLS[key] = (weakref.ref(coords), cols)

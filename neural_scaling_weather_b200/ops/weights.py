@@ -25,6 +25,15 @@ _cache: Dict[Tuple, Tuple[Tuple["weakref.ref", ...], Tuple[int, ...], torch.Tens
 _derived: Dict[Tuple, Tuple[Tuple["weakref.ref", ...], torch.Tensor, Callable[[], torch.Tensor]]] = {}
 
 
+def normal_tensor(fn: Callable[[], torch.Tensor]) -> torch.Tensor:
+    """Run ``fn`` without autograd and with inference mode off.  A cached tensor outlives the context
+    that built it: one first built during validation or a rollout (``torch.inference_mode``) would be
+    an inference tensor, and a training forward that used it later would get an output without a
+    gradient path (or an error where it is saved for backward)."""
+    with torch.inference_mode(False), torch.no_grad():
+        return fn()
+
+
 def register_shadow(param: torch.Tensor, shadow: torch.Tensor) -> None:
     _shadows[id(param)] = (weakref.ref(param), shadow)
 
@@ -79,7 +88,7 @@ def refresh_derived() -> None:
             if any(p is None for p in params):
                 dead.append(key)
                 continue
-            with torch.no_grad():
+            with torch.inference_mode(False), torch.no_grad():
                 t.copy_(rebuild())
             _cache[key] = (refs, _versions(params), t)
     for key in dead:
@@ -97,8 +106,7 @@ def get_derived(key: Tuple, params: Sequence[torch.Tensor], build: Callable[[], 
         return t
 
     def rebuild():
-        with torch.no_grad():
-            return build()
+        return normal_tensor(build)
 
     return _store(full, ps, rebuild(), rebuild)
 
@@ -116,7 +124,11 @@ def get(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     t = _lookup(key, [param])
     if t is not None:
         return t
-    return _store(key, [param], param.detach().to(dtype), lambda: param.detach().to(dtype))
+
+    def build():
+        return normal_tensor(lambda: param.detach().to(dtype))
+
+    return _store(key, [param], build(), build)
 
 
 def get_cat(params: Sequence[torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
@@ -132,8 +144,8 @@ def get_cat(params: Sequence[torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
         return t
 
     def build():
-        return torch.cat([s if (s is not None and s.dtype == dtype) else p.detach().to(dtype)
-                          for p, s in zip(ps, [_shadow_of(q) for q in ps])], dim=0)
+        return normal_tensor(lambda: torch.cat([s if (s is not None and s.dtype == dtype) else p.detach().to(dtype)
+                                                for p, s in zip(ps, [_shadow_of(q) for q in ps])], dim=0))
 
     return _store(key, ps, build(), build)
 
@@ -148,6 +160,6 @@ def get_t(params: Sequence[torch.Tensor], w: torch.Tensor) -> torch.Tensor:
     t = _lookup(key, ps)
     if t is not None:
         return t
-    t = w.t().contiguous()
+    t = normal_tensor(lambda: w.t().contiguous())
     dt, n, k = w.dtype, t.shape[1], t.shape[0]
     return _store(key, ps, t, lambda: get_cat(ps, dt).reshape(n, k).t())

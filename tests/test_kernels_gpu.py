@@ -280,6 +280,17 @@ def test_coord_pos_embed_cached_per_weight_version():
         a3 = ops.coord_pos_embed(coords, w, b, p)
         r3 = ops.patch_embed(coords, wr, br, p)
     assert rel(a3, r3) < 1e-2 and rel(a3, a) > 1e-3
+    # weights change, then a validation-style forward rebuilds the cache under inference mode: the next
+    # training forward still sends gradients to the embedding weights
+    with torch.no_grad():
+        w.add_(0.01)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        ops.coord_pos_embed(coords, w, b, p)
+    w.grad, b.grad = None, None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        a4 = ops.coord_pos_embed(coords, w, b, p)
+    a4.float().sum().backward()
+    assert w.grad is not None and b.grad is not None and torch.isfinite(w.grad).all()
 
 
 # --------------------------------------------------------------------------- losses

@@ -340,3 +340,33 @@ def test_device_loss_scaler_follows_torch_grad_scaler():
     fresh = DeviceLossScaler("cpu", **kw)
     fresh.load_state_dict(ref.state_dict())
     assert fresh.state_dict() == ours.state_dict()
+
+
+def test_weight_cache_entries_built_in_inference_mode_stay_usable_in_training():
+    """Casts, concatenations, transposes and derived tensors of the weight cache that are first built
+    during validation or a rollout (torch.inference_mode) are ordinary tensors: the training forward that
+    finds them in the cache afterwards can still build its autograd graph through them."""
+    from neural_scaling_weather_b200.ops import weights as wcache
+
+    wcache.clear()
+    w1, w2 = torch.nn.Parameter(torch.randn(4, 3)), torch.nn.Parameter(torch.randn(2, 3))
+    with torch.inference_mode():
+        a = wcache.get(w1, torch.bfloat16)
+        c = wcache.get_cat([w1, w2], torch.bfloat16)
+        t = wcache.get_t([w1, w2], c)
+        d = wcache.get_derived(("double",), [w1], lambda: w1.detach() * 2)
+    assert not any(x.is_inference() for x in (a, c, t, d))
+    assert wcache.get(w1, torch.bfloat16) is a and wcache.get_derived(("double",), [w1], lambda: None) is d
+
+    class Through(torch.autograd.Function):  # returns a cached tensor, as the positional embedding does
+        @staticmethod
+        def forward(ctx, w):
+            return d.view_as(d)
+
+        @staticmethod
+        def backward(ctx, g):
+            return 2 * g
+
+    Through.apply(w1).sum().backward()
+    assert torch.equal(w1.grad, torch.full_like(w1, 2.0))
+    wcache.clear()
