@@ -178,10 +178,14 @@ class DistributedRealSHT(torch.nn.Module):
         self._cpu_w = None  # float64 (m, l, k) table of the CPU path, built on first use
         self._cuda = {}     # device -> (P packed float32, row offsets)
 
+    # The tables are built on first use, which may come inside torch.inference_mode (validation, a
+    # rollout); they are built with inference mode off so that a later training step can save them
+    # for its backward.
     def _cpu_table(self):
         if self._cpu_w is None:
             P = legendre_orthonormal(self.m_hi, self.lmax, self._x)[self.m_lo:self.m_hi]
-            self._cpu_w = torch.from_numpy(P * self._w[None, None, :])
+            with torch.inference_mode(False):
+                self._cpu_w = torch.from_numpy(P * self._w[None, None, :])
         return self._cpu_w
 
     def _cuda_table(self, device):
@@ -192,7 +196,9 @@ class DistributedRealSHT(torch.nn.Module):
             x = torch.from_numpy(self._x).to(device)
             w = torch.from_numpy(self._w).to(device)
             m_count = max(0, min(self.m_hi, self.lmax) - self.m_lo)
-            self._cuda[key] = tuple(require().legendre_table(x, w, self.m_lo, m_count, self.lmax, True))
+            with torch.inference_mode(False):
+                self._cuda[key] = tuple(require().legendre_table(x.clone(), w.clone(), self.m_lo, m_count,
+                                                                 self.lmax, True))
         return self._cuda[key]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:

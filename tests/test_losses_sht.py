@@ -181,3 +181,17 @@ def test_power_spectrum_sharded_matches_single_rank():
     from tests.dist_utils import run
 
     run(_spectrum_worker, 4, 2, 2)
+
+
+def test_sht_table_first_built_in_inference_mode_serves_training():
+    """The Legendre table is built on first use; when that use is a validation pass under
+    torch.inference_mode, a later training step must still be able to save it for its backward."""
+    from neural_scaling_weather_b200.utils.sht import DistributedRealSHT
+
+    sht = DistributedRealSHT(8, 16)
+    x = torch.randn(2, 8, 16, dtype=torch.float64)
+    with torch.inference_mode():
+        sht(x)
+    xg = x.clone().requires_grad_()
+    sht(xg).square().sum().backward()
+    assert xg.grad is not None and torch.isfinite(xg.grad).all()
