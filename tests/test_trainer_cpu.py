@@ -370,3 +370,38 @@ def test_weight_cache_entries_built_in_inference_mode_stay_usable_in_training():
     Through.apply(w1).sum().backward()
     assert torch.equal(w1.grad, torch.full_like(w1, 2.0))
     wcache.clear()
+
+
+def _random_init_infer(rank, world, exp_dir, out_path):
+    import torch
+
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.inference.inferencer import Inferencer
+
+    cfg = C.compose("default", BASE + [
+        f"hydra.run.dir={exp_dir}", f"inference.checkpoint={exp_dir}/none.tar", "inference.checkpoint_hyperparams=null",
+        "inference.random_init=true", "inference.start_date='2018-01-01T00'", "inference.end_date='2018-01-01T12'",
+        "inference.time_horizon_in_hours=6", "inference.spectra_times_in_hours=[]",
+        "inference.unstable_rmse_threshold=1e30"])
+    out = Inferencer(cfg).launch()
+    if rank == 0:
+        torch.save({"rmse": out["rmse"]}, out_path)
+
+
+def test_inference_without_checkpoint_needs_random_init(tmp_path):
+    """inference.random_init=true rolls out random-init weights when the checkpoint does not exist (the
+    benchmark's rollout); without it a missing checkpoint is an error."""
+    out = str(tmp_path / "r.pt")
+    run(_random_init_infer, 1, str(tmp_path / "inf"), out)
+    r = torch.load(out)
+    assert torch.isfinite(r["rmse"]).all() and (r["rmse"] > 0).all()
+
+    from neural_scaling_weather_b200 import config as C
+    from neural_scaling_weather_b200.inference.inferencer import Inferencer
+
+    cfg = C.compose("default", BASE + [f"hydra.run.dir={tmp_path / 'inf2'}", f"inference.checkpoint={tmp_path}/none.tar",
+                                       "inference.checkpoint_hyperparams=null"])
+    inf = Inferencer.__new__(Inferencer)  # the checkpoint check only (no process group needed)
+    inf.cfg, inf.world_rank, inf.log_to_screen = cfg, 0, False
+    with pytest.raises(FileNotFoundError):
+        inf.init_exp_dir(str(tmp_path / "inf2"))
