@@ -121,3 +121,38 @@ def test_split_shapes():
     assert compute_split_shapes_for_patching(721, 4, 4) == [180, 180, 180, 181]
     assert compute_split_shapes_for_patching(1440, 2, 4) == [720, 720]
     assert compute_split_shapes_for_patching(720, 3, 4) == [240, 240, 240]
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "config")), reason="reference copy absent")
+def test_config_tree_keeps_every_reference_key_and_default():
+    """Every file of the reference's YAML tree exists here with every key and the same default value
+    (the defaults list included), except the data loader: DALI is not available, so `synthetic` (same
+    stateful sampling semantics) is the default.  Keys added here (e.g. train.cuda_graphs) are allowed."""
+    import yaml
+
+    def flat(d, pre=""):
+        out = {}
+        for k, v in (d or {}).items():
+            out.update(flat(v, f"{pre}{k}.") if isinstance(v, dict) else {f"{pre}{k}": v})
+        return out
+
+    mine = os.path.join(os.path.dirname(C.__file__), "yaml")
+    allowed = {("data/latlon_025deg.yaml", "loader"): ("dali", "synthetic")}
+    n = 0
+    for root, _, files in os.walk(os.path.join(REF, "config")):
+        for f in files:
+            if not f.endswith(".yaml"):
+                continue
+            rel = os.path.relpath(os.path.join(root, f), os.path.join(REF, "config"))
+            ours = os.path.join(mine, rel)
+            assert os.path.exists(ours), rel
+            a = flat(yaml.safe_load(open(os.path.join(root, f))))
+            b = flat(yaml.safe_load(open(ours)))
+            for k, v in a.items():
+                assert k in b, (rel, k)
+                if (rel, k) in allowed:
+                    assert (v, b[k]) == allowed[(rel, k)], (rel, k, v, b[k])
+                else:
+                    assert b[k] == v, (rel, k, v, b[k])
+                n += 1
+    assert n > 50
